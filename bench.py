@@ -1,0 +1,399 @@
+#!/usr/bin/env python
+"""Benchmark: routed MoE-FFN forward tokens/s (XL 64x8 layer, bf16) on B200.
+
+A step is one forward of the MoE FFN layer over one batch of T tokens
+(default: the XL 64x8 layer at T = 16384 per GPU, d = 1536, 64 experts of
+width 512, top-8).  `value` is the whole-job tokens/s with inputs resident in
+HBM; `e2e` is the same through the public module API with the hidden states
+copied in from pinned host memory and the output read back every step.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+Timing: W untimed warm-up steps, then K steps, each bracketed by CUDA events
+on the launching stream; a 256 MiB buffer (2x the L2) is rewritten before
+every step, outside the events.  Per-stage times come from events the C ABI
+records between its kernels (hmoe_ffn_forward_marked) in the same steps.
+Multi-GPU runs take the max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import datetime
+import importlib
+import json
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "MoE-FFN fwd tokens/s (XL 64x8 bf16)"
+L2_FLUSH_BYTES = 256 << 20
+# DRAM bytes per launch of the dominant kernel from `ncu` (see profiles/);
+# None until a capture of the current kernel exists.
+NCU_TRAFFIC_BYTES = {}
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--config", default="cfg2_xl64_bf16")
+    ap.add_argument("--tokens", type=int, default=0, help="tokens per GPU (default: the config's)")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0,
+                    help="target duration of the CPU baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)),
+            int(os.environ.get("LOCAL_RANK", 0)))
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained"), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "source": "fallback"}
+
+
+# ------------------------------------------------------------------ clocks --
+class ClockSampler:
+    """nvidia-smi samples of one GPU while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.gpu_id = gpu_id
+        self.proc = None
+        self.path = pathlib.Path(os.environ.get("TMPDIR", "/tmp")) / f"hmoe_clocks_{os.getpid()}.csv"
+
+    def __enter__(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", self.gpu_id], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.f.close()
+        return False
+
+    def summary(self):
+        if self.proc is None or not self.path.exists():
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, smax, power, reasons = [], [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.path.read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+                power.append(float(parts[3]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        self.path.unlink(missing_ok=True)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        loaded = [s for s in sm if s > 0.5 * max(sm)] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(smax),
+                "power_w_max": max(power), "samples": len(sm), "reasons": sorted(reasons)}
+
+
+def gpu_uuid(torch, dev: int) -> str:
+    try:
+        return "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:
+        return str(dev)
+
+
+# ------------------------------------------------------------- CPU timing --
+def cpu_oracle_tokens_per_s(shape, target_s: float, seed: int = 0, max_tokens: int = 16384):
+    """Time the CPU port of the reference path (oracle) on a bounded sample."""
+    from oracle import moe_oracle as O
+    syn = importlib.import_module("hrm-moe_b200.synthetic")
+    w_r, w_gu, w_d = syn.make_weights(shape, seed)
+
+    def run(T):
+        sub = syn.MoEShape(T, shape.hidden, shape.experts, shape.intermediate, shape.top_k,
+                           shape.norm_topk_prob, shape.dtype)
+        x = syn.make_hidden(sub, seed)
+        t0 = time.perf_counter()
+        O.moe_forward(x, w_r, w_gu, w_d, shape.top_k, shape.norm_topk_prob, shape.dtype)
+        return time.perf_counter() - t0
+
+    run(64)  # warm-up (threads, BLAS)
+    T, dt = 128, run(128)
+    while dt < target_s / 2 and T < max_tokens:
+        T = min(max_tokens, int(T * min(8.0, max(2.0, target_s / max(dt, 1e-3)))))
+        dt = run(T)
+    return T / dt, T, dt
+
+
+# --------------------------------------------------------- reference arm --
+def reference_arm(args, rank, world):
+    """The reference's CPU path (the oracle port of it) on the host cores."""
+    if rank != 0:
+        return 0
+    syn = importlib.import_module("hrm-moe_b200.synthetic")
+    shape = syn.CONFIGS[args.config]
+    from oracle import moe_oracle as O
+    w_r, w_gu, w_d = syn.make_weights(shape, 0)
+    sample_T = 256
+    sub = syn.MoEShape(sample_T, shape.hidden, shape.experts, shape.intermediate, shape.top_k,
+                       shape.norm_topk_prob, shape.dtype)
+    x = syn.make_hidden(sub, 0)
+    times = []
+    for i in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        O.moe_forward(x, w_r, w_gu, w_d, shape.top_k, shape.norm_topk_prob, shape.dtype)
+        if i >= args.warmup:
+            times.append(time.perf_counter() - t0)
+    ms = 1e3 * statistics.mean(times)
+    value = sample_T / (ms * 1e-3)
+    cores = os.cpu_count()
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": shape.dtype,
+        "data": "synthetic: x~N(0,1), weights~N(0,0.02), numpy PCG64 seed 0",
+        "impl": "reference",
+        "config": {"workload": f"{args.config}: XL 64x8 MoE-FFN layer forward, "
+                               f"sample of {sample_T} tokens per step on the host CPU",
+                   "tokens_per_step": sample_T, "hidden": shape.hidden,
+                   "experts": shape.experts, "intermediate": shape.intermediate,
+                   "top_k": shape.top_k},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": f"{sample_T} tokens of the {args.config} layer per step "
+                                   f"(numpy/OpenBLAS + C, all {cores} host threads)"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------- B200 arm --
+def b200_arm(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=dev)
+    pkg = importlib.import_module("hrm-moe_b200")
+    _lib = importlib.import_module("hrm-moe_b200._lib")
+    ops = importlib.import_module("hrm-moe_b200.ops")
+    layers = importlib.import_module("hrm-moe_b200.layers")
+    syn = pkg.synthetic
+    base = syn.CONFIGS[args.config]
+    T = args.tokens or base.tokens
+    shape = syn.MoEShape(T, base.hidden, base.experts, base.intermediate, base.top_k,
+                         base.norm_topk_prob, base.dtype)
+    d, E, I, k = shape.hidden, shape.experts, shape.intermediate, shape.top_k
+    dt = torch.bfloat16 if shape.dtype == "bf16" else torch.float32
+    es = 2 if shape.dtype == "bf16" else 4
+
+    g = torch.Generator(device=dev).manual_seed(1234)
+    wg = torch.Generator(device=dev).manual_seed(1000 + rank)
+    w_router = (torch.randn((E, d), generator=g, device=dev) * 0.02).to(dt)
+    w_gate_up = (torch.randn((E, 2 * I, d), generator=g, device=dev) * 0.02).to(dt)
+    w_down = (torch.randn((E, d, I), generator=g, device=dev) * 0.02).to(dt)
+    x = torch.randn((T, d), generator=wg, device=dev).to(dt)
+    y = torch.empty_like(x)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+
+    lib = _lib.load()
+    cshape = ops.make_shape(T, d, E, I, k, dt, shape.norm_topk_prob)
+    ws_bytes = lib.hmoe_ffn_workspace_bytes(ctypes.byref(cshape))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    n_marks = 6
+
+    def make_events(n):
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(n)]
+        for e in evs:
+            e.record(stream)  # create the underlying cudaEvent_t
+        return evs
+
+    def step(marks):
+        arr = (ctypes.c_void_p * n_marks)(*[ctypes.c_void_p(m.cuda_event) for m in marks])
+        _lib.check(lib.hmoe_ffn_forward_marked(
+            ctypes.byref(cshape), ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(w_router.data_ptr()),
+            None, ctypes.c_void_p(w_gate_up.data_ptr()), ctypes.c_void_p(w_down.data_ptr()),
+            ctypes.c_void_p(y.data_ptr()), 0, ctypes.c_void_p(ws.data_ptr()), ws.numel(),
+            ctypes.c_void_p(stream.cuda_stream), arr))
+
+    warm_marks = make_events(n_marks)
+    for _ in range(args.warmup):
+        flush.zero_()
+        step(warm_marks)
+    torch.cuda.synchronize()
+    ops.workspace_status(ws)
+
+    marks = [make_events(n_marks) for _ in range(args.steps)]
+    starts = make_events(args.steps)
+    ends = make_events(args.steps)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(gpu_uuid(torch, local_rank)) as clocks:
+        for i in range(args.steps):
+            flush.zero_()
+            starts[i].record(stream)
+            step(marks[i])
+            ends[i].record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ops.workspace_status(ws)
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    phase_names = ["router", "dispatch", "gate_up_gemm", "down_gemm", "combine"]
+    phase_ms = {n: statistics.mean(m[i].elapsed_time(m[i + 1]) for m in marks)
+                for i, n in enumerate(phase_names)}
+    ms = statistics.mean(step_ms)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+
+    # ------------------------------------------------- end to end (public API)
+    e2e = None
+    if not args.no_e2e:
+        mod = layers.SparseMoESwiGLU(d, I, E, k, shape.norm_topk_prob).to(dev, dt)
+        with torch.no_grad():
+            mod.gate.weight.copy_(w_router)
+            mod.experts.gate_up_weight.copy_(w_gate_up)
+            mod.experts.down_weight.copy_(w_down)
+        x_host = x.cpu().pin_memory()
+        y_host = torch.empty_like(x_host).pin_memory()
+        e_s, e_e = make_events(args.steps), make_events(args.steps)
+        with torch.no_grad():
+            for i in range(args.warmup + args.steps):
+                flush.zero_()
+                if i >= args.warmup:
+                    e_s[i - args.warmup].record(stream)
+                xd = x_host.to(dev, non_blocking=True)
+                yd = mod(xd)
+                y_host.copy_(yd, non_blocking=True)
+                if i >= args.warmup:
+                    e_e[i - args.warmup].record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = statistics.mean(s.elapsed_time(e) for s, e in zip(e_s, e_e))
+        if world > 1:
+            t = torch.tensor([e2e_ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e_ms = float(t.item())
+        e2e = {"value": world * T / (e2e_ms * 1e-3), "unit": "tokens/s",
+               "ms_per_step": e2e_ms, "h2d_bytes_per_step": T * d * es,
+               "d2h_bytes_per_step": T * d * es, "api": "layers.SparseMoESwiGLU.forward"}
+
+    # ------------------------------------------------------------ roofline
+    peaks = measured_peaks()
+    A = T * k
+    gu_flops, dn_flops = shape.gemm_flops()
+    algo = {
+        "router": ("hbm", T * d * es + E * d * es + T * k * (4 + es)),
+        "dispatch": ("hbm", T * d * es + A * d * es + A * 8),
+        "gate_up_gemm": ("tensor", gu_flops),
+        "down_gemm": ("tensor", dn_flops),
+        "combine": ("hbm", A * d * es + A * (4 + es) + T * d * es),
+    }
+    phases = {}
+    for n in phase_names:
+        bound, work = algo[n]
+        sec = phase_ms[n] * 1e-3
+        if bound == "tensor":
+            ach = work / sec / 1e12
+            phases[n] = {"ms": phase_ms[n], "bound": "tensor", "achieved": ach,
+                         "unit": "TFLOP/s", "frac": ach / peaks["bf16_tflops"]}
+        else:
+            ach = work / sec / 1e9
+            phases[n] = {"ms": phase_ms[n], "bound": "hbm", "achieved": ach, "unit": "GB/s",
+                         "frac": ach / peaks["hbm_gbs"]}
+    dom = max(phase_names, key=lambda n: phase_ms[n])
+    dp = phases[dom]
+    roofline = {"kernel": dom, "bound": dp["bound"], "achieved": dp["achieved"],
+                "peak": peaks["bf16_tflops"] if dp["bound"] == "tensor" else peaks["hbm_gbs"],
+                "unit": dp["unit"], "frac": dp["frac"],
+                "peak_source": f"{peaks['source']} (burst)" if dp["bound"] == "tensor" else peaks["source"],
+                "traffic": NCU_TRAFFIC_BYTES.get(dom),
+                "algorithmic": algo[dom][1]}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        tps, Ts, secs = cpu_oracle_tokens_per_s(shape, args.cpu_seconds)
+        cpu = {"value": tps, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+               "sample": f"{Ts} tokens of the {args.config} layer in {secs:.1f} s "
+                         f"(numpy/OpenBLAS + C router, {os.cpu_count()} host threads)"}
+
+    clk = clocks.summary()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    line = {
+        "metric": METRIC, "value": world * T / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": shape.dtype,
+        "data": "synthetic: x~N(0,1), weights~N(0,0.02) (seeded torch.Generator on device)",
+        "config": {"workload": f"{args.config}: XL 64x8 MoE-FFN layer forward "
+                               f"(T={T} tokens per GPU, d={d}, E={E}, I={I}, top-{k})",
+                   "tokens_per_gpu": T, "global_tokens": world * T,
+                   "parallelism": "single GPU" if world == 1 else f"replicas x{world}",
+                   "l2": "256 MiB buffer rewritten before every step (outside the timed events)"},
+        "roofline": roofline,
+        "phases": phases,
+        "cpu_baseline": cpu,
+        "e2e": e2e,
+        "gpu_launches": 7 * args.steps,
+        "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    args = parse_args()
+    rank, world, local_rank = dist_env()
+    if args.impl == "reference":
+        return reference_arm(args, rank, world)
+    return b200_arm(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

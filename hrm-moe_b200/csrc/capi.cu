@@ -1,0 +1,516 @@
+// extern "C" entry points declared in include/hrm_moe.h.
+//
+// Each call validates its arguments, selects the device that owns the first
+// data pointer, carves its scratch buffers out of the caller's workspace and
+// enqueues the kernels on the caller's stream.  Nothing here synchronises
+// the host except hmoe_workspace_status().
+#include <stdarg.h>
+#include <stdio.h>
+#include <stdlib.h>
+
+#include <mutex>
+#include <string>
+
+#include "common.cuh"
+#include "hrm_moe.h"
+#include "internal.h"
+
+using namespace hmoe;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* where) {
+  return fail(HMOE_EIO, "%s: %s", where, cudaGetErrorString(e));
+}
+
+#define HMOE_CUDA(call, where)                  \
+  do {                                          \
+    cudaError_t e_ = (call);                    \
+    if (e_ != cudaSuccess) return cuda_fail(e_, where); \
+  } while (0)
+
+constexpr size_t kAlign = 1024;
+size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
+
+size_t elem_size(int dtype) { return dtype == kDtypeBF16 ? 2 : 4; }
+
+int validate_shape(const hmoe_shape* s) {
+  if (!s) return fail(HMOE_EINVAL, "shape is NULL");
+  if (s->tokens < 0) return fail(HMOE_EINVAL, "tokens must be >= 0, got %lld", (long long)s->tokens);
+  if (s->dtype != HMOE_DTYPE_BF16 && s->dtype != HMOE_DTYPE_F32)
+    return fail(HMOE_EINVAL, "unsupported dtype %d (bf16 = 0, f32 = 1)", s->dtype);
+  if (s->hidden <= 0 || s->hidden % 8 != 0)
+    return fail(HMOE_EINVAL, "hidden must be a positive multiple of 8, got %d", s->hidden);
+  if (s->intermediate <= 0 || s->intermediate % 8 != 0)
+    return fail(HMOE_EINVAL, "intermediate must be a positive multiple of 8, got %d", s->intermediate);
+  if (s->experts <= 0 || s->experts > 128)
+    return fail(HMOE_EINVAL, "experts must be in [1, 128], got %d", s->experts);
+  if (s->top_k <= 0 || s->top_k > s->experts || s->top_k > 32)
+    return fail(HMOE_EINVAL, "top_k must be in [1, min(experts, 32)], got %d", s->top_k);
+  if (s->tokens * (int64_t)s->top_k > 0x7fffffffll)
+    return fail(HMOE_EINVAL, "tokens * top_k must fit in int32");
+  return HMOE_OK;
+}
+
+int aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Make the device that owns `ptr` current; refuse non-sm_100 devices.
+int select_device(const void* ptr) {
+  cudaPointerAttributes attr;
+  cudaError_t e = cudaPointerGetAttributes(&attr, ptr);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return cuda_fail(e, "cudaPointerGetAttributes");
+  }
+  if (attr.type != cudaMemoryTypeDevice && attr.type != cudaMemoryTypeManaged)
+    return fail(HMOE_EINVAL, "expected a device pointer (got host memory)");
+  int cur = -1;
+  HMOE_CUDA(cudaGetDevice(&cur), "cudaGetDevice");
+  if (cur != attr.device) HMOE_CUDA(cudaSetDevice(attr.device), "cudaSetDevice");
+  static int major[64];
+  static std::once_flag once[64];
+  const int dev = attr.device;
+  if (dev < 0 || dev >= 64) return fail(HMOE_EINVAL, "device ordinal %d out of range", dev);
+  std::call_once(once[dev], [dev] {
+    int m = 0;
+    cudaDeviceGetAttribute(&m, cudaDevAttrComputeCapabilityMajor, dev);
+    major[dev] = m;
+  });
+  if (major[dev] != 10)
+    return fail(HMOE_ENOSYS, "device %d is sm_%d0, this library is built for sm_100a", dev,
+                major[dev]);
+  return HMOE_OK;
+}
+
+// ------------------------------------------------------- workspace plans ----
+struct Carve {
+  char* base;
+  size_t off = 0;
+  template <class T>
+  T* take(size_t bytes) {
+    T* p = base ? reinterpret_cast<T*>(base + off) : nullptr;
+    off = align_up(off + bytes);
+    return p;
+  }
+};
+
+struct DispatchBufs {
+  int* err;
+  int32_t* local_rank;
+  int32_t* block_counts;
+  int32_t* counts;
+  int32_t* offsets;
+};
+
+DispatchBufs carve_dispatch(Carve& c, const hmoe_shape& s) {
+  DispatchBufs b;
+  const int64_t A = s.tokens * s.top_k;
+  const int64_t nblk = dispatch_num_blocks(s.tokens, s.top_k);
+  b.err = c.take<int>(sizeof(int));
+  b.local_rank = c.take<int32_t>(sizeof(int32_t) * A);
+  b.block_counts = c.take<int32_t>(sizeof(int32_t) * nblk * s.experts);
+  b.counts = c.take<int32_t>(sizeof(int32_t) * s.experts);
+  b.offsets = c.take<int32_t>(sizeof(int32_t) * (s.experts + 1));
+  return b;
+}
+
+struct ExpertBufs {
+  DispatchBufs d;
+  int32_t* pos;
+  void* xs;   // [A, d]: gathered rows, then (aliased) the down-projection output
+  void* h;    // [A, I]
+};
+
+ExpertBufs carve_experts(Carve& c, const hmoe_shape& s) {
+  ExpertBufs b;
+  const int64_t A = s.tokens * s.top_k;
+  const size_t es = elem_size(s.dtype);
+  b.d = carve_dispatch(c, s);
+  b.pos = c.take<int32_t>(sizeof(int32_t) * A);
+  b.xs = c.take<void>(es * A * s.hidden);
+  b.h = c.take<void>(es * A * s.intermediate);
+  return b;
+}
+
+struct FfnBufs {
+  ExpertBufs x;
+  int32_t* topk_idx;
+  float* topk_w;
+};
+
+FfnBufs carve_ffn(Carve& c, const hmoe_shape& s) {
+  FfnBufs b;
+  const int64_t A = s.tokens * s.top_k;
+  b.x = carve_experts(c, s);
+  b.topk_idx = c.take<int32_t>(sizeof(int32_t) * A);
+  b.topk_w = c.take<float>(sizeof(float) * A);
+  return b;
+}
+
+template <class F>
+size_t plan_bytes(const hmoe_shape* s, F carve) {
+  if (validate_shape(s) != HMOE_OK) return 0;
+  Carve c{nullptr};
+  carve(c, *s);
+  return c.off;
+}
+
+int check_ws(void* ws, size_t have, size_t need) {
+  if (need > have) return fail(HMOE_ENOSPC, "workspace too small: need %zu bytes, got %zu", need, have);
+  if (need > 0 && !ws) return fail(HMOE_EINVAL, "workspace is NULL");
+  if (reinterpret_cast<uintptr_t>(ws) % 256 != 0) return fail(HMOE_EINVAL, "workspace must be 256-byte aligned");
+  return HMOE_OK;
+}
+
+int sm_margin() {
+  static int margin = [] {
+    const char* v = getenv("HRM_MOE_B200_SM_MARGIN");
+    return v ? atoi(v) : 0;
+  }();
+  return margin;
+}
+
+// Dispatch stages shared by the layer, the experts module and hmoe_dispatch.
+int run_dispatch(const hmoe_shape& s, const int32_t* idx, const void* w, int w_is_f32,
+                 const void* x, const DispatchBufs& b, int32_t* pos, int32_t* sort_idx,
+                 int32_t* sorted_token, void* sorted_w, void* x_sorted, cudaStream_t st) {
+  const int64_t nblk = dispatch_num_blocks(s.tokens, s.top_k);
+  HMOE_CUDA(launch_hist_rank(idx, s.tokens, s.top_k, s.experts, b.local_rank, b.block_counts,
+                             b.err, st), "hist_rank");
+  HMOE_CUDA(launch_scan(b.block_counts, nblk, s.experts, b.counts, b.offsets, st), "scan");
+  HMOE_CUDA(launch_permute_gather(idx, b.local_rank, b.block_counts, w, w_is_f32, x, s.tokens,
+                                  s.hidden, s.top_k, s.experts, s.dtype, pos, sort_idx,
+                                  sorted_token, sorted_w, x_sorted, st), "permute_gather");
+  return HMOE_OK;
+}
+
+int run_grouped(const void* a, const void* b, const int32_t* counts, int64_t M, int N, int K,
+                int G, int dtype, int swiglu, void* out, int* err, cudaStream_t st) {
+  GroupedGemmArgs g;
+  g.a = a;
+  g.b = b;
+  g.counts = counts;
+  g.out = out;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.G = G;
+  g.swiglu = swiglu;
+  g.dtype = dtype;
+  g.err = err;
+  g.sm_limit = 0;
+  const cudaError_t e = dtype == kDtypeBF16 ? launch_grouped_gemm_sm100(g, st)
+                                            : launch_grouped_gemm_simt(g, st);
+  if (e != cudaSuccess) return cuda_fail(e, swiglu ? "grouped_swiglu" : "grouped_linear");
+  return HMOE_OK;
+}
+
+// Experts on routed tokens: dispatch, two grouped GEMMs, combine.
+// Optional timing marks between stages (events[i] recorded after stage i).
+struct PhaseMarks {
+  void* const* ev = nullptr;
+  int mark(int i, cudaStream_t st) const {
+    if (ev && ev[i]) {
+      cudaError_t e = cudaEventRecord(static_cast<cudaEvent_t>(ev[i]), st);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
+    }
+    return HMOE_OK;
+  }
+};
+
+int run_experts(const hmoe_shape& s, const void* x, const int32_t* idx, const void* w,
+                int w_is_f32, const void* w_gate_up, const void* w_down, const void* final_in,
+                void* out, int32_t* counts_out, int32_t* sort_idx, const ExpertBufs& b,
+                cudaStream_t st, const PhaseMarks& pm = PhaseMarks()) {
+  const int64_t A = s.tokens * s.top_k;
+  int rc = run_dispatch(s, idx, w, w_is_f32, x, b.d, b.pos, sort_idx, nullptr, nullptr, b.xs, st);
+  if (rc) return rc;
+  if (counts_out)
+    HMOE_CUDA(cudaMemcpyAsync(counts_out, b.d.counts, sizeof(int32_t) * s.experts,
+                              cudaMemcpyDeviceToDevice, st), "copy counts");
+  if ((rc = pm.mark(2, st))) return rc;
+  rc = run_grouped(b.xs, w_gate_up, b.d.counts, A, s.intermediate, s.hidden, s.experts, s.dtype,
+                   1, b.h, b.d.err, st);
+  if (rc) return rc;
+  if ((rc = pm.mark(3, st))) return rc;
+  rc = run_grouped(b.h, w_down, b.d.counts, A, s.hidden, s.intermediate, s.experts, s.dtype, 0,
+                   b.xs, b.d.err, st);
+  if (rc) return rc;
+  if ((rc = pm.mark(4, st))) return rc;
+  HMOE_CUDA(launch_combine(b.xs, b.pos, w, w_is_f32, idx, s.experts, s.tokens, s.hidden, s.top_k,
+                           s.dtype, final_in, out, st), "combine");
+  return pm.mark(5, st);
+}
+
+int ffn_forward_impl(const hmoe_shape* shape, const void* x, const void* w_router,
+                     const void* router_bias, const void* w_gate_up, const void* w_down, void* y,
+                     int accumulate, int32_t* topk_idx, void* topk_weight, int32_t* counts,
+                     int32_t* sort_idx, void* workspace, size_t workspace_bytes, void* stream,
+                     const PhaseMarks& pm);
+
+}  // namespace
+
+namespace hmoe {
+int num_sms_for_current_device() {
+  static int sms[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (!sms[dev]) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    sms[dev] = n > 0 ? n : 148;
+  }
+  const int n = sms[dev] - sm_margin();
+  return n > 0 ? n : 1;
+}
+}  // namespace hmoe
+
+extern "C" {
+
+const char* hmoe_version(void) { return "hrm-moe-b200 0.1 (sm_100a)"; }
+
+const char* hmoe_last_error(void) { return g_last_error.c_str(); }
+
+size_t hmoe_ffn_workspace_bytes(const hmoe_shape* shape) {
+  return plan_bytes(shape, [](Carve& c, const hmoe_shape& s) { carve_ffn(c, s); });
+}
+
+int hmoe_ffn_forward(const hmoe_shape* shape, const void* x, const void* w_router,
+                     const void* router_bias, const void* w_gate_up, const void* w_down, void* y,
+                     int accumulate, int32_t* topk_idx, void* topk_weight, int32_t* counts,
+                     int32_t* sort_idx, void* workspace, size_t workspace_bytes, void* stream) {
+  return ffn_forward_impl(shape, x, w_router, router_bias, w_gate_up, w_down, y, accumulate,
+                          topk_idx, topk_weight, counts, sort_idx, workspace, workspace_bytes,
+                          stream, PhaseMarks());
+}
+
+int hmoe_ffn_forward_marked(const hmoe_shape* shape, const void* x, const void* w_router,
+                            const void* router_bias, const void* w_gate_up, const void* w_down,
+                            void* y, int accumulate, void* workspace, size_t workspace_bytes,
+                            void* stream, void* const* phase_events) {
+  PhaseMarks pm;
+  pm.ev = phase_events;
+  return ffn_forward_impl(shape, x, w_router, router_bias, w_gate_up, w_down, y, accumulate,
+                          nullptr, nullptr, nullptr, nullptr, workspace, workspace_bytes, stream,
+                          pm);
+}
+
+}  // extern "C"
+
+namespace {
+int ffn_forward_impl(const hmoe_shape* shape, const void* x, const void* w_router,
+                     const void* router_bias, const void* w_gate_up, const void* w_down, void* y,
+                     int accumulate, int32_t* topk_idx, void* topk_weight, int32_t* counts,
+                     int32_t* sort_idx, void* workspace, size_t workspace_bytes, void* stream,
+                     const PhaseMarks& pm) {
+  int rc = validate_shape(shape);
+  if (rc) return rc;
+  const hmoe_shape& s = *shape;
+  if (s.tokens == 0) return HMOE_OK;
+  if (!x || !w_router || !w_gate_up || !w_down || !y)
+    return fail(HMOE_EINVAL, "x, w_router, w_gate_up, w_down and y are required");
+  if (!aligned16(x) || !aligned16(w_gate_up) || !aligned16(w_down) || !aligned16(y) ||
+      !aligned16(w_router))
+    return fail(HMOE_EINVAL, "x, weights and y must be 16-byte aligned");
+  if ((rc = select_device(x))) return rc;
+  const size_t need = hmoe_ffn_workspace_bytes(shape);
+  if ((rc = check_ws(workspace, workspace_bytes, need))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Carve c{static_cast<char*>(workspace)};
+  FfnBufs b = carve_ffn(c, s);
+  int32_t* idx = topk_idx ? topk_idx : b.topk_idx;
+  HMOE_CUDA(cudaMemsetAsync(b.x.d.err, 0, sizeof(int), st), "reset error word");
+  if ((rc = pm.mark(0, st))) return rc;
+  HMOE_CUDA(launch_router_topk(x, w_router, router_bias, s.tokens, s.hidden, s.experts, s.top_k,
+                               s.dtype, s.norm_topk_prob, idx, b.topk_w, topk_weight, nullptr, st),
+            "router_topk");
+  if ((rc = pm.mark(1, st))) return rc;
+  return run_experts(s, x, idx, b.topk_w, 1, w_gate_up, w_down, accumulate ? y : nullptr, y,
+                     counts, sort_idx, b.x, st, pm);
+}
+}  // namespace
+
+extern "C" {
+
+int hmoe_router_topk(const hmoe_shape* shape, const void* x, const void* w_router,
+                     const void* router_bias, int32_t* topk_idx, void* topk_weight, void* logits,
+                     void* stream) {
+  int rc = validate_shape(shape);
+  if (rc) return rc;
+  const hmoe_shape& s = *shape;
+  if (s.tokens == 0) return HMOE_OK;
+  if (!x || !w_router || !topk_idx) return fail(HMOE_EINVAL, "x, w_router and topk_idx are required");
+  if (!aligned16(x) || !aligned16(w_router)) return fail(HMOE_EINVAL, "x and w_router must be 16-byte aligned");
+  if ((rc = select_device(x))) return rc;
+  HMOE_CUDA(launch_router_topk(x, w_router, router_bias, s.tokens, s.hidden, s.experts, s.top_k,
+                               s.dtype, s.norm_topk_prob, topk_idx, nullptr, topk_weight, logits,
+                               static_cast<cudaStream_t>(stream)),
+            "router_topk");
+  return HMOE_OK;
+}
+
+size_t hmoe_dispatch_workspace_bytes(const hmoe_shape* shape) {
+  return plan_bytes(shape, [](Carve& c, const hmoe_shape& s) {
+    carve_dispatch(c, s);
+    c.take<int32_t>(sizeof(int32_t) * s.tokens * s.top_k);  // pos
+  });
+}
+
+int hmoe_dispatch(const hmoe_shape* shape, const int32_t* topk_idx, const void* topk_weight,
+                  const void* x, int32_t* sort_idx, int32_t* counts, int32_t* sorted_token,
+                  void* sorted_weight, void* x_sorted, void* workspace, size_t workspace_bytes,
+                  void* stream) {
+  int rc = validate_shape(shape);
+  if (rc) return rc;
+  const hmoe_shape& s = *shape;
+  if (s.tokens == 0) return HMOE_OK;
+  if (!topk_idx) return fail(HMOE_EINVAL, "topk_idx is required");
+  if (sorted_weight && !topk_weight) return fail(HMOE_EINVAL, "sorted_weight needs topk_weight");
+  if (x_sorted && (!x || !aligned16(x) || !aligned16(x_sorted)))
+    return fail(HMOE_EINVAL, "x_sorted needs a 16-byte aligned x");
+  if ((rc = select_device(topk_idx))) return rc;
+  if ((rc = check_ws(workspace, workspace_bytes, hmoe_dispatch_workspace_bytes(shape)))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Carve c{static_cast<char*>(workspace)};
+  DispatchBufs b = carve_dispatch(c, s);
+  int32_t* pos = c.take<int32_t>(sizeof(int32_t) * s.tokens * s.top_k);
+  HMOE_CUDA(cudaMemsetAsync(b.err, 0, sizeof(int), st), "reset error word");
+  rc = run_dispatch(s, topk_idx, topk_weight, 0, x, b, pos, sort_idx, sorted_token, sorted_weight,
+                    x_sorted, st);
+  if (rc) return rc;
+  if (counts)
+    HMOE_CUDA(cudaMemcpyAsync(counts, b.counts, sizeof(int32_t) * s.experts,
+                              cudaMemcpyDeviceToDevice, st), "copy counts");
+  return HMOE_OK;
+}
+
+size_t hmoe_experts_workspace_bytes(const hmoe_shape* shape) {
+  return plan_bytes(shape, [](Carve& c, const hmoe_shape& s) { carve_experts(c, s); });
+}
+
+int hmoe_experts_forward(const hmoe_shape* shape, const void* hidden, const int32_t* topk_idx,
+                         const void* topk_weight, const void* w_gate_up, const void* w_down,
+                         void* final_hidden_states, int32_t* counts, int32_t* sort_idx,
+                         void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = validate_shape(shape);
+  if (rc) return rc;
+  const hmoe_shape& s = *shape;
+  if (s.tokens == 0) return HMOE_OK;
+  if (!hidden || !topk_idx || !topk_weight || !w_gate_up || !w_down || !final_hidden_states)
+    return fail(HMOE_EINVAL, "all tensor arguments are required");
+  if (!aligned16(hidden) || !aligned16(w_gate_up) || !aligned16(w_down) ||
+      !aligned16(final_hidden_states))
+    return fail(HMOE_EINVAL, "hidden, weights and final_hidden_states must be 16-byte aligned");
+  if ((rc = select_device(hidden))) return rc;
+  if ((rc = check_ws(workspace, workspace_bytes, hmoe_experts_workspace_bytes(shape)))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Carve c{static_cast<char*>(workspace)};
+  ExpertBufs b = carve_experts(c, s);
+  HMOE_CUDA(cudaMemsetAsync(b.d.err, 0, sizeof(int), st), "reset error word");
+  return run_experts(s, hidden, topk_idx, topk_weight, 0, w_gate_up, w_down, final_hidden_states,
+                     final_hidden_states, counts, sort_idx, b, st);
+}
+
+size_t hmoe_grouped_linear_workspace_bytes(int32_t groups) {
+  (void)groups;
+  return kAlign;  // the device error word
+}
+
+static int grouped_common(const void* input, const void* weight, const int32_t* tpe, int64_t M,
+                          int32_t N, int32_t K, int32_t G, int32_t dtype, void* output,
+                          void* workspace, size_t workspace_bytes, void* stream, int swiglu) {
+  if (M < 0 || N <= 0 || K <= 0 || G <= 0)
+    return fail(HMOE_EINVAL, "bad grouped GEMM shape M=%lld N=%d K=%d G=%d", (long long)M, N, K, G);
+  if (dtype != HMOE_DTYPE_BF16 && dtype != HMOE_DTYPE_F32)
+    return fail(HMOE_EINVAL, "unsupported dtype %d", dtype);
+  if (N % 8 != 0 || K % 8 != 0) return fail(HMOE_EINVAL, "N and K must be multiples of 8");
+  if (G > 1024) return fail(HMOE_EINVAL, "at most 1024 groups");
+  if (M == 0) return HMOE_OK;
+  if (!input || !weight || !tpe || !output) return fail(HMOE_EINVAL, "NULL tensor argument");
+  if (!aligned16(input) || !aligned16(weight) || !aligned16(output))
+    return fail(HMOE_EINVAL, "input, weight and output must be 16-byte aligned");
+  int rc = select_device(input);
+  if (rc) return rc;
+  int* err = nullptr;
+  if (workspace && workspace_bytes >= sizeof(int)) {
+    err = static_cast<int*>(workspace);
+    HMOE_CUDA(cudaMemsetAsync(err, 0, sizeof(int), static_cast<cudaStream_t>(stream)),
+              "reset error word");
+  }
+  return run_grouped(input, weight, tpe, M, N, K, G, dtype, swiglu, output, err,
+                     static_cast<cudaStream_t>(stream));
+}
+
+int hmoe_grouped_linear(const void* input, const void* weight, const int32_t* tokens_per_expert,
+                        int64_t M, int32_t N, int32_t K, int32_t groups, int32_t dtype,
+                        void* output, void* workspace, size_t workspace_bytes, void* stream) {
+  return grouped_common(input, weight, tokens_per_expert, M, N, K, groups, dtype, output,
+                        workspace, workspace_bytes, stream, 0);
+}
+
+int hmoe_grouped_swiglu(const void* input, const void* w_gate_up,
+                        const int32_t* tokens_per_expert, int64_t M, int32_t I, int32_t K,
+                        int32_t groups, int32_t dtype, void* output, void* workspace,
+                        size_t workspace_bytes, void* stream) {
+  return grouped_common(input, w_gate_up, tokens_per_expert, M, I, K, groups, dtype, output,
+                        workspace, workspace_bytes, stream, 1);
+}
+
+size_t hmoe_combine_workspace_bytes(const hmoe_shape* shape) {
+  return plan_bytes(shape, [](Carve& c, const hmoe_shape& s) {
+    c.take<int32_t>(sizeof(int32_t) * s.tokens * s.top_k);
+  });
+}
+
+int hmoe_combine(const hmoe_shape* shape, const void* expert_out, const int32_t* sort_idx,
+                 const void* topk_weight, void* final_hidden_states, void* workspace,
+                 size_t workspace_bytes, void* stream) {
+  int rc = validate_shape(shape);
+  if (rc) return rc;
+  const hmoe_shape& s = *shape;
+  if (s.tokens == 0) return HMOE_OK;
+  if (!expert_out || !sort_idx || !topk_weight || !final_hidden_states)
+    return fail(HMOE_EINVAL, "all tensor arguments are required");
+  if (!aligned16(expert_out) || !aligned16(final_hidden_states))
+    return fail(HMOE_EINVAL, "expert_out and final_hidden_states must be 16-byte aligned");
+  if ((rc = select_device(expert_out))) return rc;
+  if ((rc = check_ws(workspace, workspace_bytes, hmoe_combine_workspace_bytes(shape)))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int32_t* pos = static_cast<int32_t*>(workspace);
+  const int64_t A = s.tokens * s.top_k;
+  HMOE_CUDA(cudaMemsetAsync(pos, 0xff, sizeof(int32_t) * A, st), "clear positions");
+  HMOE_CUDA(launch_invert_perm(sort_idx, A, pos, st), "invert_perm");
+  HMOE_CUDA(launch_combine(expert_out, pos, topk_weight, 0, nullptr, s.experts, s.tokens, s.hidden,
+                           s.top_k, s.dtype, final_hidden_states, final_hidden_states, st),
+            "combine");
+  return HMOE_OK;
+}
+
+int hmoe_workspace_status(const void* workspace, void* stream) {
+  if (!workspace) return fail(HMOE_EINVAL, "workspace is NULL");
+  int rc = select_device(workspace);
+  if (rc) return rc;
+  int word = 0;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  HMOE_CUDA(cudaMemcpyAsync(&word, workspace, sizeof(int), cudaMemcpyDeviceToHost, st),
+            "read error word");
+  HMOE_CUDA(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+  if (word == kDevBadExpert) return fail(HMOE_EINVAL, "an expert id outside [0, experts) was dropped");
+  if (word == kDevTimeout) return fail(HMOE_ETIMEDOUT, "a device-side wait gave up");
+  if (word != kDevOk) return fail(HMOE_EIO, "unknown device error word %d", word);
+  return HMOE_OK;
+}
+
+}  // extern "C"

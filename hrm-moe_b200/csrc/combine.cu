@@ -1,0 +1,116 @@
+// Combine: weighted sum of each token's k expert outputs, back in token order.
+//
+// Mirrors models/layers.py:332-334 of HRM-MoE:
+//   expert_output = expert_output * sorted_weights[:, None]
+//   final_hidden_states.index_add_(0, sorted_token_idx, expert_output)
+// as a gather instead of a scatter: one warp per token reads the k rows
+// pos(t, 0..k-1) of the expert-sorted output, accumulates w_j * row_j in
+// fp32 (j ascending) on top of the existing accumulator and rounds once.
+// No atomics, so the result is deterministic (the reference's CUDA
+// index_add_ is not).
+#include "common.cuh"
+#include "internal.h"
+
+namespace hmoe {
+namespace {
+
+constexpr int kCombThreads = 256;
+constexpr int kMaxK = 32;
+
+template <bool BF16>
+__global__ void __launch_bounds__(kCombThreads)
+combine_kernel(const void* __restrict__ expert_out, const int32_t* __restrict__ pos,
+               const void* __restrict__ topk_w, int topk_w_is_f32, int64_t T, int row_chunks,
+               int k, const void* __restrict__ final_in, void* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * (kCombThreads / 32) + (threadIdx.x >> 5);
+  if (t >= T) return;
+  int p = -1;
+  float w = 0.0f;
+  if (lane < k) {
+    p = pos[t * k + lane];
+    if (topk_w_is_f32)
+      w = static_cast<const float*>(topk_w)[t * k + lane];
+    else
+      w = BF16 ? bf16_bits_to_f32(static_cast<const uint16_t*>(topk_w)[t * k + lane])
+               : static_cast<const float*>(topk_w)[t * k + lane];
+  }
+  const uint4* src = static_cast<const uint4*>(expert_out);
+  const uint4* fin = static_cast<const uint4*>(final_in);
+  uint4* dst = static_cast<uint4*>(out);
+  constexpr int EPC = BF16 ? 8 : 4;  // elements per 16-byte chunk
+  // every lane runs the same trip count so the shuffles below see all 32 lanes
+  for (int c0 = 0; c0 < row_chunks; c0 += 32) {
+    const int c = c0 + lane;
+    const bool live = c < row_chunks;
+    float acc[EPC];
+    if (fin && live) {
+      const uint4 u = fin[t * row_chunks + c];
+      if (BF16) {
+        const uint32_t q[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) { acc[2 * i] = bf16_lo(q[i]); acc[2 * i + 1] = bf16_hi(q[i]); }
+      } else {
+        acc[0] = __uint_as_float(u.x); acc[1] = __uint_as_float(u.y);
+        acc[2] = __uint_as_float(u.z); acc[3] = __uint_as_float(u.w);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < EPC; ++i) acc[i] = 0.0f;
+    }
+    for (int j = 0; j < k; ++j) {
+      const int pj = __shfl_sync(0xffffffffu, p, j);
+      const float wj = __shfl_sync(0xffffffffu, w, j);
+      if (pj < 0 || !live) continue;
+      const uint4 u = __ldg(src + static_cast<int64_t>(pj) * row_chunks + c);
+      if (BF16) {
+        const uint32_t q[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          acc[2 * i] = fmaf(wj, bf16_lo(q[i]), acc[2 * i]);
+          acc[2 * i + 1] = fmaf(wj, bf16_hi(q[i]), acc[2 * i + 1]);
+        }
+      } else {
+        acc[0] = fmaf(wj, __uint_as_float(u.x), acc[0]);
+        acc[1] = fmaf(wj, __uint_as_float(u.y), acc[1]);
+        acc[2] = fmaf(wj, __uint_as_float(u.z), acc[2]);
+        acc[3] = fmaf(wj, __uint_as_float(u.w), acc[3]);
+      }
+    }
+    uint4 o;
+    if (BF16) {
+      o.x = pack_bf16x2(acc[0], acc[1]);
+      o.y = pack_bf16x2(acc[2], acc[3]);
+      o.z = pack_bf16x2(acc[4], acc[5]);
+      o.w = pack_bf16x2(acc[6], acc[7]);
+    } else {
+      o.x = __float_as_uint(acc[0]); o.y = __float_as_uint(acc[1]);
+      o.z = __float_as_uint(acc[2]); o.w = __float_as_uint(acc[3]);
+    }
+    if (live) dst[t * row_chunks + c] = o;
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_combine(const void* expert_out, const int32_t* pos, const void* topk_w,
+                           int topk_w_is_f32, const int32_t* /*topk_idx*/, int /*E*/, int64_t T,
+                           int d, int k, int dtype, const void* final_in, void* out,
+                           cudaStream_t stream) {
+  if (T == 0) return cudaSuccess;
+  if (k > kMaxK) return cudaErrorInvalidValue;
+  const bool bf16 = dtype == kDtypeBF16;
+  const int row_chunks = d * (bf16 ? 2 : 4) / 16;
+  const unsigned blocks = static_cast<unsigned>(cdiv64(T, kCombThreads / 32));
+  if (bf16)
+    combine_kernel<true><<<blocks, kCombThreads, 0, stream>>>(expert_out, pos, topk_w,
+                                                              topk_w_is_f32, T, row_chunks, k,
+                                                              final_in, out);
+  else
+    combine_kernel<false><<<blocks, kCombThreads, 0, stream>>>(expert_out, pos, topk_w,
+                                                               topk_w_is_f32, T, row_chunks, k,
+                                                               final_in, out);
+  return cudaGetLastError();
+}
+
+}  // namespace hmoe

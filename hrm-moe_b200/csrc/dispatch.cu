@@ -1,0 +1,237 @@
+// Dispatch: stable sort of the T*k assignments by expert, counts, gather.
+//
+// Mirrors models/layers.py:311-322 of HRM-MoE:
+//   flat_experts = selected_experts.reshape(-1)
+//   sorted_experts, sort_idx = torch.sort(flat_experts, stable=True)
+//   sorted_hidden_states = hidden_states.index_select(0, sort_idx // k)
+//   tokens_per_expert = bincount(sorted_experts)
+//
+// Positions are computed without atomics, so they equal the stable sort:
+//  1. hist_rank: each block of tokens counts its assignments per expert and
+//     gives every assignment its rank among same-expert assignments of the
+//     block with a smaller flat index (warp __match_any_sync + chunk scan).
+//  2. scan: block counts -> absolute row offset of (expert, block), plus
+//     tokens_per_expert.
+//  3. permute_gather: position = offset(expert, block) + rank; one warp per
+//     token reads its hidden row once and writes it to its k positions.
+#include "common.cuh"
+#include "internal.h"
+
+namespace hmoe {
+namespace {
+
+constexpr int kHistThreads = 256;
+constexpr int kHistFlat = 1024;          // assignments per histogram block
+constexpr int kHistChunks = kHistFlat / 32;
+constexpr int kMaxExperts = 128;
+
+__global__ void __launch_bounds__(kHistThreads)
+hist_rank_kernel(const int32_t* __restrict__ topk_idx, int64_t T, int k, int E, int tblk,
+                 int32_t* __restrict__ local_rank, int32_t* __restrict__ block_counts,
+                 int* __restrict__ err) {
+  __shared__ int32_t cnt[kHistChunks][kMaxExperts];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t f0 = static_cast<int64_t>(blockIdx.x) * tblk * k;  // first flat index
+  const int64_t fend = min(static_cast<int64_t>(T) * k, f0 + static_cast<int64_t>(tblk) * k);
+  const int nflat = static_cast<int>(fend - f0);
+  const int nchunks = cdiv(nflat, 32);
+
+  for (int i = tid; i < kHistChunks * kMaxExperts; i += kHistThreads)
+    (&cnt[0][0])[i] = 0;
+  __syncthreads();
+
+  constexpr int kRounds = kHistChunks / (kHistThreads / 32);  // 4
+  int my_e[kRounds], my_rank[kRounds];
+#pragma unroll
+  for (int r = 0; r < kRounds; ++r) {
+    const int c = r * (kHistThreads / 32) + warp;
+    const int f = c * 32 + lane;
+    int e = -1;
+    if (f < nflat) {
+      e = topk_idx[f0 + f];
+      if (e < 0 || e >= E) {
+        record_error(err, kDevBadExpert);
+        e = -1;
+      }
+    }
+    const unsigned m = __match_any_sync(0xffffffffu, e);
+    my_e[r] = e;
+    my_rank[r] = __popc(m & ((1u << lane) - 1u));
+    if (e >= 0 && lane == __ffs(m) - 1) cnt[c][e] = __popc(m);
+  }
+  __syncthreads();
+  // exclusive scan over chunks, per expert
+  if (tid < E) {
+    int run = 0;
+    for (int c = 0; c < nchunks; ++c) {
+      const int v = cnt[c][tid];
+      cnt[c][tid] = run;
+      run += v;
+    }
+    block_counts[static_cast<int64_t>(blockIdx.x) * E + tid] = run;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int r = 0; r < kRounds; ++r) {
+    const int c = r * (kHistThreads / 32) + warp;
+    const int f = c * 32 + lane;
+    if (f < nflat) local_rank[f0 + f] = my_e[r] >= 0 ? cnt[c][my_e[r]] + my_rank[r] : -1;
+  }
+}
+
+// One CTA: per expert, exclusive scan of its block counts (in place), then
+// an exclusive scan over expert totals, then absolute offsets.
+constexpr int kScanThreads = 1024;
+
+__global__ void __launch_bounds__(kScanThreads)
+scan_kernel(int32_t* __restrict__ block_counts, int64_t nblk, int E,
+            int32_t* __restrict__ counts, int32_t* __restrict__ expert_offsets) {
+  __shared__ int32_t totals[kMaxExperts];
+  __shared__ int32_t base[kMaxExperts + 1];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int e = warp; e < E; e += kScanThreads / 32) {
+    int carry = 0;
+    for (int64_t b0 = 0; b0 < nblk; b0 += 32) {
+      const int64_t b = b0 + lane;
+      const int v = b < nblk ? block_counts[b * E + e] : 0;
+      int incl = v;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int o = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += o;
+      }
+      if (b < nblk) block_counts[b * E + e] = carry + incl - v;
+      carry += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) totals[e] = carry;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int run = 0;
+    for (int e = 0; e < E; ++e) {
+      base[e] = run;
+      run += totals[e];
+    }
+    base[E] = run;
+  }
+  __syncthreads();
+  if (tid < E) {
+    if (counts) counts[tid] = totals[tid];
+  }
+  if (tid <= E && expert_offsets) expert_offsets[tid] = base[tid];
+  const int64_t n = nblk * E;
+  for (int64_t i = tid; i < n; i += kScanThreads) block_counts[i] += base[i % E];
+}
+
+// One warp per token.  Row bytes must be a multiple of 16.
+constexpr int kPermThreads = 256;
+constexpr int kPermSeg = 8;  // 16-byte chunks per lane held in registers at a time
+
+__global__ void __launch_bounds__(kPermThreads)
+permute_gather_kernel(const int32_t* __restrict__ topk_idx, const int32_t* __restrict__ local_rank,
+                      const int32_t* __restrict__ block_offsets, const void* __restrict__ topk_w,
+                      int topk_w_is_f32, const void* __restrict__ x, int64_t T, int row_chunks,
+                      int k, int E, int tblk, int dtype, int32_t* __restrict__ pos,
+                      int32_t* __restrict__ sort_idx, int32_t* __restrict__ sorted_token,
+                      void* __restrict__ sorted_w, uint4* __restrict__ x_sorted) {
+  const int lane = threadIdx.x & 31;
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * (kPermThreads / 32) + (threadIdx.x >> 5);
+  if (t >= T) return;
+  const int64_t blk = t / tblk;
+  // lane j < k resolves assignment j of this token
+  int p = -1;
+  if (lane < k) {
+    const int64_t f = t * k + lane;
+    const int e = topk_idx[f];
+    const int r = local_rank[f];
+    if (e >= 0 && e < E && r >= 0) {
+      p = block_offsets[blk * E + e] + r;
+      if (sort_idx) sort_idx[p] = static_cast<int32_t>(f);
+      if (sorted_token) sorted_token[p] = static_cast<int32_t>(t);
+      if (sorted_w) {
+        const float w = topk_w_is_f32 ? static_cast<const float*>(topk_w)[f]
+                                      : load_elem(topk_w, f, dtype);
+        store_elem(sorted_w, p, w, dtype);
+      }
+    }
+    pos[f] = p;
+  }
+  if (!x_sorted) return;
+  const uint4* src = static_cast<const uint4*>(x) + t * row_chunks;
+  for (int c0 = 0; c0 < row_chunks; c0 += 32 * kPermSeg) {
+    uint4 buf[kPermSeg];
+#pragma unroll
+    for (int s = 0; s < kPermSeg; ++s) {
+      const int c = c0 + s * 32 + lane;
+      if (c < row_chunks) buf[s] = __ldg(src + c);
+    }
+    for (int j = 0; j < k; ++j) {
+      const int pj = __shfl_sync(0xffffffffu, p, j);
+      if (pj < 0) continue;
+      uint4* dst = x_sorted + static_cast<int64_t>(pj) * row_chunks;
+#pragma unroll
+      for (int s = 0; s < kPermSeg; ++s) {
+        const int c = c0 + s * 32 + lane;
+        if (c < row_chunks) dst[c] = buf[s];
+      }
+    }
+  }
+}
+
+__global__ void invert_perm_kernel(const int32_t* __restrict__ sort_idx, int64_t n,
+                                   int32_t* __restrict__ pos) {
+  const int64_t p = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (p < n) {
+    const int32_t f = sort_idx[p];
+    if (f >= 0 && f < n) pos[f] = static_cast<int32_t>(p);
+  }
+}
+
+}  // namespace
+
+int dispatch_block_tokens(int k) { return k > 0 ? (kHistFlat / k > 0 ? kHistFlat / k : 1) : 1; }
+
+int64_t dispatch_num_blocks(int64_t T, int k) { return cdiv64(T, dispatch_block_tokens(k)); }
+
+cudaError_t launch_hist_rank(const int32_t* topk_idx, int64_t T, int k, int E,
+                             int32_t* local_rank, int32_t* block_counts, int* err,
+                             cudaStream_t stream) {
+  if (T == 0) return cudaSuccess;
+  const int tblk = dispatch_block_tokens(k);
+  const int64_t nblk = dispatch_num_blocks(T, k);
+  hist_rank_kernel<<<static_cast<unsigned>(nblk), kHistThreads, 0, stream>>>(
+      topk_idx, T, k, E, tblk, local_rank, block_counts, err);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_scan(int32_t* block_counts, int64_t nblk, int E, int32_t* counts,
+                        int32_t* expert_offsets, cudaStream_t stream) {
+  scan_kernel<<<1, kScanThreads, 0, stream>>>(block_counts, nblk, E, counts, expert_offsets);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_permute_gather(const int32_t* topk_idx, const int32_t* local_rank,
+                                  const int32_t* block_offsets, const void* topk_w,
+                                  int topk_w_is_f32, const void* x, int64_t T, int d, int k,
+                                  int E, int dtype, int32_t* pos, int32_t* sort_idx,
+                                  int32_t* sorted_token, void* sorted_w, void* x_sorted,
+                                  cudaStream_t stream) {
+  if (T == 0) return cudaSuccess;
+  const int es = dtype == kDtypeBF16 ? 2 : 4;
+  const int row_chunks = d * es / 16;
+  const int64_t blocks = cdiv64(T, kPermThreads / 32);
+  permute_gather_kernel<<<static_cast<unsigned>(blocks), kPermThreads, 0, stream>>>(
+      topk_idx, local_rank, block_offsets, topk_w, topk_w_is_f32, x, T, row_chunks, k, E,
+      dispatch_block_tokens(k), dtype, pos, sort_idx, sorted_token, sorted_w,
+      static_cast<uint4*>(x_sorted));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_invert_perm(const int32_t* sort_idx, int64_t n, int32_t* pos,
+                               cudaStream_t stream) {
+  if (n == 0) return cudaSuccess;
+  invert_perm_kernel<<<static_cast<unsigned>(cdiv64(n, 256)), 256, 0, stream>>>(sort_idx, n, pos);
+  return cudaGetLastError();
+}
+
+}  // namespace hmoe

@@ -1,0 +1,413 @@
+// Grouped expert GEMMs on the sm_100a tensor cores (tcgen05 + TMEM + TMA).
+//
+// Replaces the forward kernel of models/moe_triton_grouped_gemm.py
+// (_m_grouped_gemm_bk_kernel, :113-184, launched from :358-417): for every
+// group g (an expert) the rows [off_g, off_g + n_g) of A are multiplied by
+// B[g]^T, with fp32 accumulation and a bf16 result:
+//   plain:   out[r, :] = A[r, :] @ B[g]^T                      B[g]: [N, K]
+//   swiglu:  out[r, :] = silu(A[r] @ Bg^T) * (A[r] @ Bu^T)     B[g]: [2N, K]
+//            (Bg = rows 0..N-1, Bu = rows N..2N-1; models/layers.py:326-329)
+//
+// Design (one persistent CTA per SM, 192 threads):
+//   warp 0      TMA producer: A tile [128 x 64] and two B boxes [128 x 64]
+//               per k-step into a 4-stage ring (128-byte swizzle).
+//   warp 1      allocates 512 TMEM columns; lane 0 issues tcgen05.mma
+//               (M=128, N=256, K=16) into one of two 256-column fp32
+//               accumulators and commits stage / accumulator barriers.
+//   warps 2..5  epilogue: tcgen05.ld the accumulator (each warp its 32-lane
+//               quadrant), apply the activation, convert to bf16, store the
+//               rows that belong to the group; then free the accumulator so
+//               the next tile's MMAs overlap this tile's stores.
+// Tiles are (group, 128-row block, column block); the table of group row
+// offsets and tile prefixes is built in shared memory from the per-group
+// counts on the device, so no host synchronisation is needed.  A group's
+// last row block may run into the next group's rows: those rows are loaded
+// (or zero-filled past the end of A) but never stored.
+//
+// Every mbarrier wait is bounded (kWaitLimitNs): on a timeout the kernel
+// records kDevTimeout, the roles leave their loops, outstanding bulk copies
+// and MMAs are waited for (again bounded) and TMEM is released.
+//
+// No TMA multicast is used anywhere (this kernel also runs in expert-
+// parallel jobs on several GPUs).
+#include <mutex>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace hmoe {
+namespace {
+
+constexpr int BM = 128;                       // rows per tile (MMA M)
+constexpr int BK = 64;                        // bf16 per swizzled 128-byte row
+constexpr int BNH = 128;                      // rows per B box
+constexpr int kStages = 4;
+constexpr int kABytes = BM * BK * 2;          // 16 KB
+constexpr int kBBoxBytes = BNH * BK * 2;      // 16 KB
+constexpr int kStageBytes = kABytes + 2 * kBBoxBytes;  // 48 KB
+constexpr int kAccCols = 256;                 // fp32 accumulator columns (MMA N)
+constexpr int kNumAcc = 2;
+constexpr int kTmemCols = kAccCols * kNumAcc; // 512 = all of TMEM
+constexpr int kThreads = 192;
+constexpr int kMaxGroups = 1024;
+
+struct SmemCtl {
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
+  uint64_t acc_full[kNumAcc];
+  uint64_t acc_empty[kNumAcc];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+  int num_m_tiles;
+  int pad_;
+  int group_rows[kMaxGroups + 1];   // exclusive prefix of rows
+  int tile_prefix[kMaxGroups + 1];  // exclusive prefix of 128-row blocks
+};
+
+constexpr size_t kSmemBytes = 1024 + static_cast<size_t>(kStages) * kStageBytes + sizeof(SmemCtl);
+
+struct KParams {
+  const int32_t* counts;
+  int G;
+  int64_t M;
+  int N;                    // output columns
+  int K;
+  int n_tiles;              // column blocks
+  int out_cols_per_tile;    // 128 (swiglu) or 256 (plain)
+  int b_rows_per_group;     // rows of B per group (2N swiglu, N plain)
+  int b_second_off;         // row offset of the second B box (N swiglu, 128 plain)
+  uint16_t* out;
+  int* err;
+  unsigned long long wait_limit_ns;
+};
+
+__device__ __forceinline__ void decode_tile(const SmemCtl& ctl, int G, int n_tiles, int tile,
+                                            int& g, int& row0, int& nrows, int& n) {
+  const int mt = tile / n_tiles;
+  n = tile - mt * n_tiles;
+  int lo = 0, hi = G;  // tile_prefix[lo] <= mt < tile_prefix[hi]
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (ctl.tile_prefix[mid] <= mt) lo = mid; else hi = mid;
+  }
+  g = lo;
+  row0 = ctl.group_rows[g] + (mt - ctl.tile_prefix[g]) * BM;
+  nrows = min(BM, ctl.group_rows[g + 1] - row0);
+}
+
+template <bool SWIGLU>
+__device__ __forceinline__ void store_chunk32(const uint32_t (&a)[32], const uint32_t (&b)[32],
+                                              uint16_t* orow, int col0, int N) {
+  uint32_t packed[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    float v0, v1;
+    if (SWIGLU) {
+      // gate_up is a bf16 tensor in the reference, F.silu returns bf16 and
+      // the product is rounded again (models/layers.py:326-329).
+      const float g0 = round_bf16(__uint_as_float(a[2 * i]));
+      const float g1 = round_bf16(__uint_as_float(a[2 * i + 1]));
+      const float u0 = round_bf16(__uint_as_float(b[2 * i]));
+      const float u1 = round_bf16(__uint_as_float(b[2 * i + 1]));
+      const float s0 = round_bf16(g0 / (1.0f + expf(-g0)));
+      const float s1 = round_bf16(g1 / (1.0f + expf(-g1)));
+      v0 = s0 * u0;
+      v1 = s1 * u1;
+    } else {
+      v0 = __uint_as_float(a[2 * i]);
+      v1 = __uint_as_float(a[2 * i + 1]);
+    }
+    packed[i] = pack_bf16x2(v0, v1);
+  }
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    if (col0 + c * 8 + 8 <= N) {
+      uint4 v = make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2], packed[4 * c + 3]);
+      *reinterpret_cast<uint4*>(orow + col0 + c * 8) = v;
+    }
+  }
+}
+
+template <bool SWIGLU>
+__global__ void __launch_bounds__(kThreads, 1)
+grouped_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
+                          const __grid_constant__ CUtensorMap tmB, const KParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  SmemCtl& ctl = *reinterpret_cast<SmemCtl*>(smem + kStages * kStageBytes);
+  const uint32_t sbase = smem_u32(smem);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int G = p.G;
+
+  // ---------------------------------------------------------------- setup
+  if (warp == 0) {
+    const int per = cdiv(G, 32);
+    const int g0 = min(G, lane * per), g1 = min(G, g0 + per);
+    int rows = 0, tiles = 0;
+    for (int g = g0; g < g1; ++g) {
+      const int c = max(0, p.counts[g]);
+      rows += c;
+      tiles += cdiv(c, BM);
+    }
+    int rin = rows, tin = tiles;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int ro = __shfl_up_sync(0xffffffffu, rin, off);
+      const int to = __shfl_up_sync(0xffffffffu, tin, off);
+      if (lane >= off) { rin += ro; tin += to; }
+    }
+    int rr = rin - rows, tr = tin - tiles;
+    for (int g = g0; g < g1; ++g) {
+      const int c = max(0, p.counts[g]);
+      ctl.group_rows[g] = rr;
+      ctl.tile_prefix[g] = tr;
+      rr += c;
+      tr += cdiv(c, BM);
+    }
+    if (lane == 31) {
+      ctl.group_rows[G] = rin;
+      ctl.tile_prefix[G] = tin;
+      ctl.num_m_tiles = tin;
+    }
+    if (lane == 0) {
+      for (int s = 0; s < kStages; ++s) {
+        mbar_init(smem_u32(&ctl.full[s]), 1);
+        mbar_init(smem_u32(&ctl.empty[s]), 1);
+      }
+      for (int a = 0; a < kNumAcc; ++a) {
+        mbar_init(smem_u32(&ctl.acc_full[a]), 1);
+        mbar_init(smem_u32(&ctl.acc_empty[a]), 4);
+      }
+      mbar_init(smem_u32(&ctl.drain), 1);
+      ctl.abort = 0;
+      fence_mbar_init();
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB);
+    }
+  } else if (warp == 1) {
+    tmem_alloc(smem_u32(&ctl.tmem_base), kTmemCols);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+
+  const uint32_t tmem_base = ctl.tmem_base;
+  const int num_tiles = ctl.num_m_tiles * p.n_tiles;
+  const int nkb = cdiv(p.K, BK);
+  volatile int* abort = &ctl.abort;
+  int never = 0;  // an abort flag nobody raises, for the teardown waits
+  const unsigned long long lim = p.wait_limit_ns;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0, pending = 0, pend_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+        int g, row0, nrows, n;
+        decode_tile(ctl, G, p.n_tiles, tile, g, row0, nrows, n);
+        const int rb0 = g * p.b_rows_per_group + n * p.out_cols_per_tile;
+        const int rb1 = rb0 + p.b_second_off;
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!mbar_wait_bounded(smem_u32(&ctl.empty[stage]), phase ^ 1u, abort, p.err, lim)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = smem_u32(&ctl.full[stage]);
+          const uint32_t sa = sbase + stage * kStageBytes;
+          mbar_arrive_expect_tx(fb, kStageBytes);
+          tma_load_2d(sa, &tmA, kb * BK, row0, fb);
+          tma_load_2d(sa + kABytes, &tmB, kb * BK, rb0, fb);
+          tma_load_2d(sa + kABytes + kBBoxBytes, &tmB, kb * BK, rb1, fb);
+          pending |= 1u << stage;
+          pend_phase = (pend_phase & ~(1u << stage)) | (phase << stage);
+          if (++stage == kStages) { stage = 0; phase ^= 1u; }
+        }
+      }
+      // no bulk copy may still be landing in shared memory when the CTA exits
+      for (int s = 0; s < kStages; ++s)
+        if ((pending >> s) & 1u)
+          mbar_wait_bounded(smem_u32(&ctl.full[s]), (pend_phase >> s) & 1u, &never, p.err, lim);
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      int stage = 0, acc = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      constexpr uint32_t idesc = idesc_bf16_f32(BM, kAccCols);
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+        if (!mbar_wait_bounded(smem_u32(&ctl.acc_empty[acc]), acc_phase ^ 1u, abort, p.err, lim)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kAccCols);
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!mbar_wait_bounded(smem_u32(&ctl.full[stage]), phase, abort, p.err, lim)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = sbase + stage * kStageBytes;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t ad = smem_desc_sw128(sa + kk * 32);
+            const uint64_t bd = smem_desc_sw128(sa + kABytes + kk * 32);
+            tc_mma_bf16(d_tmem, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          tc_commit(smem_u32(&ctl.empty[stage]));
+          if (++stage == kStages) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        tc_commit(smem_u32(&ctl.acc_full[acc]));
+        if (++acc == kNumAcc) { acc = 0; acc_phase ^= 1u; }
+      }
+      // every MMA issued above has finished before TMEM is released
+      tc_commit(smem_u32(&ctl.drain));
+      mbar_wait_bounded(smem_u32(&ctl.drain), 0, &never, p.err, lim);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quad = warp & 3;                 // TMEM lanes this warp may read
+    const int r_in_tile = quad * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      int g, row0, nrows, n;
+      decode_tile(ctl, G, p.n_tiles, tile, g, row0, nrows, n);
+      if (!mbar_wait_bounded(smem_u32(&ctl.acc_full[acc]), acc_phase, abort, p.err, lim)) break;
+      tc_fence_after();
+      const uint32_t trow = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
+                            static_cast<uint32_t>(acc * kAccCols);
+      const int64_t grow = static_cast<int64_t>(row0) + r_in_tile;
+      const bool row_ok = r_in_tile < nrows && grow < p.M;
+      uint16_t* orow = p.out + grow * p.N;
+      if (SWIGLU) {
+#pragma unroll 1
+        for (int c = 0; c < BNH / 32; ++c) {
+          uint32_t ga[32], ua[32];
+          tmem_ld_32cols(trow + c * 32, ga);
+          tmem_ld_32cols(trow + BNH + c * 32, ua);
+          tc_wait_ld();
+          if (row_ok) store_chunk32<true>(ga, ua, orow, n * p.out_cols_per_tile + c * 32, p.N);
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < kAccCols / 32; ++c) {
+          uint32_t ra[32];
+          tmem_ld_32cols(trow + c * 32, ra);
+          tc_wait_ld();
+          if (row_ok) store_chunk32<false>(ra, ra, orow, n * p.out_cols_per_tile + c * 32, p.N);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&ctl.acc_empty[acc]));
+      if (++acc == kNumAcc) { acc = 0; acc_phase ^= 1u; }
+    }
+  }
+
+  // --------------------------------------------------------------- teardown
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------ host side ----
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+// Row-major bf16 matrix [rows, cols] as a 2-D map with [box_rows, 64] boxes.
+bool make_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return false;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {cols * 2};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(BK), box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
+                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <bool SWIGLU>
+cudaError_t ensure_smem_attr() {
+  // once per device: opt in to the large dynamic shared memory carve-out
+  static int done[64] = {0};
+  static std::mutex mu;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!done[dev]) {
+    e = cudaFuncSetAttribute(grouped_gemm_sm100_kernel<SWIGLU>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kSmemBytes));
+    if (e != cudaSuccess) return e;
+    done[dev] = 1;
+  }
+  return cudaSuccess;
+}
+
+}  // namespace
+
+cudaError_t launch_grouped_gemm_sm100(const GroupedGemmArgs& a, cudaStream_t stream) {
+  if (a.M == 0 || a.G == 0) return cudaSuccess;
+  if (a.G > kMaxGroups || a.K % 8 != 0 || a.N % 8 != 0) return cudaErrorInvalidValue;
+  const int nw = a.swiglu ? 2 * a.N : a.N;          // rows of B per group
+  CUtensorMap ma, mb;
+  if (!make_map(&ma, a.a, static_cast<uint64_t>(a.M), static_cast<uint64_t>(a.K), BM) ||
+      !make_map(&mb, a.b, static_cast<uint64_t>(a.G) * nw, static_cast<uint64_t>(a.K), BNH))
+    return cudaErrorInvalidValue;
+  KParams p;
+  p.counts = a.counts;
+  p.G = a.G;
+  p.M = a.M;
+  p.N = a.N;
+  p.K = a.K;
+  p.out_cols_per_tile = a.swiglu ? BNH : kAccCols;
+  p.n_tiles = cdiv(a.N, p.out_cols_per_tile);
+  p.b_rows_per_group = nw;
+  p.b_second_off = a.swiglu ? a.N : BNH;
+  p.out = static_cast<uint16_t*>(a.out);
+  p.err = a.err;
+  p.wait_limit_ns = kWaitLimitNs;
+  const int sms = a.sm_limit > 0 ? a.sm_limit : num_sms_for_current_device();
+  const int64_t max_tiles = (cdiv64(a.M, BM) + a.G) * p.n_tiles;
+  const int grid = static_cast<int>(max_tiles < sms ? max_tiles : sms);
+  cudaError_t e;
+  if (a.swiglu) {
+    if ((e = ensure_smem_attr<true>()) != cudaSuccess) return e;
+    grouped_gemm_sm100_kernel<true><<<grid, kThreads, kSmemBytes, stream>>>(ma, mb, p);
+  } else {
+    if ((e = ensure_smem_attr<false>()) != cudaSuccess) return e;
+    grouped_gemm_sm100_kernel<false><<<grid, kThreads, kSmemBytes, stream>>>(ma, mb, p);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace hmoe

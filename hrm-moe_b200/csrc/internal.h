@@ -1,0 +1,67 @@
+// Host-side launchers shared between the kernel files and the C ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace hmoe {
+
+// router.cu -------------------------------------------------------------
+// topk_w_f32: fp32 copy of the routing weights (rounded to the layer dtype).
+cudaError_t launch_router_topk(const void* x, const void* w_router, const void* bias,
+                               int64_t T, int d, int E, int k, int dtype, int norm,
+                               int32_t* topk_idx, float* topk_w_f32, void* topk_w_dtype,
+                               void* logits_out, cudaStream_t stream);
+
+// dispatch.cu -----------------------------------------------------------
+// Tokens per histogram block for a given top_k.
+int dispatch_block_tokens(int k);
+int64_t dispatch_num_blocks(int64_t T, int k);
+
+// local_rank[T*k], block_counts[nblk*E] (turned into block offsets by scan).
+cudaError_t launch_hist_rank(const int32_t* topk_idx, int64_t T, int k, int E,
+                             int32_t* local_rank, int32_t* block_counts, int* err,
+                             cudaStream_t stream);
+// In place: block_counts -> absolute row offsets; counts[E], expert_offsets[E+1].
+cudaError_t launch_scan(int32_t* block_counts, int64_t nblk, int E, int32_t* counts,
+                        int32_t* expert_offsets, cudaStream_t stream);
+// pos[T*k] and (optionally) sort_idx, sorted_token, sorted weights, x_sorted.
+cudaError_t launch_permute_gather(const int32_t* topk_idx, const int32_t* local_rank,
+                                  const int32_t* block_offsets, const void* topk_w,
+                                  int topk_w_is_f32, const void* x, int64_t T, int d, int k,
+                                  int E, int dtype, int32_t* pos, int32_t* sort_idx,
+                                  int32_t* sorted_token, void* sorted_w, void* x_sorted,
+                                  cudaStream_t stream);
+// pos[sort_idx[p]] = p for p < n.
+cudaError_t launch_invert_perm(const int32_t* sort_idx, int64_t n, int32_t* pos,
+                               cudaStream_t stream);
+
+// combine.cu ------------------------------------------------------------
+cudaError_t launch_combine(const void* expert_out, const int32_t* pos, const void* topk_w,
+                           int topk_w_is_f32, const int32_t* topk_idx, int E, int64_t T,
+                           int d, int k, int dtype, const void* final_in, void* out,
+                           cudaStream_t stream);
+
+// gemm_sm100.cu (bf16, tcgen05) and gemm_simt.cu (fp32) ------------------
+struct GroupedGemmArgs {
+  const void* a;             // [M, K]
+  const void* b;             // [G, Nw, K]  (Nw = 2N for swiglu, N otherwise)
+  const int32_t* counts;     // [G] rows per group, device
+  void* out;                 // [M, N]
+  int64_t M;
+  int N;                     // output columns
+  int K;
+  int G;
+  int swiglu;                // fused silu(gate) * up epilogue
+  int dtype;
+  int* err;                  // device error word (may be null)
+  int sm_limit;              // persistent CTAs (0 = all SMs)
+};
+cudaError_t launch_grouped_gemm_sm100(const GroupedGemmArgs& args, cudaStream_t stream);
+cudaError_t launch_grouped_gemm_simt(const GroupedGemmArgs& args, cudaStream_t stream);
+
+// capi.cu ---------------------------------------------------------------
+int num_sms_for_current_device();
+
+}  // namespace hmoe

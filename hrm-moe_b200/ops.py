@@ -1,0 +1,300 @@
+"""Functional API on torch tensors, one function per reference operator.
+
+Each function mirrors a piece of XiaoYee/HRM-MoE's MoE path (argument
+meaning, dtypes, error types) and runs the matching C-ABI entry point on the
+current CUDA stream.  torch provides device memory and the stream only; all
+arithmetic runs in the native sm_100a kernels.  Scratch workspaces come from
+torch's caching allocator on the current stream.
+
+Errors follow the reference: ``ValueError`` for bad shapes
+(models/layers.py:531-539, models/moe_triton_grouped_gemm.py:367-368),
+``TypeError`` for an unsupported dtype (moe_triton_grouped_gemm.py:350-355),
+``RuntimeError`` when the backend cannot run.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional
+
+import torch
+
+from . import _lib
+
+_DTYPES = {torch.bfloat16: _lib.DTYPE_BF16, torch.float32: _lib.DTYPE_F32}
+
+
+def dtype_code(dtype: torch.dtype) -> int:
+    try:
+        return _DTYPES[dtype]
+    except KeyError:
+        raise TypeError(f"B200 MoE kernels support bf16 and fp32, got {dtype}") from None
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(device: torch.device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _require_cuda(*tensors: torch.Tensor) -> torch.device:
+    dev = None
+    for t in tensors:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise RuntimeError("B200 MoE kernels need CUDA tensors (there is no CPU path)")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise ValueError(f"tensors on different devices: {dev} and {t.device}")
+    return dev
+
+
+def _contig(t: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
+    return None if t is None else t.contiguous()
+
+
+def make_shape(tokens: int, hidden: int, experts: int, intermediate: int, top_k: int,
+               dtype: torch.dtype, norm_topk_prob: bool = True) -> _lib.HmoeShape:
+    return _lib.HmoeShape(int(tokens), int(hidden), int(experts), int(intermediate), int(top_k),
+                          dtype_code(dtype), 1 if norm_topk_prob else 0)
+
+
+def _workspace(nbytes: int, device: torch.device) -> torch.Tensor:
+    return torch.empty(max(int(nbytes), 1024), dtype=torch.uint8, device=device)
+
+
+# ------------------------------------------------------------------ router --
+def router_topk(x: torch.Tensor, w_router: torch.Tensor, top_k: int, norm_topk_prob: bool,
+                router_bias: Optional[torch.Tensor] = None, return_logits: bool = False):
+    """Router of SparseMoESwiGLU.forward (models/layers.py:604-610).
+
+    Returns (topk_idx int32 [T, k], topk_weight [T, k] in x.dtype) and, with
+    ``return_logits``, the rounded logits [T, E] in x.dtype.
+    """
+    dev = _require_cuda(x, w_router, router_bias)
+    T, d = x.shape
+    E = w_router.shape[0]
+    if w_router.shape[1] != d:
+        raise ValueError(f"router weight is {tuple(w_router.shape)}, hidden size is {d}")
+    shape = make_shape(T, d, E, 8, top_k, x.dtype, norm_topk_prob)
+    x, w_router, router_bias = _contig(x), _contig(w_router.to(x.dtype)), _contig(
+        None if router_bias is None else router_bias.to(x.dtype))
+    idx = torch.empty((T, top_k), dtype=torch.int32, device=dev)
+    w = torch.empty((T, top_k), dtype=x.dtype, device=dev)
+    logits = torch.empty((T, E), dtype=x.dtype, device=dev) if return_logits else None
+    lib = _lib.load()
+    _lib.check(lib.hmoe_router_topk(ctypes.byref(shape), _ptr(x), _ptr(w_router), _ptr(router_bias),
+                                    _ptr(idx), _ptr(w), _ptr(logits), _stream(dev)))
+    return (idx, w, logits) if return_logits else (idx, w)
+
+
+# ---------------------------------------------------------------- dispatch --
+def dispatch(topk_idx: torch.Tensor, num_experts: int, x: Optional[torch.Tensor] = None,
+             topk_weight: Optional[torch.Tensor] = None, gather: bool = True):
+    """Dispatch of SparseMoEGroupedExperts.forward (models/layers.py:311-322).
+
+    Returns a dict with ``sort_idx`` (int32 [T*k], the stable sort order of
+    the flattened assignments), ``counts`` (int32 [E]), ``sorted_token``
+    (int32 [T*k]) and, when given, ``sorted_weight`` and ``x_sorted``.
+    """
+    dev = _require_cuda(topk_idx, x, topk_weight)
+    T, k = topk_idx.shape
+    dtype = x.dtype if x is not None else (topk_weight.dtype if topk_weight is not None else torch.bfloat16)
+    d = x.shape[1] if x is not None else 8
+    shape = make_shape(T, d, num_experts, 8, k, dtype)
+    idx32 = topk_idx.to(torch.int32).contiguous()
+    out = {
+        "sort_idx": torch.empty(T * k, dtype=torch.int32, device=dev),
+        "counts": torch.zeros(num_experts, dtype=torch.int32, device=dev),
+        "sorted_token": torch.empty(T * k, dtype=torch.int32, device=dev),
+    }
+    if topk_weight is not None:
+        topk_weight = topk_weight.to(dtype).contiguous()
+        out["sorted_weight"] = torch.empty(T * k, dtype=dtype, device=dev)
+    if x is not None and gather:
+        x = x.contiguous()
+        out["x_sorted"] = torch.empty((T * k, d), dtype=dtype, device=dev)
+    lib = _lib.load()
+    ws_bytes = lib.hmoe_dispatch_workspace_bytes(ctypes.byref(shape))
+    if ws_bytes == 0:
+        raise ValueError(_lib.last_error())
+    ws = _workspace(ws_bytes, dev)
+    _lib.check(lib.hmoe_dispatch(ctypes.byref(shape), _ptr(idx32), _ptr(topk_weight), _ptr(x),
+                                 _ptr(out["sort_idx"]), _ptr(out["counts"]),
+                                 _ptr(out["sorted_token"]), _ptr(out.get("sorted_weight")),
+                                 _ptr(out.get("x_sorted")), _ptr(ws), ws.numel(), _stream(dev)))
+    return out
+
+
+# ------------------------------------------------------------ grouped GEMM --
+def _grouped(input: torch.Tensor, weight: torch.Tensor, tokens_per_expert: torch.Tensor,
+             swiglu: bool) -> torch.Tensor:
+    if input.shape[0] == 0:
+        n = weight.shape[1] // (2 if swiglu else 1)
+        return input.new_empty((0, n))
+    dev = _require_cuda(input, weight, tokens_per_expert)
+    M, K = input.shape
+    G, NW, WK = weight.shape
+    if WK != K:
+        raise ValueError(f"grouped GEMM K mismatch: input K={K}, weight K={WK}")
+    if tokens_per_expert.numel() != G:
+        raise ValueError(f"tokens_per_expert has {tokens_per_expert.numel()} entries, weight has {G} groups")
+    code = dtype_code(input.dtype)
+    if weight.dtype != input.dtype:
+        raise TypeError(f"input is {input.dtype} but weight is {weight.dtype}")
+    if swiglu and NW % 2:
+        raise ValueError("gate_up weight needs an even number of rows")
+    N = NW // 2 if swiglu else NW
+    input, weight = input.contiguous(), weight.contiguous()
+    tpe = tokens_per_expert.to(device=dev, dtype=torch.int32).contiguous()
+    out = torch.empty((M, N), dtype=input.dtype, device=dev)
+    lib = _lib.load()
+    ws = _workspace(lib.hmoe_grouped_linear_workspace_bytes(G), dev)
+    fn = lib.hmoe_grouped_swiglu if swiglu else lib.hmoe_grouped_linear
+    _lib.check(fn(_ptr(input), _ptr(weight), _ptr(tpe), M, N, K, G, code, _ptr(out), _ptr(ws),
+                  ws.numel(), _stream(dev)))
+    return out
+
+
+def grouped_linear(input: torch.Tensor, weight: torch.Tensor,
+                   tokens_per_expert: torch.Tensor) -> torch.Tensor:
+    """triton_grouped_linear (models/moe_triton_grouped_gemm.py:478-485).
+
+    input [M, K], weight [G, N, K], tokens_per_expert [G] (rows per group,
+    contiguous in order) -> [M, N].  Forward only.
+    """
+    return _grouped(input, weight, tokens_per_expert, swiglu=False)
+
+
+def grouped_swiglu(input: torch.Tensor, w_gate_up: torch.Tensor,
+                   tokens_per_expert: torch.Tensor) -> torch.Tensor:
+    """gate_up GEMM + silu(gate) * up fused (models/layers.py:326-329).
+
+    w_gate_up [G, 2I, K] -> [M, I].
+    """
+    return _grouped(input, w_gate_up, tokens_per_expert, swiglu=True)
+
+
+# ----------------------------------------------------------------- combine --
+def combine(expert_out: torch.Tensor, sort_idx: torch.Tensor, topk_weight: torch.Tensor,
+            final_hidden_states: torch.Tensor) -> torch.Tensor:
+    """Weighted combine (models/layers.py:332-334), in place on final_hidden_states."""
+    dev = _require_cuda(expert_out, sort_idx, topk_weight, final_hidden_states)
+    T, d = final_hidden_states.shape
+    k = topk_weight.shape[1]
+    if not final_hidden_states.is_contiguous():
+        raise ValueError("final_hidden_states must be contiguous (it is updated in place)")
+    shape = make_shape(T, d, max(k, 1), 8, k, final_hidden_states.dtype)
+    expert_out = expert_out.to(final_hidden_states.dtype).contiguous()
+    sort_idx = sort_idx.to(torch.int32).contiguous()
+    topk_weight = topk_weight.to(final_hidden_states.dtype).contiguous()
+    lib = _lib.load()
+    ws = _workspace(lib.hmoe_combine_workspace_bytes(ctypes.byref(shape)), dev)
+    _lib.check(lib.hmoe_combine(ctypes.byref(shape), _ptr(expert_out), _ptr(sort_idx),
+                                _ptr(topk_weight), _ptr(final_hidden_states), _ptr(ws), ws.numel(),
+                                _stream(dev)))
+    return final_hidden_states
+
+
+# ----------------------------------------------------------------- experts --
+def experts_forward(hidden_states: torch.Tensor, selected_experts: torch.Tensor,
+                    routing_weights: torch.Tensor, final_hidden_states: torch.Tensor,
+                    w_gate_up: torch.Tensor, w_down: torch.Tensor,
+                    counts_out: Optional[torch.Tensor] = None,
+                    sort_idx_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """SparseMoEGroupedExperts.forward (models/layers.py:285-335).
+
+    Adds the routed experts' output into ``final_hidden_states`` in place and
+    returns it.  selected_experts [T, k] (any integer dtype), routing_weights
+    [T, k], w_gate_up [E, 2I, d], w_down [E, d, I].
+    """
+    T = hidden_states.shape[0]
+    if T == 0:
+        return final_hidden_states
+    dev = _require_cuda(hidden_states, selected_experts, routing_weights, final_hidden_states,
+                        w_gate_up, w_down)
+    d = hidden_states.shape[1]
+    E, two_i, wd = w_gate_up.shape
+    I = two_i // 2
+    k = selected_experts.shape[-1]
+    if wd != d or tuple(w_down.shape) != (E, d, I):
+        raise ValueError(f"expert weights {tuple(w_gate_up.shape)} / {tuple(w_down.shape)} do not "
+                         f"match hidden size {d}")
+    if not final_hidden_states.is_contiguous():
+        raise ValueError("final_hidden_states must be contiguous (it is updated in place)")
+    dt = hidden_states.dtype
+    shape = make_shape(T, d, E, I, k, dt)
+    hs = hidden_states.contiguous()
+    idx = selected_experts.reshape(T, k).to(torch.int32).contiguous()
+    rw = routing_weights.reshape(T, k).to(dt).contiguous()
+    w_gate_up, w_down = w_gate_up.to(dt).contiguous(), w_down.to(dt).contiguous()
+    lib = _lib.load()
+    ws_bytes = lib.hmoe_experts_workspace_bytes(ctypes.byref(shape))
+    if ws_bytes == 0:
+        raise ValueError(_lib.last_error())
+    ws = _workspace(ws_bytes, dev)
+    _lib.check(lib.hmoe_experts_forward(ctypes.byref(shape), _ptr(hs), _ptr(idx), _ptr(rw),
+                                        _ptr(w_gate_up), _ptr(w_down), _ptr(final_hidden_states),
+                                        _ptr(counts_out), _ptr(sort_idx_out), _ptr(ws), ws.numel(),
+                                        _stream(dev)))
+    return final_hidden_states
+
+
+# ------------------------------------------------------------------- layer --
+def ffn_forward(x: torch.Tensor, w_router: torch.Tensor, w_gate_up: torch.Tensor,
+                w_down: torch.Tensor, top_k: int, norm_topk_prob: bool,
+                router_bias: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+                accumulate: bool = False, return_routing: bool = False):
+    """SparseMoESwiGLU.forward on a flat [T, d] input (models/layers.py:596-634).
+
+    Returns y [T, d] and, with ``return_routing``, a dict with ``topk_idx``
+    (int32 [T, k]), ``topk_weight`` ([T, k]), ``counts`` (int32 [E]) and
+    ``sort_idx`` (int32 [T*k]).
+    """
+    T, d = x.shape
+    dt = x.dtype
+    code = dtype_code(dt)
+    E = w_router.shape[0]
+    I = w_gate_up.shape[1] // 2
+    if tuple(w_gate_up.shape) != (E, 2 * I, d) or tuple(w_down.shape) != (E, d, I):
+        raise ValueError(f"expert weights {tuple(w_gate_up.shape)} / {tuple(w_down.shape)} do not "
+                         f"match hidden size {d} and {E} experts")
+    if out is None:
+        out = (torch.zeros if accumulate else torch.empty)((T, d), dtype=dt, device=x.device)
+    routing = None
+    if T == 0:
+        return (out, routing) if return_routing else out
+    dev = _require_cuda(x, w_router, w_gate_up, w_down, router_bias, out)
+    shape = _lib.HmoeShape(T, d, E, I, top_k, code, 1 if norm_topk_prob else 0)
+    x = x.contiguous()
+    w_router = w_router.to(dt).contiguous()
+    w_gate_up = w_gate_up.to(dt).contiguous()
+    w_down = w_down.to(dt).contiguous()
+    bias = None if router_bias is None else router_bias.to(dt).contiguous()
+    if return_routing:
+        routing = {
+            "topk_idx": torch.empty((T, top_k), dtype=torch.int32, device=dev),
+            "topk_weight": torch.empty((T, top_k), dtype=dt, device=dev),
+            "counts": torch.empty(E, dtype=torch.int32, device=dev),
+            "sort_idx": torch.empty(T * top_k, dtype=torch.int32, device=dev),
+        }
+    r = routing or {}
+    lib = _lib.load()
+    ws_bytes = lib.hmoe_ffn_workspace_bytes(ctypes.byref(shape))
+    if ws_bytes == 0:
+        raise ValueError(_lib.last_error())
+    ws = _workspace(ws_bytes, dev)
+    _lib.check(lib.hmoe_ffn_forward(
+        ctypes.byref(shape), _ptr(x), _ptr(w_router), _ptr(bias), _ptr(w_gate_up), _ptr(w_down),
+        _ptr(out), 1 if accumulate else 0, _ptr(r.get("topk_idx")), _ptr(r.get("topk_weight")),
+        _ptr(r.get("counts")), _ptr(r.get("sort_idx")), _ptr(ws), ws.numel(), _stream(dev)))
+    return (out, routing) if return_routing else out
+
+
+def workspace_status(workspace: torch.Tensor) -> None:
+    """Raise if kernels flagged an error in ``workspace`` (synchronises)."""
+    lib = _lib.load()
+    _lib.check(lib.hmoe_workspace_status(_ptr(workspace), _stream(workspace.device)))

@@ -1,0 +1,177 @@
+/*
+ * hrm_moe.h -- C ABI of the B200-native routed MoE-FFN forward.
+ *
+ * Drop-in for the grouped expert path of XiaoYee/HRM-MoE
+ * (models/layers.py SparseMoESwiGLU / SparseMoEGroupedExperts and
+ * models/moe_triton_grouped_gemm.py triton_grouped_linear).  Every entry
+ * point takes plain device pointers and sizes, runs stream-ordered on the
+ * given cudaStream_t (passed as void*; NULL = legacy default stream) and
+ * never synchronises the host.  Buffers are owned by the caller.  Scratch
+ * memory comes from a caller-owned workspace whose size the matching
+ * *_workspace_bytes() function returns; one call may be in flight per
+ * workspace at a time.
+ *
+ * Layouts (row-major, contiguous):
+ *   x           [T, d]       hidden states, layer dtype
+ *   w_router    [E, d]       gate.weight            (layers.py:548)
+ *   router_bias [E]          gate.bias or NULL, layer dtype
+ *   w_gate_up   [E, 2I, d]   experts.gate_up_weight (layers.py:272-277);
+ *                            rows 0..I-1 gate, I..2I-1 up (layers.py:328)
+ *   w_down      [E, d, I]    experts.down_weight    (layers.py:278-283)
+ *   topk_idx    [T, k]       int32 expert ids
+ *   topk_weight [T, k]       layer dtype
+ *   counts      [E]          int32 tokens_per_expert
+ *   sort_idx    [T*k]        int32; position p holds the flat index t*k+j of
+ *                            the p-th assignment in stable expert order
+ *                            (torch.sort(flat, stable=True), layers.py:317)
+ *
+ * Status codes are errno values; hmoe_last_error() describes the last
+ * failure on the calling thread.
+ */
+#ifndef HRM_MOE_H
+#define HRM_MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define HMOE_OK 0
+#define HMOE_EIO 5          /* CUDA runtime error */
+#define HMOE_EINVAL 22      /* bad shape, dtype or pointer */
+#define HMOE_ENOSPC 28      /* workspace too small */
+#define HMOE_ENOSYS 38      /* device is not an sm_100 GPU */
+#define HMOE_ETIMEDOUT 110  /* a bounded device-side wait gave up */
+
+#define HMOE_DTYPE_BF16 0
+#define HMOE_DTYPE_F32 1
+
+typedef struct hmoe_shape {
+  int64_t tokens;          /* T */
+  int32_t hidden;          /* d, multiple of 8 */
+  int32_t experts;         /* E, 1..128 */
+  int32_t intermediate;    /* I, multiple of 8 */
+  int32_t top_k;           /* k, 1..min(E, 32) */
+  int32_t dtype;           /* HMOE_DTYPE_* : hidden / weight / output dtype */
+  int32_t norm_topk_prob;  /* renormalise the top-k probabilities */
+} hmoe_shape;
+
+/* Library identification, and the message of the last failing call. */
+const char* hmoe_version(void);
+const char* hmoe_last_error(void);
+
+/*
+ * Whole layer: SparseMoESwiGLU.forward (models/layers.py:596-634) without
+ * the training-only aux-loss block (layers.py:619-632).
+ *   y = [y +] sum_j w[t,j] * SwiGLU_{idx[t,j]}(x[t])
+ * accumulate = 0 writes y; 1 adds into it (the reference adds into a zeros
+ * accumulator, layers.py:612-617).  topk_idx / topk_weight / counts /
+ * sort_idx are optional outputs (NULL = not written).
+ */
+size_t hmoe_ffn_workspace_bytes(const hmoe_shape* shape);
+int hmoe_ffn_forward(const hmoe_shape* shape, const void* x, const void* w_router,
+                     const void* router_bias, const void* w_gate_up, const void* w_down,
+                     void* y, int accumulate, int32_t* topk_idx, void* topk_weight,
+                     int32_t* counts, int32_t* sort_idx, void* workspace,
+                     size_t workspace_bytes, void* stream);
+
+/*
+ * hmoe_ffn_forward with timing marks: phase_events points to 6 cudaEvent_t
+ * (NULL entries skipped) recorded on the stream before the router, after
+ * the router, after dispatch, after the gate_up GEMM, after the down GEMM
+ * and after the combine.  Same kernels, same results.
+ */
+int hmoe_ffn_forward_marked(const hmoe_shape* shape, const void* x, const void* w_router,
+                            const void* router_bias, const void* w_gate_up, const void* w_down,
+                            void* y, int accumulate, void* workspace, size_t workspace_bytes,
+                            void* stream, void* const* phase_events);
+
+/*
+ * Router: self.gate + fp32 softmax + top-k + renormalise + cast
+ * (models/layers.py:604-610).  Logits are accumulated in fp32 in a fixed
+ * order (one fma per k, ascending) and rounded to the layer dtype as the
+ * reference's F.linear output is; selection takes the k largest logits,
+ * equal logits going to the lower expert index.  logits (optional, [T, E],
+ * layer dtype) returns the rounded logits.  No workspace.
+ */
+int hmoe_router_topk(const hmoe_shape* shape, const void* x, const void* w_router,
+                     const void* router_bias, int32_t* topk_idx, void* topk_weight,
+                     void* logits, void* stream);
+
+/*
+ * Dispatch: flatten, stable sort by expert, gather rows, count
+ * (models/layers.py:311-322).  Writes sort_idx [T*k], counts [E] and, when
+ * non-NULL, sorted_token [T*k] (int32), sorted_weight [T*k] (layer dtype)
+ * and x_sorted [T*k, d].  Deterministic, no atomics on positions.
+ */
+size_t hmoe_dispatch_workspace_bytes(const hmoe_shape* shape);
+int hmoe_dispatch(const hmoe_shape* shape, const int32_t* topk_idx,
+                  const void* topk_weight, const void* x, int32_t* sort_idx,
+                  int32_t* counts, int32_t* sorted_token, void* sorted_weight,
+                  void* x_sorted, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Experts: SparseMoEGroupedExperts.forward (models/layers.py:285-335) --
+ * dispatch, gate_up GEMM + SiLU(gate)*up, down GEMM, weighted combine into
+ * final_hidden_states (accumulated in place, like the reference's
+ * index_add_).  topk_idx is int32 here; ids outside [0, E) are dropped.
+ */
+size_t hmoe_experts_workspace_bytes(const hmoe_shape* shape);
+int hmoe_experts_forward(const hmoe_shape* shape, const void* hidden,
+                         const int32_t* topk_idx, const void* topk_weight,
+                         const void* w_gate_up, const void* w_down,
+                         void* final_hidden_states, int32_t* counts, int32_t* sort_idx,
+                         void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Grouped GEMM: triton_grouped_linear(input, weight, tokens_per_expert)
+ * (models/moe_triton_grouped_gemm.py:478-485, kernel :113-184):
+ *   output[rows of group g] = input[rows of group g] @ weight[g]^T
+ * input [M, K], weight [G, N, K], output [M, N], tokens_per_expert [G]
+ * int32 on the device, groups contiguous in row order.  bf16 runs on the
+ * tcgen05 tensor cores, fp32 on CUDA cores.  K and N multiples of 8.
+ */
+size_t hmoe_grouped_linear_workspace_bytes(int32_t groups);
+int hmoe_grouped_linear(const void* input, const void* weight,
+                        const int32_t* tokens_per_expert, int64_t M, int32_t N,
+                        int32_t K, int32_t groups, int32_t dtype, void* output,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Fused gate_up GEMM + activation (models/layers.py:326-329):
+ *   gate_up = grouped_linear(input, w_gate_up, tokens_per_expert)  [M, 2I]
+ *   output  = silu(gate_up[:, :I]) * gate_up[:, I:]                 [M, I]
+ * with the bf16 roundings of the reference's intermediate tensors applied
+ * in the epilogue.  w_gate_up [G, 2I, K].
+ */
+int hmoe_grouped_swiglu(const void* input, const void* w_gate_up,
+                        const int32_t* tokens_per_expert, int64_t M, int32_t I,
+                        int32_t K, int32_t groups, int32_t dtype, void* output,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Combine (models/layers.py:332-334): for every token t,
+ *   final[t] += sum_j topk_weight[t, j] * expert_out[pos(t, j)]
+ * where pos is the inverse of sort_idx (sort_idx[pos(t,j)] = t*k + j).
+ * Accumulates in fp32 and rounds once per output element.
+ */
+size_t hmoe_combine_workspace_bytes(const hmoe_shape* shape);
+int hmoe_combine(const hmoe_shape* shape, const void* expert_out, const int32_t* sort_idx,
+                 const void* topk_weight, void* final_hidden_states, void* workspace,
+                 size_t workspace_bytes, void* stream);
+
+/*
+ * Read (and synchronise the stream for) the error word kernels leave at the
+ * start of a workspace used by hmoe_ffn_forward, hmoe_experts_forward,
+ * hmoe_dispatch or hmoe_grouped_*: HMOE_OK, HMOE_EINVAL (an expert id was
+ * outside [0, E) and was dropped) or HMOE_ETIMEDOUT.  Not for hot loops.
+ */
+int hmoe_workspace_status(const void* workspace, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HRM_MOE_H */

@@ -1,0 +1,91 @@
+"""Router kernel vs the oracle (bit-exact) and vs the reference (tie-aware)."""
+import numpy as np
+import pytest
+
+from _helpers import golden_names, load_golden, routing_agrees, synthetic
+from gpu_util import get_ops, to_dev, to_np
+from oracle import moe_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def _run(x, w, bias, k, norm, dtype):
+    ops = get_ops()
+    bt = None if bias is None else to_dev(bias, dtype)
+    idx, wt, logits = ops.router_topk(to_dev(x, dtype), to_dev(w, dtype), k, norm, bt,
+                                      return_logits=True)
+    return to_np(idx).astype(np.int64), to_np(wt), to_np(logits)
+
+
+def _check_against_oracle(x, w, bias, k, norm, dtype):
+    idx, wt, logits = _run(x, w, bias, k, norm, dtype)
+    ol = O.router_logits(x, w, bias, dtype)
+    # same fma order, same rounding: identical bits (including -inf)
+    assert np.array_equal(logits, ol)
+    oidx, ow, _ = O.route(ol, k, norm, dtype)
+    assert np.array_equal(idx, oidx)
+    if dtype == "bf16":
+        np.testing.assert_allclose(wt, ow, rtol=2 ** -8, atol=0)
+    else:
+        np.testing.assert_allclose(wt, ow, rtol=2e-6, atol=1e-7)
+    return idx, wt, logits
+
+
+@pytest.mark.parametrize("name", golden_names())
+def test_router_golden(name):
+    inp, ref, meta = load_golden(name)
+    k = meta["k"]
+    idx, _, logits = _check_against_oracle(inp.x, inp.w_router, inp.router_bias, k, meta["norm"],
+                                           meta["dtype"])
+    exact, tie_only, real = routing_agrees(idx, logits, ref["topk_idx"], ref["logits"], k)
+    if meta["dtype"] == "bf16":
+        assert not real.any()
+    else:
+        # fp32 logits differ from BLAS in the last bits; a real mismatch may
+        # only happen where the k-th and (k+1)-th logits are that close
+        near = O.boundary_tie_rows(ref["logits"], k, rel=1e-5)
+        assert not (real & ~near).any()
+
+
+@pytest.mark.parametrize("T,d,E,k,dtype,seed", [
+    (1, 1536, 64, 8, "bf16", 1),
+    (63, 1536, 64, 8, "bf16", 2),
+    (65, 1280, 64, 8, "f32", 3),
+    (4096, 1536, 64, 8, "bf16", 4),
+    (2048, 1280, 64, 8, "f32", 0),
+    (1024, 1536, 128, 8, "bf16", 5),
+    (300, 40, 8, 3, "bf16", 6),
+    (77, 16, 5, 5, "f32", 7),
+    (129, 256, 100, 32, "bf16", 8),
+])
+def test_router_seeded(T, d, E, k, dtype, seed):
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((T, d), dtype=np.float32)
+    w = (rng.standard_normal((E, d), dtype=np.float32) * np.float32(0.02))
+    if dtype == "bf16":
+        x, w = O.round_to_bf16(x), O.round_to_bf16(w)
+    _check_against_oracle(x, w, None, k, True, dtype)
+
+
+def test_router_norm_false_and_bias():
+    rng = np.random.default_rng(11)
+    x = O.round_to_bf16(rng.standard_normal((500, 256), dtype=np.float32))
+    w = O.round_to_bf16(rng.standard_normal((64, 256), dtype=np.float32) * np.float32(0.02))
+    bias = O.round_to_bf16(synthetic().zipf_router_bias(64, 3, dead_experts=4))
+    idx, _, _ = _check_against_oracle(x, w, bias, 8, False, "bf16")
+    dead = np.nonzero(np.isinf(bias))[0]
+    assert not np.isin(idx, dead).any()
+
+
+def test_router_exact_ties_go_to_lower_index():
+    rng = np.random.default_rng(12)
+    x = O.round_to_bf16(rng.standard_normal((256, 64), dtype=np.float32))
+    w = O.round_to_bf16(rng.standard_normal((16, 64), dtype=np.float32) * np.float32(0.02))
+    w[7] = w[2]
+    w[9] = w[4]
+    w[15] = w[0]
+    idx, _, logits = _check_against_oracle(x, w, None, 4, True, "bf16")
+    vals = np.take_along_axis(logits, idx, axis=1)
+    eq = np.diff(vals, axis=1) == 0
+    assert eq.any()
+    assert (np.diff(idx, axis=1)[eq] > 0).all()
