@@ -1,13 +1,15 @@
 // Combine: weighted sum of each token's k expert outputs, back in token order.
 //
 // Mirrors models/layers.py:332-334 of HRM-MoE:
-//   expert_output = expert_output * sorted_weights[:, None]
+//   expert_output = expert_output * sorted_weights[:, None]      # layer dtype
 //   final_hidden_states.index_add_(0, sorted_token_idx, expert_output)
 // as a gather instead of a scatter: one warp per token reads the k rows
-// pos(t, 0..k-1) of the expert-sorted output, accumulates w_j * row_j in
-// fp32 (j ascending) on top of the existing accumulator and rounds once.
-// No atomics, so the result is deterministic (the reference's CUDA
-// index_add_ is not).
+// pos(t, 0..k-1) of the expert-sorted output.  The arithmetic follows the
+// reference step by step: each product w * y is rounded to the layer dtype,
+// and the products are added into the accumulator one at a time, each sum
+// rounded, in ascending sorted position -- the order index_add_ visits a
+// token's rows (ascending expert id, the stable sort order).  No atomics, so
+// the result is deterministic (the reference's CUDA index_add_ is not).
 #include "common.cuh"
 #include "internal.h"
 
@@ -16,6 +18,11 @@ namespace {
 
 constexpr int kCombThreads = 256;
 constexpr int kMaxK = 32;
+
+template <bool BF16>
+__device__ __forceinline__ float round_dt(float v) {
+  return BF16 ? round_bf16(v) : v;
+}
 
 template <bool BF16>
 __global__ void __launch_bounds__(kCombThreads)
@@ -35,6 +42,20 @@ combine_kernel(const void* __restrict__ expert_out, const int32_t* __restrict__ 
       w = BF16 ? bf16_bits_to_f32(static_cast<const uint16_t*>(topk_w)[t * k + lane])
                : static_cast<const float*>(topk_w)[t * k + lane];
   }
+  // visit the token's assignments in ascending position: lane of rank r
+  const unsigned live_k = __ballot_sync(0xffffffffu, lane < k && p >= 0);
+  int rank = 0;
+  for (int j = 0; j < k; ++j) {
+    const int pj = __shfl_sync(0xffffffffu, p, j);
+    if (((live_k >> j) & 1u) && pj < p) ++rank;
+  }
+  const int nlive = __popc(live_k);
+  int src_of_rank = 0;  // lane r holds the source lane of rank r
+  for (int r = 0; r < nlive; ++r) {
+    const unsigned m = __ballot_sync(0xffffffffu, ((live_k >> lane) & 1u) && rank == r);
+    if (lane == r) src_of_rank = __ffs(m) - 1;
+  }
+
   const uint4* src = static_cast<const uint4*>(expert_out);
   const uint4* fin = static_cast<const uint4*>(final_in);
   uint4* dst = static_cast<uint4*>(out);
@@ -58,23 +79,26 @@ combine_kernel(const void* __restrict__ expert_out, const int32_t* __restrict__ 
 #pragma unroll
       for (int i = 0; i < EPC; ++i) acc[i] = 0.0f;
     }
-    for (int j = 0; j < k; ++j) {
-      const int pj = __shfl_sync(0xffffffffu, p, j);
-      const float wj = __shfl_sync(0xffffffffu, w, j);
-      if (pj < 0 || !live) continue;
+    for (int r = 0; r < nlive; ++r) {
+      const int sl = __shfl_sync(0xffffffffu, src_of_rank, r);
+      const int pj = __shfl_sync(0xffffffffu, p, sl);
+      const float wj = __shfl_sync(0xffffffffu, w, sl);
+      if (!live) continue;
       const uint4 u = __ldg(src + static_cast<int64_t>(pj) * row_chunks + c);
+      float y[EPC];
       if (BF16) {
         const uint32_t q[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          acc[2 * i] = fmaf(wj, bf16_lo(q[i]), acc[2 * i]);
-          acc[2 * i + 1] = fmaf(wj, bf16_hi(q[i]), acc[2 * i + 1]);
-        }
+        for (int i = 0; i < 4; ++i) { y[2 * i] = bf16_lo(q[i]); y[2 * i + 1] = bf16_hi(q[i]); }
       } else {
-        acc[0] = fmaf(wj, __uint_as_float(u.x), acc[0]);
-        acc[1] = fmaf(wj, __uint_as_float(u.y), acc[1]);
-        acc[2] = fmaf(wj, __uint_as_float(u.z), acc[2]);
-        acc[3] = fmaf(wj, __uint_as_float(u.w), acc[3]);
+        y[0] = __uint_as_float(u.x); y[1] = __uint_as_float(u.y);
+        y[2] = __uint_as_float(u.z); y[3] = __uint_as_float(u.w);
+      }
+#pragma unroll
+      for (int i = 0; i < EPC; ++i) {
+        // two separate roundings, as the reference's mul then add (no fma)
+        const float prod = round_dt<BF16>(__fmul_rn(y[i], wj));
+        acc[i] = round_dt<BF16>(__fadd_rn(acc[i], prod));
       }
     }
     uint4 o;

@@ -126,11 +126,12 @@ class SparseMoESwiGLU(nn.Module):
         _check_no_grad(x, self.gate.weight, self.gate.bias, self.experts.gate_up_weight,
                        self.experts.down_weight)
         want_counts = moe_context is not None
-        y, routing = ops.ffn_forward(
+        res = ops.ffn_forward(
             hidden_states, self.gate.weight, self.experts.gate_up_weight,
             self.experts.down_weight, self.top_k, self.norm_topk_prob,
             router_bias=self.gate.bias, return_routing=want_counts)
-        if want_counts and routing is not None:
+        y, routing = res if want_counts else (res, None)
+        if routing is not None:
             # the reference records aux losses only when gradients flow
             # (layers.py:619); without them it keeps nothing, and the expert
             # counts are exposed here for monitoring

@@ -57,9 +57,15 @@ def test_grouped_swiglu_bf16(M, N, K, G, zeros):
     gu = O.round_to_bf16(to_np(_ref_grouped(a, b, counts)))
     gate, up = gu[:, :N], gu[:, N:]
     ref = O.round_to_bf16(O.round_to_bf16(O.silu_f32(gate)) * up)
-    # the reference rounds gate_up to bf16 first: allow one-ulp flips of gate_up
-    assert bf16_close(out, ref, rel=2.0 ** -7)
-    assert np.mean(out == ref) > 0.95
+    # gate_up is rounded to bf16 before the activation (as in the reference);
+    # where the fp32 sums of the two sides straddle a bf16 rounding midpoint
+    # the inputs differ by one ulp, which the three roundings can grow to a
+    # few ulps of h.  Everything else must match bit for bit.
+    diff = np.abs(out - ref)
+    tol = 2.0 ** -6 * np.abs(ref) + 2.0 ** -10 * np.abs(ref).max()
+    exact = np.mean(out == ref)
+    assert (diff <= tol).all(), (diff.max(), (diff > tol).sum(), exact)
+    assert exact > 0.97, exact
 
 
 @pytest.mark.parametrize("M,N,K,G,zeros", [(300, 512, 128, 3, 1), (2000, 448, 1280, 64, 3),
