@@ -74,6 +74,8 @@ SIGNATURES = {
     "hmoe_combine": (c_int, [ShapeP, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                              c_size_t, c_void_p]),
     "hmoe_workspace_status": (c_int, [c_void_p, c_void_p]),
+    "hmoe_dispatch_noalloc": (c_int, [ShapeP, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                      c_void_p, c_void_p, c_void_p, c_void_p]),
 }
 
 _lib = None

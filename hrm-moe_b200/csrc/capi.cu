@@ -263,6 +263,19 @@ int ffn_forward_impl(const hmoe_shape* shape, const void* x, const void* w_route
 }  // namespace
 
 namespace hmoe {
+int report_error(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  return fail(code, "%s", buf);
+}
+
+int make_device_current(const void* ptr) { return select_device(ptr); }
+
+int validate_shape_public(const hmoe_shape* shape) { return validate_shape(shape); }
+
 int num_sms_for_current_device() {
   static int sms[64] = {0};
   int dev = 0;

@@ -5,6 +5,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+struct hmoe_shape;  // include/hrm_moe.h
+
 namespace hmoe {
 
 // router.cu -------------------------------------------------------------
@@ -63,5 +65,11 @@ cudaError_t launch_grouped_gemm_simt(const GroupedGemmArgs& args, cudaStream_t s
 
 // capi.cu ---------------------------------------------------------------
 int num_sms_for_current_device();
+// Entry-point plumbing for files other than capi.cu: set hmoe_last_error()
+// and return `code`; make the device owning `ptr` current (sm_100 only);
+// validate a shape.
+int report_error(int code, const char* fmt, ...);
+int make_device_current(const void* ptr);
+int validate_shape_public(const ::hmoe_shape* shape);
 
 }  // namespace hmoe

@@ -163,6 +163,26 @@ int hmoe_combine(const hmoe_shape* shape, const void* expert_out, const int32_t*
                  size_t workspace_bytes, void* stream);
 
 /*
+ * hmoe_dispatch without a workspace.  No counterpart in the reference: it
+ * exists for hosts that cannot give this library device memory for scratch
+ * (a plugin host with no CUDA allocator binding, a process whose device
+ * memory another framework has reserved up front, a serving loop that must
+ * not allocate after start-up).  Same inputs, outputs and results as
+ * hmoe_dispatch; the scratch lives in one fixed __device__ array of about
+ * 2.3 MiB that every GPU loading the library keeps until exit.  At most
+ * HMOE_DISPATCH_NOALLOC_MAX_ASSIGNMENTS assignments (tokens * top_k) per
+ * call; larger calls fail with HMOE_EINVAL.  The first call on a device
+ * looks up the array's device address (make it before any stream capture).
+ * Calls share the array: two calls that overlap on the GPU race.  Expert ids
+ * outside [0, E) are dropped without an error report.  Allocates nothing.
+ */
+#define HMOE_DISPATCH_NOALLOC_MAX_ASSIGNMENTS 262144
+int hmoe_dispatch_noalloc(const hmoe_shape* shape, const int32_t* topk_idx,
+                          const void* topk_weight, const void* x, int32_t* sort_idx,
+                          int32_t* counts, int32_t* sorted_token, void* sorted_weight,
+                          void* x_sorted, void* stream);
+
+/*
  * Read (and synchronise the stream for) the error word kernels leave at the
  * start of a workspace used by hmoe_ffn_forward, hmoe_experts_forward,
  * hmoe_dispatch or hmoe_grouped_*: HMOE_OK, HMOE_EINVAL (an expert id was
