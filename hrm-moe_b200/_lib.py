@@ -57,8 +57,9 @@ SIGNATURES = {
     "hmoe_ffn_forward_marked": (c_int, [ShapeP, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                         c_void_p, c_int, c_void_p, c_size_t, c_void_p,
                                         ctypes.POINTER(c_void_p)]),
+    "hmoe_router_workspace_bytes": (c_size_t, [ShapeP]),
     "hmoe_router_topk": (c_int, [ShapeP, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
-                                 c_void_p, c_void_p]),
+                                 c_void_p, c_void_p, c_size_t, c_void_p]),
     "hmoe_dispatch_workspace_bytes": (c_size_t, [ShapeP]),
     "hmoe_dispatch": (c_int, [ShapeP, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                               c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),

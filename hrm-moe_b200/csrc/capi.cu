@@ -148,6 +148,7 @@ struct FfnBufs {
   ExpertBufs x;
   int32_t* topk_idx;
   float* topk_w;
+  void* router_scratch;  // fix-up list of the tensor-core router
 };
 
 FfnBufs carve_ffn(Carve& c, const hmoe_shape& s) {
@@ -156,7 +157,19 @@ FfnBufs carve_ffn(Carve& c, const hmoe_shape& s) {
   b.x = carve_experts(c, s);
   b.topk_idx = c.take<int32_t>(sizeof(int32_t) * A);
   b.topk_w = c.take<float>(sizeof(float) * A);
+  b.router_scratch = c.take<void>(router_tc_scratch_bytes(s.tokens));
   return b;
+}
+
+// Router stage: tensor cores with exact-order fix-up for bf16, CUDA cores for fp32.
+cudaError_t run_router(const hmoe_shape& s, const void* x, const void* w_router, const void* bias,
+                       int32_t* idx, float* w_f32, void* w_dtype, void* logits, void* scratch,
+                       int* err, cudaStream_t st) {
+  if (s.dtype == kDtypeBF16)
+    return launch_router_topk_tc(x, w_router, bias, s.tokens, s.hidden, s.experts, s.top_k,
+                                 s.norm_topk_prob, idx, w_f32, w_dtype, logits, scratch, err, st);
+  return launch_router_topk(x, w_router, bias, s.tokens, s.hidden, s.experts, s.top_k, s.dtype,
+                            s.norm_topk_prob, idx, w_f32, w_dtype, logits, st);
 }
 
 template <class F>
@@ -346,8 +359,8 @@ int ffn_forward_impl(const hmoe_shape* shape, const void* x, const void* w_route
   int32_t* idx = topk_idx ? topk_idx : b.topk_idx;
   HMOE_CUDA(cudaMemsetAsync(b.x.d.err, 0, sizeof(int), st), "reset error word");
   if ((rc = pm.mark(0, st))) return rc;
-  HMOE_CUDA(launch_router_topk(x, w_router, router_bias, s.tokens, s.hidden, s.experts, s.top_k,
-                               s.dtype, s.norm_topk_prob, idx, b.topk_w, topk_weight, nullptr, st),
+  HMOE_CUDA(run_router(s, x, w_router, router_bias, idx, b.topk_w, topk_weight, nullptr,
+                       b.router_scratch, b.x.d.err, st),
             "router_topk");
   if ((rc = pm.mark(1, st))) return rc;
   return run_experts(s, x, idx, b.topk_w, 1, w_gate_up, w_down, accumulate ? y : nullptr, y,
@@ -357,9 +370,16 @@ int ffn_forward_impl(const hmoe_shape* shape, const void* x, const void* w_route
 
 extern "C" {
 
+size_t hmoe_router_workspace_bytes(const hmoe_shape* shape) {
+  return plan_bytes(shape, [](Carve& c, const hmoe_shape& s) {
+    c.take<int>(sizeof(int));  // error word
+    c.take<void>(router_tc_scratch_bytes(s.tokens));
+  });
+}
+
 int hmoe_router_topk(const hmoe_shape* shape, const void* x, const void* w_router,
                      const void* router_bias, int32_t* topk_idx, void* topk_weight, void* logits,
-                     void* stream) {
+                     void* workspace, size_t workspace_bytes, void* stream) {
   int rc = validate_shape(shape);
   if (rc) return rc;
   const hmoe_shape& s = *shape;
@@ -367,9 +387,14 @@ int hmoe_router_topk(const hmoe_shape* shape, const void* x, const void* w_route
   if (!x || !w_router || !topk_idx) return fail(HMOE_EINVAL, "x, w_router and topk_idx are required");
   if (!aligned16(x) || !aligned16(w_router)) return fail(HMOE_EINVAL, "x and w_router must be 16-byte aligned");
   if ((rc = select_device(x))) return rc;
-  HMOE_CUDA(launch_router_topk(x, w_router, router_bias, s.tokens, s.hidden, s.experts, s.top_k,
-                               s.dtype, s.norm_topk_prob, topk_idx, nullptr, topk_weight, logits,
-                               static_cast<cudaStream_t>(stream)),
+  if ((rc = check_ws(workspace, workspace_bytes, hmoe_router_workspace_bytes(shape)))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Carve c{static_cast<char*>(workspace)};
+  int* err = c.take<int>(sizeof(int));
+  void* scratch = c.take<void>(router_tc_scratch_bytes(s.tokens));
+  HMOE_CUDA(cudaMemsetAsync(err, 0, sizeof(int), st), "reset error word");
+  HMOE_CUDA(run_router(s, x, w_router, router_bias, topk_idx, nullptr, topk_weight, logits, scratch,
+                       err, st),
             "router_topk");
   return HMOE_OK;
 }

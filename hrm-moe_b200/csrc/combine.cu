@@ -20,11 +20,6 @@ constexpr int kCombThreads = 256;
 constexpr int kMaxK = 32;
 
 template <bool BF16>
-__device__ __forceinline__ float round_dt(float v) {
-  return BF16 ? round_bf16(v) : v;
-}
-
-template <bool BF16>
 __global__ void __launch_bounds__(kCombThreads)
 combine_kernel(const void* __restrict__ expert_out, const int32_t* __restrict__ pos,
                const void* __restrict__ topk_w, int topk_w_is_f32, int64_t T, int row_chunks,
@@ -42,7 +37,8 @@ combine_kernel(const void* __restrict__ expert_out, const int32_t* __restrict__ 
       w = BF16 ? bf16_bits_to_f32(static_cast<const uint16_t*>(topk_w)[t * k + lane])
                : static_cast<const float*>(topk_w)[t * k + lane];
   }
-  // visit the token's assignments in ascending position: lane of rank r
+  // visit the token's assignments in ascending position: lane r ends up
+  // holding the (position, weight) of the r-th assignment in that order
   const unsigned live_k = __ballot_sync(0xffffffffu, lane < k && p >= 0);
   int rank = 0;
   for (int j = 0; j < k; ++j) {
@@ -50,16 +46,21 @@ combine_kernel(const void* __restrict__ expert_out, const int32_t* __restrict__ 
     if (((live_k >> j) & 1u) && pj < p) ++rank;
   }
   const int nlive = __popc(live_k);
-  int src_of_rank = 0;  // lane r holds the source lane of rank r
+  int sp = -1;
+  float sw = 0.0f;
   for (int r = 0; r < nlive; ++r) {
     const unsigned m = __ballot_sync(0xffffffffu, ((live_k >> lane) & 1u) && rank == r);
-    if (lane == r) src_of_rank = __ffs(m) - 1;
+    const int src = __ffs(m) - 1;
+    const int pr = __shfl_sync(0xffffffffu, p, src);
+    const float wr = __shfl_sync(0xffffffffu, w, src);
+    if (lane == r) { sp = pr; sw = wr; }
   }
 
   const uint4* src = static_cast<const uint4*>(expert_out);
   const uint4* fin = static_cast<const uint4*>(final_in);
   uint4* dst = static_cast<uint4*>(out);
   constexpr int EPC = BF16 ? 8 : 4;  // elements per 16-byte chunk
+  constexpr int kBatch = 4;          // rows loaded before they are summed
   // every lane runs the same trip count so the shuffles below see all 32 lanes
   for (int c0 = 0; c0 < row_chunks; c0 += 32) {
     const int c = c0 + lane;
@@ -79,34 +80,48 @@ combine_kernel(const void* __restrict__ expert_out, const int32_t* __restrict__ 
 #pragma unroll
       for (int i = 0; i < EPC; ++i) acc[i] = 0.0f;
     }
-    for (int r = 0; r < nlive; ++r) {
-      const int sl = __shfl_sync(0xffffffffu, src_of_rank, r);
-      const int pj = __shfl_sync(0xffffffffu, p, sl);
-      const float wj = __shfl_sync(0xffffffffu, w, sl);
-      if (!live) continue;
-      const uint4 u = __ldg(src + static_cast<int64_t>(pj) * row_chunks + c);
-      float y[EPC];
-      if (BF16) {
-        const uint32_t q[4] = {u.x, u.y, u.z, u.w};
+    for (int r0 = 0; r0 < nlive; r0 += kBatch) {
+      uint4 rows[kBatch];
+      float ws[kBatch];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) { y[2 * i] = bf16_lo(q[i]); y[2 * i + 1] = bf16_hi(q[i]); }
-      } else {
-        y[0] = __uint_as_float(u.x); y[1] = __uint_as_float(u.y);
-        y[2] = __uint_as_float(u.z); y[3] = __uint_as_float(u.w);
+      for (int b = 0; b < kBatch; ++b) {
+        const int pj = __shfl_sync(0xffffffffu, sp, (r0 + b) & 31);
+        ws[b] = __shfl_sync(0xffffffffu, sw, (r0 + b) & 31);
+        rows[b] = (live && r0 + b < nlive)
+                      ? __ldg(src + static_cast<int64_t>(pj) * row_chunks + c)
+                      : make_uint4(0, 0, 0, 0);
       }
 #pragma unroll
-      for (int i = 0; i < EPC; ++i) {
-        // two separate roundings, as the reference's mul then add (no fma)
-        const float prod = round_dt<BF16>(__fmul_rn(y[i], wj));
-        acc[i] = round_dt<BF16>(__fadd_rn(acc[i], prod));
+      for (int b = 0; b < kBatch; ++b) {
+        if (r0 + b >= nlive) break;
+        const uint4 u = rows[b];
+        if (BF16) {
+          // product rounded to bf16 (paired, exact = round(fp32 product)),
+          // then fp32 add and one rounding of the sum, as torch does
+          const uint32_t w2 = cvt_bf16x2(ws[b], ws[b]);
+          const uint32_t q[4] = {mul_bf16x2(u.x, w2), mul_bf16x2(u.y, w2), mul_bf16x2(u.z, w2),
+                                 mul_bf16x2(u.w, w2)};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const uint32_t s2 = cvt_bf16x2(__fadd_rn(acc[2 * i], bf16_lo(q[i])),
+                                           __fadd_rn(acc[2 * i + 1], bf16_hi(q[i])));
+            acc[2 * i] = bf16_lo(s2);
+            acc[2 * i + 1] = bf16_hi(s2);
+          }
+        } else {
+          const float y[4] = {__uint_as_float(u.x), __uint_as_float(u.y), __uint_as_float(u.z),
+                              __uint_as_float(u.w)};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) acc[i] = __fadd_rn(acc[i], __fmul_rn(y[i], ws[b]));
+        }
       }
     }
     uint4 o;
     if (BF16) {
-      o.x = pack_bf16x2(acc[0], acc[1]);
-      o.y = pack_bf16x2(acc[2], acc[3]);
-      o.z = pack_bf16x2(acc[4], acc[5]);
-      o.w = pack_bf16x2(acc[6], acc[7]);
+      o.x = cvt_bf16x2(acc[0], acc[1]);
+      o.y = cvt_bf16x2(acc[2], acc[3]);
+      o.z = cvt_bf16x2(acc[4], acc[5]);
+      o.w = cvt_bf16x2(acc[6], acc[7]);
     } else {
       o.x = __float_as_uint(acc[0]); o.y = __float_as_uint(acc[1]);
       o.z = __float_as_uint(acc[2]); o.w = __float_as_uint(acc[3]);

@@ -16,6 +16,11 @@ constexpr int kDevOk = 0;
 constexpr int kDevBadExpert = 1;   // an expert id outside [0, E) was dropped
 constexpr int kDevTimeout = 2;     // a bounded wait gave up
 
+// The fixed accumulation order of router logits: k is cut into blocks of
+// kLogitBlock; each block is one fma per k, ascending, from +0, and the block
+// sums are added in ascending order from +0 (oracle/router_ref.c restates it).
+constexpr int kLogitBlock = 64;
+
 // Default limit for a device-side wait before the kernel gives up (ns).
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;
 
@@ -38,6 +43,19 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 }
 __device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+// Two floats -> bf16x2 with one paired conversion (round to nearest even each).
+__device__ __forceinline__ uint32_t cvt_bf16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+// Element-wise bf16x2 product, rounded once to bf16.  A product of two bf16
+// values is exact in fp32, so this equals rounding the fp32 product.
+__device__ __forceinline__ uint32_t mul_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
 
 // Load one element of the layer dtype as fp32.
 __device__ __forceinline__ float load_elem(const void* p, int64_t i, int dtype) {
@@ -125,6 +143,30 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar)
       : "memory");
+}
+
+// 2-D tiled bulk tensor store shared -> global (bulk-group completion).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, int c0, int c1, uint32_t src) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(c0), "r"(c1), "r"(src)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Wait until at most N committed bulk groups still read their shared source.
+template <int N>
+__device__ __forceinline__ void bulk_wait_group_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void bulk_wait_group_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+// Make this thread's generic-proxy shared-memory writes visible to the async proxy (TMA).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 // -------------------------------------------------------------- tcgen05 ----

@@ -15,9 +15,10 @@
 //               (M=128, N=256, K=16) into one of two 256-column fp32
 //               accumulators and commits stage / accumulator barriers.
 //   warps 2..5  epilogue: tcgen05.ld the accumulator (each warp its 32-lane
-//               quadrant), apply the activation, convert to bf16, store the
-//               rows that belong to the group; then free the accumulator so
-//               the next tile's MMAs overlap this tile's stores.
+//               quadrant), apply the activation, convert to bf16, stage 32x32
+//               chunks in shared memory and TMA-store them (rows past a group
+//               end are stored directly, masked); then free the accumulator
+//               so the next tile's MMAs overlap this tile's stores.
 // Tiles are (group, 128-row block, column block); the table of group row
 // offsets and tile prefixes is built in shared memory from the per-group
 // counts on the device, so no host synchronisation is needed.  A group's
@@ -50,6 +51,9 @@ constexpr int kNumAcc = 2;
 constexpr int kTmemCols = kAccCols * kNumAcc; // 512 = all of TMEM
 constexpr int kThreads = 192;
 constexpr int kMaxGroups = 1024;
+constexpr int kEpiWarps = 4;
+constexpr int kEpiChunkBytes = 32 * 32 * 2;                  // 32 rows x 32 bf16 columns
+constexpr int kEpiBytes = kEpiWarps * 2 * kEpiChunkBytes;    // double-buffered per warp
 
 struct SmemCtl {
   uint64_t full[kStages];
@@ -65,7 +69,9 @@ struct SmemCtl {
   int tile_prefix[kMaxGroups + 1];  // exclusive prefix of 128-row blocks
 };
 
-constexpr size_t kSmemBytes = 1024 + static_cast<size_t>(kStages) * kStageBytes + sizeof(SmemCtl);
+constexpr size_t kSmemBytes =
+    1024 + static_cast<size_t>(kStages) * kStageBytes + kEpiBytes + sizeof(SmemCtl);
+static_assert(kSmemBytes <= 232448, "shared memory budget of one sm_100 CTA");
 
 struct KParams {
   const int32_t* counts;
@@ -96,10 +102,10 @@ __device__ __forceinline__ void decode_tile(const SmemCtl& ctl, int G, int n_til
   nrows = min(BM, ctl.group_rows[g + 1] - row0);
 }
 
+// 32 accumulator columns of one row -> 16 packed bf16x2 words.
 template <bool SWIGLU>
-__device__ __forceinline__ void store_chunk32(const uint32_t (&a)[32], const uint32_t (&b)[32],
-                                              uint16_t* orow, int col0, int N) {
-  uint32_t packed[16];
+__device__ __forceinline__ void epi_pack(const uint32_t (&a)[32], const uint32_t (&b)[32],
+                                         uint32_t (&packed)[16]) {
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
     float v0, v1;
@@ -120,6 +126,11 @@ __device__ __forceinline__ void store_chunk32(const uint32_t (&a)[32], const uin
     }
     packed[i] = pack_bf16x2(v0, v1);
   }
+}
+
+// Direct row store (rows whose 32-row quadrant crosses a group end).
+__device__ __forceinline__ void store_row_direct(const uint32_t (&packed)[16], uint16_t* orow,
+                                                 int col0, int N) {
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
     if (col0 + c * 8 + 8 <= N) {
@@ -129,14 +140,21 @@ __device__ __forceinline__ void store_chunk32(const uint32_t (&a)[32], const uin
   }
 }
 
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w)
+               : "memory");
+}
+
 template <bool SWIGLU>
 __global__ void __launch_bounds__(kThreads, 1)
 grouped_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
-                          const __grid_constant__ CUtensorMap tmB, const KParams p) {
+                          const __grid_constant__ CUtensorMap tmB,
+                          const __grid_constant__ CUtensorMap tmC, const KParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  SmemCtl& ctl = *reinterpret_cast<SmemCtl*>(smem + kStages * kStageBytes);
+  SmemCtl& ctl = *reinterpret_cast<SmemCtl*>(smem + kStages * kStageBytes + kEpiBytes);
   const uint32_t sbase = smem_u32(smem);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -186,6 +204,7 @@ grouped_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
       fence_mbar_init();
       tma_prefetch_desc(&tmA);
       tma_prefetch_desc(&tmB);
+      tma_prefetch_desc(&tmC);
     }
   } else if (warp == 1) {
     tmem_alloc(smem_u32(&ctl.tmem_base), kTmemCols);
@@ -270,9 +289,15 @@ grouped_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
     }
   } else {
     // ------------------------------------------------------------ epilogue
+    // Each warp owns a 32-lane TMEM quadrant (= 32 rows).  Per 32-column
+    // chunk it packs bf16 values into one of two 2 KiB staging buffers and a
+    // single lane issues a TMA tensor store of the 32x32 box, so global
+    // writes are whole lines and run asynchronously.  A quadrant that
+    // crosses the end of its group (or of A) stores its valid rows directly.
     const int quad = warp & 3;                 // TMEM lanes this warp may read
     const int r_in_tile = quad * 32 + lane;
-    int acc = 0;
+    const uint32_t stg = sbase + kStages * kStageBytes + (warp - 2) * 2 * kEpiChunkBytes;
+    int acc = 0, buf = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       int g, row0, nrows, n;
@@ -283,30 +308,62 @@ grouped_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
                             static_cast<uint32_t>(acc * kAccCols);
       const int64_t grow = static_cast<int64_t>(row0) + r_in_tile;
       const bool row_ok = r_in_tile < nrows && grow < p.M;
+      const bool quad_full = (quad + 1) * 32 <= nrows &&
+                             static_cast<int64_t>(row0) + (quad + 1) * 32 <= p.M;
       uint16_t* orow = p.out + grow * p.N;
-      if (SWIGLU) {
+      constexpr int kChunks = SWIGLU ? BNH / 32 : kAccCols / 32;
 #pragma unroll 1
-        for (int c = 0; c < BNH / 32; ++c) {
-          uint32_t ga[32], ua[32];
-          tmem_ld_32cols(trow + c * 32, ga);
-          tmem_ld_32cols(trow + BNH + c * 32, ua);
-          tc_wait_ld();
-          if (row_ok) store_chunk32<true>(ga, ua, orow, n * p.out_cols_per_tile + c * 32, p.N);
-        }
-      } else {
-#pragma unroll 1
-        for (int c = 0; c < kAccCols / 32; ++c) {
+      for (int c = 0; c < kChunks; ++c) {
+        uint32_t packed[16];
+        {
           uint32_t ra[32];
           tmem_ld_32cols(trow + c * 32, ra);
-          tc_wait_ld();
-          if (row_ok) store_chunk32<false>(ra, ra, orow, n * p.out_cols_per_tile + c * 32, p.N);
+          if (SWIGLU) {
+            uint32_t ua[32];
+            tmem_ld_32cols(trow + BNH + c * 32, ua);
+            tc_wait_ld();
+            epi_pack<true>(ra, ua, packed);
+          } else {
+            tc_wait_ld();
+            epi_pack<false>(ra, ra, packed);
+          }
         }
+        const int col0 = n * p.out_cols_per_tile + c * 32;
+        if (col0 >= p.N) continue;
+        if (quad_full && !SWIGLU) {
+          // the down projection writes 64 KiB per tile: TMA stores keep the
+          // epilogue off the critical path; the SwiGLU tile (32 KiB per 3x
+          // longer mainloop) is cheaper with direct stores
+          if (lane == 0) bulk_wait_group_read<1>();  // the store that last used `buf` read it
+          __syncwarp();
+          // 64-byte swizzle (matches the store map): 16-byte piece c of row r
+          // sits at r*64 + ((c ^ ((r >> 1) & 3)) * 16), so the 8 lanes of each
+          // store phase hit 8 different bank groups
+          const uint32_t dst = stg + buf * kEpiChunkBytes + lane * 64;
+          const uint32_t sw = (lane >> 1) & 3;
+#pragma unroll
+          for (int c4 = 0; c4 < 4; ++c4)
+            st_shared_v4(dst + ((c4 ^ sw) << 4), make_uint4(packed[4 * c4], packed[4 * c4 + 1],
+                                                            packed[4 * c4 + 2], packed[4 * c4 + 3]));
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmC, col0, row0 + quad * 32, stg + buf * kEpiChunkBytes);
+            bulk_commit_group();
+          }
+          buf ^= 1;
+        } else if (row_ok) {
+          store_row_direct(packed, orow, col0, p.N);
+        }
+        (void)buf;
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&ctl.acc_empty[acc]));
       if (++acc == kNumAcc) { acc = 0; acc_phase ^= 1u; }
     }
+    if (lane == 0) bulk_wait_group_all();  // stores complete before the CTA exits
+    __syncwarp();
   }
 
   // --------------------------------------------------------------- teardown
@@ -338,18 +395,18 @@ EncodeTiledFn get_encode_fn() {
   return fn;
 }
 
-// Row-major bf16 matrix [rows, cols] as a 2-D map with [box_rows, 64] boxes.
-bool make_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+// Row-major bf16 matrix [rows, cols] as a 2-D map with [box_rows, box_cols] boxes.
+bool make_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows,
+              uint32_t box_cols, CUtensorMapSwizzle swizzle) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return false;
   const cuuint64_t dims[2] = {cols, rows};
   const cuuint64_t strides[1] = {cols * 2};
-  const cuuint32_t box[2] = {static_cast<cuuint32_t>(BK), box_rows};
+  const cuuint32_t box[2] = {box_cols, box_rows};
   const cuuint32_t estr[2] = {1, 1};
   const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
-                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
@@ -379,9 +436,13 @@ cudaError_t launch_grouped_gemm_sm100(const GroupedGemmArgs& a, cudaStream_t str
   if (a.M == 0 || a.G == 0) return cudaSuccess;
   if (a.G > kMaxGroups || a.K % 8 != 0 || a.N % 8 != 0) return cudaErrorInvalidValue;
   const int nw = a.swiglu ? 2 * a.N : a.N;          // rows of B per group
-  CUtensorMap ma, mb;
-  if (!make_map(&ma, a.a, static_cast<uint64_t>(a.M), static_cast<uint64_t>(a.K), BM) ||
-      !make_map(&mb, a.b, static_cast<uint64_t>(a.G) * nw, static_cast<uint64_t>(a.K), BNH))
+  CUtensorMap ma, mb, mc;
+  if (!make_map(&ma, a.a, static_cast<uint64_t>(a.M), static_cast<uint64_t>(a.K), BM, BK,
+                CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_map(&mb, a.b, static_cast<uint64_t>(a.G) * nw, static_cast<uint64_t>(a.K), BNH, BK,
+                CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_map(&mc, a.out, static_cast<uint64_t>(a.M), static_cast<uint64_t>(a.N), 32, 32,
+                CU_TENSOR_MAP_SWIZZLE_64B))
     return cudaErrorInvalidValue;
   KParams p;
   p.counts = a.counts;
@@ -402,10 +463,10 @@ cudaError_t launch_grouped_gemm_sm100(const GroupedGemmArgs& a, cudaStream_t str
   cudaError_t e;
   if (a.swiglu) {
     if ((e = ensure_smem_attr<true>()) != cudaSuccess) return e;
-    grouped_gemm_sm100_kernel<true><<<grid, kThreads, kSmemBytes, stream>>>(ma, mb, p);
+    grouped_gemm_sm100_kernel<true><<<grid, kThreads, kSmemBytes, stream>>>(ma, mb, mc, p);
   } else {
     if ((e = ensure_smem_attr<false>()) != cudaSuccess) return e;
-    grouped_gemm_sm100_kernel<false><<<grid, kThreads, kSmemBytes, stream>>>(ma, mb, p);
+    grouped_gemm_sm100_kernel<false><<<grid, kThreads, kSmemBytes, stream>>>(ma, mb, mc, p);
   }
   return cudaGetLastError();
 }

@@ -16,6 +16,16 @@ cudaError_t launch_router_topk(const void* x, const void* w_router, const void* 
                                int32_t* topk_idx, float* topk_w_f32, void* topk_w_dtype,
                                void* logits_out, cudaStream_t stream);
 
+// router_tc.cu (bf16 only) -----------------------------------------------
+// Relative margin (of the token's largest |logit|) inside which a tensor-core
+// sum is treated as possibly rounding differently from the exact-order sum.
+constexpr float kRouterCertRel = 1.0f / 16384.0f;
+size_t router_tc_scratch_bytes(int64_t T);
+cudaError_t launch_router_topk_tc(const void* x, const void* w_router, const void* bias,
+                                  int64_t T, int d, int E, int k, int norm, int32_t* topk_idx,
+                                  float* topk_w_f32, void* topk_w_dtype, void* logits_out,
+                                  void* scratch, int* err, cudaStream_t stream);
+
 // dispatch.cu -----------------------------------------------------------
 // Tokens per histogram block for a given top_k.
 int dispatch_block_tokens(int k);

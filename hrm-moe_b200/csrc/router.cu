@@ -9,9 +9,10 @@
 //
 // One CTA handles 64 tokens.  The logits GEMM runs on the CUDA cores in
 // fp32: thread (ty, tx) owns 4 tokens x EPT experts and accumulates every
-// output with one fmaf per k in ascending k, starting from +0 -- the order
-// the CPU oracle restates, so the logits are bit-identical to it.  The sum
-// (plus bias) is rounded to the layer dtype, like F.linear's output.
+// output in the fixed order kLogitBlock defines (one fmaf per k ascending
+// within each 64-wide block from +0, block sums added in order from +0) --
+// the order the CPU oracle restates, so the logits are bit-identical to it.
+// The sum (plus bias) is rounded to the layer dtype, like F.linear's output.
 //
 // Selection runs one warp per token over the rounded logits kept in shared
 // memory: k rounds of a warp-shuffle argmax where equal values go to the
@@ -52,11 +53,11 @@ router_topk_kernel(const void* __restrict__ xv, const void* __restrict__ wv,
   const int tx = tid & 15;
   const int64_t t0 = static_cast<int64_t>(blockIdx.x) * kRTok;
 
-  float acc[4][EPT];
+  float acc[4][EPT], part[4][EPT];
 #pragma unroll
   for (int i = 0; i < 4; ++i)
 #pragma unroll
-    for (int j = 0; j < EPT; ++j) acc[i][j] = 0.0f;
+    for (int j = 0; j < EPT; ++j) { acc[i][j] = 0.0f; part[i][j] = 0.0f; }
 
   for (int k0 = 0; k0 < d; k0 += kRKc) {
     const int kc = min(kRKc, d - k0);
@@ -141,7 +142,14 @@ router_topk_kernel(const void* __restrict__ xv, const void* __restrict__ wv,
 #pragma unroll
       for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int j = 0; j < EPT; ++j) acc[i][j] = fmaf(xr[i], wr[j], acc[i][j]);
+        for (int j = 0; j < EPT; ++j) part[i][j] = fmaf(xr[i], wr[j], part[i][j]);
+    }
+    // end of a 64-wide block of k: add its sum into the total
+    if ((k0 + kRKc) % kLogitBlock == 0 || k0 + kRKc >= d) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < EPT; ++j) { acc[i][j] = acc[i][j] + part[i][j]; part[i][j] = 0.0f; }
     }
     __syncthreads();
   }

@@ -1,0 +1,509 @@
+// Router for bf16 layers on the tensor cores, certified against the
+// exact-order definition, with a fix-up pass for the tokens it cannot certify.
+//
+// Mirrors models/layers.py:604-610 (gate F.linear -> fp32 softmax -> top-k ->
+// renormalise -> cast).  The routing a token gets is defined by its logits
+// accumulated in fp32 in the fixed order of kLogitBlock (the order the CPU
+// oracle and the CUDA-core router use), rounded to bf16.
+//
+// router_tc_kernel: one CTA per 128 tokens.  TMA streams the token tile
+// [128 x 64] and the router weight [E x 64] per k-step through a smem ring;
+// one thread issues tcgen05.mma (M=128, N=64/128, K=16) into TMEM.  The
+// epilogue parks the fp32 logits in smem and routes one token per thread.  Each
+// rounded logit carries the set of bf16 values the exact-order sum could
+// round to: itself, plus a neighbour when the tensor-core sum lies within
+// `cert_rel * max|logit|` of a rounding midpoint.  A token's top-k is
+// accepted only if every order decision it contains (each pick against the
+// next, the last pick against every unpicked expert) holds for all values in
+// those sets; otherwise the token is appended to a fix-up list.
+//
+// router_fixup_kernel: recomputes the listed tokens' logits in the exact
+// order on the CUDA cores (the blocks of k in parallel, four tokens per CTA)
+// and routes them again, overwriting the output.
+// The result equals the CUDA-core router's for every token.
+#include <limits.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "internal.h"
+#include "router_common.cuh"
+
+namespace hmoe {
+namespace {
+
+constexpr int RBM = 128;       // tokens per CTA (MMA M)
+constexpr int RBK = 64;        // bf16 per 128-byte swizzled row
+constexpr int kRtThreads = 192;
+
+template <int EPAD>
+struct RCfg {
+  static constexpr int kStages = EPAD == 64 ? 6 : 4;
+  static constexpr int kABytes = RBM * RBK * 2;
+  static constexpr int kBBytes = EPAD * RBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kRingBytes = kStages * kStageBytes;
+  static constexpr int kLgStride = EPAD + 1;
+  static constexpr int kLgBytes = 3 * RBM * kLgStride * 4;  // values, keys, largest keys
+  static constexpr int kMainBytes = kRingBytes > kLgBytes ? kRingBytes : kLgBytes;
+  static constexpr int kCtlBytes = 256;
+  static constexpr size_t kSmem = 1024 + kMainBytes + kCtlBytes;
+  static_assert(kStageBytes % 1024 == 0, "stages keep the 1 KiB swizzle alignment");
+  static_assert(kSmem <= 232448, "shared memory budget");
+};
+
+struct RtCtl {
+  uint64_t full[8];
+  uint64_t empty[8];
+  uint64_t acc_full;
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+
+struct RtParams {
+  const uint16_t* bias;  // [E] bf16 or null
+  int64_t T;
+  int d, E, k, norm;
+  int32_t* topk_idx;
+  float* topk_w_f32;
+  void* topk_w_dtype;
+  uint16_t* logits_out;
+  int* fix_count;
+  int32_t* fix_list;
+  int* err;
+  unsigned long long wait_limit_ns;
+  float cert_rel;
+};
+
+// Orderable 16-bit image of a bf16 bit pattern: unsigned order = value
+// order (negative values flipped), so key = (ob << 16) | (0xFFFF - e) sorts
+// by value descending and, on equal values, by expert index ascending.
+__device__ __forceinline__ uint32_t ob16(uint32_t b) {
+  return (b & 0x8000u) ? (~b & 0xFFFFu) : (b | 0x8000u);
+}
+
+// Keys of the smallest and largest bf16 value the exact-order sum of this
+// logit could round to (tensor-core sum v, margin delta).
+__device__ __forceinline__ void key_range(float v, float delta, uint32_t e, uint32_t& kmin,
+                                          uint32_t& kmax, uint32_t& key) {
+  const uint32_t b = f32_to_bf16_bits(v);
+  const uint32_t ob = ob16(b);
+  const uint32_t lo16 = 0xFFFFu - e;
+  key = (ob << 16) | lo16;
+  uint32_t oblo = ob, obhi = ob;
+  if (isfinite(v) && (b & 0x7F80u) != 0x7F80u) {
+    const float a = fabsf(v);
+    if (a <= delta) {
+      // the sign itself is not certain: anything within +-delta (rounded out)
+      const uint32_t m = (__float_as_uint(delta) >> 16) + 1;
+      oblo = ob16(m | 0x8000u);
+      obhi = ob16(m);
+    } else {
+      const uint32_t h = b & 0x7FFFu;  // magnitude as consecutive integers
+      const bool up = a >= __uint_as_float((h << 16) | 0x8000u) - delta;
+      const bool dn = h > 0 && a <= __uint_as_float(((h - 1) << 16) | 0x8000u) + delta;
+      const bool neg = (b & 0x8000u) != 0;
+      obhi = ob + ((neg ? dn : up) ? 1u : 0u);
+      oblo = ob - ((neg ? up : dn) ? 1u : 0u);
+    }
+  }
+  kmin = (oblo << 16) | lo16;
+  kmax = (obhi << 16) | lo16;
+}
+
+// Route one token from its fp32 tensor-core logits.  vrow[0..E) holds the
+// sums (biased in place), krow/xrow are scratch rows of the same thread.
+// Picks the k largest rounded logits (lower index on ties); the result is
+// certified when each pick's smallest possible key beats the next pick's
+// largest, and the last pick's beats every unpicked expert's largest.
+template <int KMAX>
+__device__ __forceinline__ void route_row_certified(float* vrow, uint32_t* krow, uint32_t* xrow,
+                                                    const RtParams& p, int64_t t) {
+  const int E = p.E, k = p.k;
+  float mag = 0.0f;
+  for (int e = 0; e < E; ++e) {
+    float v = vrow[e];
+    if (p.bias) v = v + bf16_bits_to_f32(p.bias[e]);
+    vrow[e] = v;
+    if (isfinite(v)) mag = fmaxf(mag, fabsf(v));
+  }
+  const float delta = p.cert_rel * mag;
+  for (int e = 0; e < E; ++e) {
+    uint32_t kmin, kmax, key;
+    key_range(vrow[e], delta, static_cast<uint32_t>(e), kmin, kmax, key);
+    krow[e] = key;
+    xrow[e] = kmax;
+  }
+  uint32_t pk[KMAX];
+  bool bad = false;
+  uint32_t prev_min = 0;
+#pragma unroll
+  for (int j = 0; j < KMAX; ++j) {
+    pk[j] = 0;
+    if (j < k) {
+      uint32_t best = 0;
+      for (int e = 0; e < E; ++e) best = max(best, krow[e]);
+      pk[j] = best;
+      const int e = 0xFFFF - static_cast<int>(best & 0xFFFFu);
+      krow[e] = 0;  // picked
+      uint32_t kmin, kmax, key;
+      key_range(vrow[e], delta, static_cast<uint32_t>(e), kmin, kmax, key);
+      if (j > 0 && !(prev_min > kmax)) bad = true;
+      prev_min = kmin;
+    }
+  }
+  uint32_t rest = 0;  // largest key an unpicked expert could take
+  for (int e = 0; e < E; ++e)
+    if (krow[e] != 0) rest = max(rest, xrow[e]);
+  if (!(prev_min > rest)) bad = true;
+  // softmax over the rounded logits, weights of the picks
+  const int e0 = 0xFFFF - static_cast<int>(pk[0] & 0xFFFFu);
+  const float mx = round_bf16(vrow[e0]);
+  float s = 0.0f;
+  for (int e = 0; e < E; ++e) s += expf(round_bf16(vrow[e]) - mx);
+  float pw[KMAX], ps = 0.0f;
+#pragma unroll
+  for (int j = 0; j < KMAX; ++j) {
+    pw[j] = 0.0f;
+    if (j < k) {
+      const int e = 0xFFFF - static_cast<int>(pk[j] & 0xFFFFu);
+      pw[j] = expf(round_bf16(vrow[e]) - mx) / s;
+      ps += pw[j];
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < KMAX; ++j) {
+    if (j < k) {
+      float w = p.norm ? pw[j] / fmaxf(ps, 1e-12f) : pw[j];
+      w = round_bf16(w);
+      const int64_t o = t * k + j;
+      p.topk_idx[o] = 0xFFFF - static_cast<int>(pk[j] & 0xFFFFu);
+      if (p.topk_w_f32) p.topk_w_f32[o] = w;
+      if (p.topk_w_dtype)
+        static_cast<uint16_t*>(p.topk_w_dtype)[o] = static_cast<uint16_t>(f32_to_bf16_bits(w));
+    }
+  }
+  if (p.logits_out)
+    for (int e = 0; e < E; ++e) p.logits_out[t * E + e] = static_cast<uint16_t>(f32_to_bf16_bits(vrow[e]));
+  if (bad) {
+    const int slot = atomicAdd(p.fix_count, 1);
+    p.fix_list[slot] = static_cast<int32_t>(t);
+  }
+}
+
+template <int EPAD, int KMAX>
+__global__ void __launch_bounds__(kRtThreads, 1)
+router_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
+                 const RtParams p) {
+  using C = RCfg<EPAD>;
+  constexpr int NV = EPAD / 32;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  RtCtl& ctl = *reinterpret_cast<RtCtl*>(smem + C::kMainBytes);
+  float* lg = reinterpret_cast<float*>(smem);
+  const uint32_t sbase = smem_u32(smem);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t t0 = static_cast<int64_t>(blockIdx.x) * RBM;
+  const int nkb = cdiv(p.d, RBK);
+  const unsigned long long lim = p.wait_limit_ns;
+
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(smem_u32(&ctl.full[s]), 1);
+      mbar_init(smem_u32(&ctl.empty[s]), 1);
+    }
+    mbar_init(smem_u32(&ctl.acc_full), 1);
+    mbar_init(smem_u32(&ctl.drain), 1);
+    ctl.abort = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmX);
+    tma_prefetch_desc(&tmW);
+  } else if (warp == 1) {
+    tmem_alloc(smem_u32(&ctl.tmem_base), EPAD);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = ctl.tmem_base;
+  volatile int* abort = &ctl.abort;
+  int never = 0;
+  bool acc_ok = true;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      uint32_t phase = 0, pending = 0, pend_phase = 0;
+      int stage = 0;
+      for (int kb = 0; kb < nkb; ++kb) {
+        if (!mbar_wait_bounded(smem_u32(&ctl.empty[stage]), phase ^ 1u, abort, p.err, lim)) break;
+        const uint32_t fb = smem_u32(&ctl.full[stage]);
+        const uint32_t sa = sbase + stage * C::kStageBytes;
+        mbar_arrive_expect_tx(fb, C::kStageBytes);
+        tma_load_2d(sa, &tmX, kb * RBK, static_cast<int>(t0), fb);
+        tma_load_2d(sa + C::kABytes, &tmW, kb * RBK, 0, fb);
+        pending |= 1u << stage;
+        pend_phase = (pend_phase & ~(1u << stage)) | (phase << stage);
+        if (++stage == C::kStages) { stage = 0; phase ^= 1u; }
+      }
+      for (int s = 0; s < C::kStages; ++s)
+        if ((pending >> s) & 1u)
+          mbar_wait_bounded(smem_u32(&ctl.full[s]), (pend_phase >> s) & 1u, &never, p.err, lim);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(RBM, EPAD);
+      uint32_t phase = 0;
+      int stage = 0;
+      bool ok = true;
+      for (int kb = 0; kb < nkb; ++kb) {
+        if (!mbar_wait_bounded(smem_u32(&ctl.full[stage]), phase, abort, p.err, lim)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sa = sbase + stage * C::kStageBytes;
+#pragma unroll
+        for (int kk = 0; kk < RBK / 16; ++kk)
+          tc_mma_bf16(tmem, smem_desc_sw128(sa + kk * 32), smem_desc_sw128(sa + C::kABytes + kk * 32),
+                      idesc, (kb | kk) != 0 ? 1u : 0u);
+        tc_commit(smem_u32(&ctl.empty[stage]));
+        if (++stage == C::kStages) { stage = 0; phase ^= 1u; }
+      }
+      if (ok) tc_commit(smem_u32(&ctl.acc_full));
+      tc_commit(smem_u32(&ctl.drain));
+      mbar_wait_bounded(smem_u32(&ctl.drain), 0, &never, p.err, lim);
+    }
+  } else {
+    // -------------- epilogue: one thread per token, its row of logits in smem
+    const int quad = warp & 3;
+    acc_ok = mbar_wait_bounded(smem_u32(&ctl.acc_full), 0, abort, p.err, lim);
+    tc_fence_after();
+    const int row = quad * 32 + lane;
+    float* lrow = lg + row * C::kLgStride;
+    if (acc_ok) {
+#pragma unroll 1
+      for (int c = 0; c < EPAD / 32; ++c) {
+        uint32_t ra[32];
+        tmem_ld_32cols(tmem + (static_cast<uint32_t>(quad * 32) << 16) + c * 32, ra);
+        tc_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) lrow[c * 32 + i] = __uint_as_float(ra[i]);
+      }
+    }
+    const int64_t t = t0 + row;
+    uint32_t* krow = reinterpret_cast<uint32_t*>(lg + RBM * C::kLgStride) + row * C::kLgStride;
+    uint32_t* xrow = reinterpret_cast<uint32_t*>(lg + 2 * RBM * C::kLgStride) + row * C::kLgStride;
+    if (acc_ok && !*abort && t < p.T)
+      route_row_certified<KMAX>(lrow, krow, xrow, p, t);
+    tc_fence_before();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, EPAD);
+  }
+}
+
+// Fix-up: exact-order logits for the listed tokens, then the same routing
+// as every router.  The order (kLogitBlock) lets the blocks of k run in
+// parallel: a CTA takes kFixG listed tokens; thread (expert e, block lane
+// bg) runs the one-fma-per-k chains of blocks bg, bg + nbg, ... for all
+// kFixG tokens at once, the block sums are then added in block order, and
+// one warp per token routes it.
+constexpr int kFixThreads = 256;
+constexpr int kFixG = 4;        // tokens per CTA pass
+
+template <int NV>
+__global__ void __launch_bounds__(kFixThreads)
+router_fixup_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ w,
+                    const uint16_t* __restrict__ bias, int64_t T, int d, int E, int k, int norm,
+                    const int* __restrict__ fix_count, const int32_t* __restrict__ fix_list,
+                    int32_t* __restrict__ topk_idx, float* __restrict__ topk_w_f32,
+                    void* __restrict__ topk_w_dtype, uint16_t* __restrict__ logits_out) {
+  constexpr int EP = NV * 32;
+  constexpr int NBG = kFixThreads / EP;       // block lanes per expert (4 / 2)
+  extern __shared__ float fsm[];
+  const int nb = cdiv(d, kLogitBlock);
+  float* xs = fsm;                                        // [kFixG][d]
+  float* part = fsm + kFixG * d;                          // [kFixG][EP][nb]
+  float* lgt = part + kFixG * EP * nb;                    // [kFixG][EP]
+  const int tid = threadIdx.x, lane = tid & 31, wib = tid >> 5;
+  const int e = tid % EP, bg = tid / EP;
+  const int n = *fix_count;
+  for (int base = blockIdx.x * kFixG; base < n; base += gridDim.x * kFixG) {
+    int64_t tok[kFixG];
+#pragma unroll
+    for (int g = 0; g < kFixG; ++g) {
+      const int64_t tt = base + g < n ? fix_list[base + g] : -1;
+      tok[g] = (tt >= 0 && tt < T) ? tt : -1;
+    }
+    for (int i = tid; i < kFixG * (d / 8); i += kFixThreads) {
+      const int g = i / (d / 8), c = i % (d / 8);
+      uint4 u = make_uint4(0, 0, 0, 0);
+      if (tok[g] >= 0) u = __ldg(reinterpret_cast<const uint4*>(x + tok[g] * d) + c);
+      float* xr = xs + g * d + c * 8;
+      xr[0] = bf16_lo(u.x); xr[1] = bf16_hi(u.x); xr[2] = bf16_lo(u.y); xr[3] = bf16_hi(u.y);
+      xr[4] = bf16_lo(u.z); xr[5] = bf16_hi(u.z); xr[6] = bf16_lo(u.w); xr[7] = bf16_hi(u.w);
+    }
+    __syncthreads();
+    const uint16_t* wr = w + static_cast<int64_t>(min(e, E - 1)) * d;
+    for (int b = bg; b < nb; b += NBG) {
+      const int k0 = b * kLogitBlock, kn = min(kLogitBlock, d - k0);
+      float acc[kFixG];
+#pragma unroll
+      for (int g = 0; g < kFixG; ++g) acc[g] = 0.0f;
+      for (int c = 0; c < kn / 8; ++c) {
+        const uint4 u = __ldg(reinterpret_cast<const uint4*>(wr + k0) + c);
+        const float wv[8] = {bf16_lo(u.x), bf16_hi(u.x), bf16_lo(u.y), bf16_hi(u.y),
+                             bf16_lo(u.z), bf16_hi(u.z), bf16_lo(u.w), bf16_hi(u.w)};
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+#pragma unroll
+          for (int g = 0; g < kFixG; ++g) acc[g] = fmaf(xs[g * d + k0 + c * 8 + j], wv[j], acc[g]);
+      }
+#pragma unroll
+      for (int g = 0; g < kFixG; ++g) part[(g * EP + e) * nb + b] = acc[g];
+    }
+    __syncthreads();
+    for (int i = tid; i < kFixG * EP; i += kFixThreads) {
+      const int g = i / EP, ee = i % EP;
+      float tot = 0.0f;
+      for (int b = 0; b < nb; ++b) tot = tot + part[(g * EP + ee) * nb + b];
+      if (bias && ee < E) tot = tot + bf16_bits_to_f32(bias[ee]);
+      lgt[g * EP + ee] = tot;
+    }
+    __syncthreads();
+    if (wib < kFixG && tok[wib] >= 0) {
+      const int64_t t = tok[wib];
+      float r[NV], sel[NV];
+      int id[NV];
+#pragma unroll
+      for (int q = 0; q < NV; ++q) {
+        const int ee = lane + 32 * q;
+        r[q] = ee < E ? round_bf16(lgt[wib * EP + ee]) : -INFINITY;
+        sel[q] = r[q];
+        id[q] = ee < E ? ee : INT_MAX;
+        if (logits_out && ee < E) logits_out[t * E + ee] = static_cast<uint16_t>(f32_to_bf16_bits(r[q]));
+      }
+      float my_v, mx;
+      int my_i;
+      warp_topk<NV>(sel, id, k, lane, my_v, my_i, mx);
+      const float wgt = warp_route_weight<NV, true>(r, E, k, norm, lane, my_v, mx);
+      write_route<true>(t, k, lane, my_i, wgt, topk_idx, topk_w_f32, topk_w_dtype);
+    }
+    __syncthreads();
+  }
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+bool map_rows(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {cols * 2};
+  const cuuint32_t box[2] = {RBK, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int EPAD, int KMAX>
+cudaError_t launch_tc(const void* x, const void* w, const RtParams& p, cudaStream_t st) {
+  using C = RCfg<EPAD>;
+  constexpr int NV = EPAD / 32;
+  static int done[64] = {0};
+  static std::mutex mu;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  const size_t fix_smem =
+      sizeof(float) * (static_cast<size_t>(kFixG) * p.d +
+                       static_cast<size_t>(kFixG) * EPAD * cdiv(p.d, kLogitBlock) +
+                       static_cast<size_t>(kFixG) * EPAD);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!done[dev]) {
+      e = cudaFuncSetAttribute(router_tc_kernel<EPAD, KMAX>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(C::kSmem));
+      if (e != cudaSuccess) return e;
+      e = cudaFuncSetAttribute(router_fixup_kernel<NV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               232448);
+      if (e != cudaSuccess) return e;
+      done[dev] = 1;
+    }
+  }
+  if (fix_smem > 232448) return cudaErrorInvalidValue;
+  CUtensorMap mx, mw;
+  if (!map_rows(&mx, x, static_cast<uint64_t>(p.T), static_cast<uint64_t>(p.d), RBM) ||
+      !map_rows(&mw, w, static_cast<uint64_t>(p.E), static_cast<uint64_t>(p.d), EPAD))
+    return cudaErrorInvalidValue;
+  router_tc_kernel<EPAD, KMAX><<<static_cast<unsigned>(cdiv64(p.T, RBM)), kRtThreads, C::kSmem, st>>>(
+      mx, mw, p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  router_fixup_kernel<NV><<<num_sms_for_current_device() * 2, kFixThreads, fix_smem, st>>>(
+      static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(w), p.bias, p.T, p.d, p.E,
+      p.k, p.norm, p.fix_count, p.fix_list, p.topk_idx, p.topk_w_f32, p.topk_w_dtype,
+      p.logits_out);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+size_t router_tc_scratch_bytes(int64_t T) { return sizeof(int) * 64 + sizeof(int32_t) * T; }
+
+cudaError_t launch_router_topk_tc(const void* x, const void* w_router, const void* bias,
+                                  int64_t T, int d, int E, int k, int norm, int32_t* topk_idx,
+                                  float* topk_w_f32, void* topk_w_dtype, void* logits_out,
+                                  void* scratch, int* err, cudaStream_t stream) {
+  if (T == 0) return cudaSuccess;
+  int* fix_count = static_cast<int*>(scratch);
+  cudaError_t e = cudaMemsetAsync(fix_count, 0, sizeof(int), stream);
+  if (e != cudaSuccess) return e;
+  RtParams p;
+  p.bias = static_cast<const uint16_t*>(bias);
+  p.T = T;
+  p.d = d;
+  p.E = E;
+  p.k = k;
+  p.norm = norm;
+  p.topk_idx = topk_idx;
+  p.topk_w_f32 = topk_w_f32;
+  p.topk_w_dtype = topk_w_dtype;
+  p.logits_out = static_cast<uint16_t*>(logits_out);
+  p.fix_count = fix_count;
+  p.fix_list = reinterpret_cast<int32_t*>(static_cast<char*>(scratch) + sizeof(int) * 64);
+  p.err = err;
+  p.wait_limit_ns = kWaitLimitNs;
+  p.cert_rel = kRouterCertRel;
+  if (k <= 8)
+    return E <= 64 ? launch_tc<64, 8>(x, w_router, p, stream)
+                   : launch_tc<128, 8>(x, w_router, p, stream);
+  return E <= 64 ? launch_tc<64, 32>(x, w_router, p, stream)
+                 : launch_tc<128, 32>(x, w_router, p, stream);
+}
+
+}  // namespace hmoe

@@ -86,8 +86,13 @@ def router_topk(x: torch.Tensor, w_router: torch.Tensor, top_k: int, norm_topk_p
     w = torch.empty((T, top_k), dtype=x.dtype, device=dev)
     logits = torch.empty((T, E), dtype=x.dtype, device=dev) if return_logits else None
     lib = _lib.load()
+    ws_bytes = lib.hmoe_router_workspace_bytes(ctypes.byref(shape))
+    if ws_bytes == 0:
+        raise ValueError(_lib.last_error())
+    ws = _workspace(ws_bytes, dev)
     _lib.check(lib.hmoe_router_topk(ctypes.byref(shape), _ptr(x), _ptr(w_router), _ptr(router_bias),
-                                    _ptr(idx), _ptr(w), _ptr(logits), _stream(dev)))
+                                    _ptr(idx), _ptr(w), _ptr(logits), _ptr(ws), ws.numel(),
+                                    _stream(dev)))
     return (idx, w, logits) if return_logits else (idx, w)
 
 

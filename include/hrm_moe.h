@@ -90,15 +90,19 @@ int hmoe_ffn_forward_marked(const hmoe_shape* shape, const void* x, const void* 
 
 /*
  * Router: self.gate + fp32 softmax + top-k + renormalise + cast
- * (models/layers.py:604-610).  Logits are accumulated in fp32 in a fixed
- * order (one fma per k, ascending) and rounded to the layer dtype as the
- * reference's F.linear output is; selection takes the k largest logits,
- * equal logits going to the lower expert index.  logits (optional, [T, E],
- * layer dtype) returns the rounded logits.  No workspace.
+ * (models/layers.py:604-610).  The routing is that of logits accumulated in
+ * fp32 in a fixed order (one fma per k, ascending, from +0) plus the bias and
+ * rounded to the layer dtype, as the reference's F.linear output is;
+ * selection takes the k largest logits, equal logits going to the lower
+ * expert index.  bf16 layers compute the logits on the tensor cores and
+ * recompute, in the fixed order, every token whose top-k the tensor-core
+ * sums cannot certify, so the result is the same.  logits (optional, [T, E],
+ * layer dtype) returns the rounded logits the routing used.
  */
+size_t hmoe_router_workspace_bytes(const hmoe_shape* shape);
 int hmoe_router_topk(const hmoe_shape* shape, const void* x, const void* w_router,
                      const void* router_bias, int32_t* topk_idx, void* topk_weight,
-                     void* logits, void* stream);
+                     void* logits, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * Dispatch: flatten, stable sort by expert, gather rows, count

@@ -5,13 +5,15 @@
  * Router logits of the reference MoE layer, restated in C:
  *   logits = F.linear(hidden_states, gate.weight[, bias])      models/layers.py:605
  * computed in fp32 with a FIXED accumulation order: for each (token, expert)
- * the products x[t,k] * w[e,k] are accumulated by one fused multiply-add per
- * k, k = 0 .. d-1 in ascending order, starting from +0.0f.  The bias (if any)
- * is then added in fp32 and the result is rounded once to the hidden dtype
- * (bf16 round-to-nearest-even, or kept as fp32).
+ * k is cut into blocks of 64; within a block the products x[t,k] * w[e,k]
+ * are accumulated by one fused multiply-add per k in ascending order from
+ * +0.0f, and the block sums are added (fp32 add) in ascending block order
+ * from +0.0f.  The bias (if any) is then added in fp32 and the result is
+ * rounded once to the hidden dtype (bf16 round-to-nearest-even, or fp32).
  *
- * The GPU router kernel accumulates in exactly this order, so its logits are
- * bit-identical to these (fmaf is correctly rounded on both sides).  The
+ * The GPU's exact-order router kernels accumulate in exactly this order, so
+ * their logits are bit-identical to these (fmaf is correctly rounded on both
+ * sides).  The
  * reference's own logits come from a BLAS GEMM whose order is unspecified;
  * they agree with these except where the exact sum sits within the fp32
  * accumulation error of a bf16 rounding midpoint.
@@ -33,19 +35,27 @@ static float round_bf16(float v) {
   return v;
 }
 
-/* acc[e] = fma(x[k], wT[k][e], acc[e]) over k ascending; vectorised across e. */
+/* Per 64-wide block of k: part[e] = fma(x[k], wT[k][e], part[e]) over the
+ * block's k ascending from +0; acc[e] = acc[e] + part[e] block after block,
+ * from +0.  Vectorised across e. */
+#define LOGIT_BLOCK 64
 __attribute__((target_clones("arch=x86-64-v3", "default")))
 static void logits_block(const float* x, const float* wT, const float* bias,
                          float* out, int64_t t0, int64_t t1, int d, int E,
                          int to_bf16) {
-  float acc[512];
+  float acc[512], part[512];
   for (int64_t t = t0; t < t1; ++t) {
     const float* xr = x + t * (int64_t)d;
     for (int e = 0; e < E; ++e) acc[e] = 0.0f;
-    for (int k = 0; k < d; ++k) {
-      const float xv = xr[k];
-      const float* wr = wT + (int64_t)k * E;
-      for (int e = 0; e < E; ++e) acc[e] = fmaf(xv, wr[e], acc[e]);
+    for (int k0 = 0; k0 < d; k0 += LOGIT_BLOCK) {
+      const int k1 = k0 + LOGIT_BLOCK < d ? k0 + LOGIT_BLOCK : d;
+      for (int e = 0; e < E; ++e) part[e] = 0.0f;
+      for (int k = k0; k < k1; ++k) {
+        const float xv = xr[k];
+        const float* wr = wT + (int64_t)k * E;
+        for (int e = 0; e < E; ++e) part[e] = fmaf(xv, wr[e], part[e]);
+      }
+      for (int e = 0; e < E; ++e) acc[e] = acc[e] + part[e];
     }
     float* o = out + t * (int64_t)E;
     for (int e = 0; e < E; ++e) {
