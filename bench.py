@@ -34,6 +34,8 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "MoE-FFN fwd tokens/s (XL 64x8 bf16)"
 L2_FLUSH_BYTES = 256 << 20
+# measured peer copy bandwidth per direction per GPU on this pool (NVLink 5)
+NVLINK_GBS = 770.0
 # DRAM bytes per launch of the dominant kernel from `ncu` (see profiles/);
 # None until a capture of the current kernel exists.
 NCU_TRAFFIC_BYTES = {}
@@ -255,6 +257,19 @@ def b200_arm(args, rank, world, local_rank):
             ctypes.c_void_p(y.data_ptr()), 0, ctypes.c_void_p(ws.data_ptr()), ws.numel(),
             ctypes.c_void_p(stream.cuda_stream), arr))
 
+    ep = None
+    if world > 1:
+        # expert parallel: this rank keeps experts [rank*E/N, (rank+1)*E/N)
+        ep = importlib.import_module("hrm-moe_b200.ep")
+        el = E // world
+        w_gate_up = w_gate_up[rank * el:(rank + 1) * el].contiguous()
+        w_down = w_down[rank * el:(rank + 1) * el].contiguous()
+        ep_stats = []
+
+        def step(marks):  # noqa: F811  (EP replaces the single-GPU step)
+            ep.ep_forward(x, w_router, w_gate_up, w_down, E, k, shape.norm_topk_prob,
+                          marks=marks, stats=ep_stats)
+
     warm_marks = make_events(n_marks)
     for _ in range(args.warmup):
         flush.zero_()
@@ -281,7 +296,9 @@ def b200_arm(args, rank, world, local_rank):
     torch.cuda.synchronize()
     ops.workspace_status(ws)
     step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-    phase_names = ["router", "dispatch", "gate_up_gemm", "down_gemm", "combine"]
+    phase_names = (["router", "dispatch", "gate_up_gemm", "down_gemm", "combine"] if ep is None
+                   else ["router_dispatch", "a2a_dispatch", "local_experts", "a2a_combine",
+                         "combine"])
     phase_ms = {n: statistics.mean(m[i].elapsed_time(m[i + 1]) for m in marks)
                 for i, n in enumerate(phase_names)}
     ms = statistics.mean(step_ms)
@@ -292,7 +309,7 @@ def b200_arm(args, rank, world, local_rank):
 
     # ------------------------------------------------- end to end (public API)
     e2e = None
-    if not args.no_e2e:
+    if not args.no_e2e and ep is None:
         mod = layers.SparseMoESwiGLU(d, I, E, k, shape.norm_topk_prob).to(dev, dt)
         with torch.no_grad():
             mod.gate.weight.copy_(w_router)
@@ -325,13 +342,25 @@ def b200_arm(args, rank, world, local_rank):
     peaks = measured_peaks()
     A = T * k
     gu_flops, dn_flops = shape.gemm_flops()
-    algo = {
-        "router": ("hbm", T * d * es + E * d * es + T * k * (4 + es)),
-        "dispatch": ("hbm", T * d * es + A * d * es + A * 8),
-        "gate_up_gemm": ("tensor", gu_flops),
-        "down_gemm": ("tensor", dn_flops),
-        "combine": ("hbm", A * d * es + A * (4 + es) + T * d * es),
-    }
+    if ep is None:
+        algo = {
+            "router": ("hbm", T * d * es + E * d * es + T * k * (4 + es)),
+            "dispatch": ("hbm", T * d * es + A * d * es + A * 8),
+            "gate_up_gemm": ("tensor", gu_flops),
+            "down_gemm": ("tensor", dn_flops),
+            "combine": ("hbm", A * d * es + A * (4 + es) + T * d * es),
+        }
+    else:
+        # rows this rank received / sent per step (mean over the timed steps)
+        recv_rows = statistics.mean(sum(st.recv_rows) for st in ep_stats[-args.steps:])
+        send_rows = statistics.mean(sum(st.send_rows) for st in ep_stats[-args.steps:])
+        algo = {
+            "router_dispatch": ("hbm", T * d * es + E * d * es + T * d * es + A * d * es),
+            "a2a_dispatch": ("nvlink", send_rows * d * es),
+            "local_experts": ("tensor", 2.0 * recv_rows * d * 2 * I + 2.0 * recv_rows * I * d),
+            "a2a_combine": ("nvlink", send_rows * d * es),
+            "combine": ("hbm", A * d * es + A * (4 + es) + T * d * es),
+        }
     phases = {}
     for n in phase_names:
         bound, work = algo[n]
@@ -340,14 +369,19 @@ def b200_arm(args, rank, world, local_rank):
             ach = work / sec / 1e12
             phases[n] = {"ms": phase_ms[n], "bound": "tensor", "achieved": ach,
                          "unit": "TFLOP/s", "frac": ach / peaks["bf16_tflops"]}
+        elif bound == "nvlink":
+            ach = work / sec / 1e9
+            phases[n] = {"ms": phase_ms[n], "bound": "nvlink", "achieved": ach, "unit": "GB/s",
+                         "frac": ach / NVLINK_GBS}
         else:
             ach = work / sec / 1e9
             phases[n] = {"ms": phase_ms[n], "bound": "hbm", "achieved": ach, "unit": "GB/s",
                          "frac": ach / peaks["hbm_gbs"]}
     dom = max(phase_names, key=lambda n: phase_ms[n])
     dp = phases[dom]
+    peak_of = {"tensor": peaks["bf16_tflops"], "hbm": peaks["hbm_gbs"], "nvlink": NVLINK_GBS}
     roofline = {"kernel": dom, "bound": dp["bound"], "achieved": dp["achieved"],
-                "peak": peaks["bf16_tflops"] if dp["bound"] == "tensor" else peaks["hbm_gbs"],
+                "peak": peak_of[dp["bound"]],
                 "unit": dp["unit"], "frac": dp["frac"],
                 "peak_source": f"{peaks['source']} (burst)" if dp["bound"] == "tensor" else peaks["source"],
                 "traffic": NCU_TRAFFIC_BYTES.get(dom),
@@ -374,13 +408,15 @@ def b200_arm(args, rank, world, local_rank):
         "config": {"workload": f"{args.config}: XL 64x8 MoE-FFN layer forward "
                                f"(T={T} tokens per GPU, d={d}, E={E}, I={I}, top-{k})",
                    "tokens_per_gpu": T, "global_tokens": world * T,
-                   "parallelism": "single GPU" if world == 1 else f"replicas x{world}",
+                   "parallelism": ("single GPU" if world == 1 else
+                                   f"expert parallel x{world} ({E // world} experts per GPU, "
+                                   "NCCL all_to_all)"),
                    "l2": "256 MiB buffer rewritten before every step (outside the timed events)"},
         "roofline": roofline,
         "phases": phases,
         "cpu_baseline": cpu,
         "e2e": e2e,
-        "gpu_launches": 7 * args.steps,
+        "gpu_launches": (7 if world == 1 else 8) * args.steps,
         "clocks": clk,
     }
     print(json.dumps(line), flush=True)

@@ -71,6 +71,9 @@ SIGNATURES = {
                                     c_int32, c_int32, c_void_p, c_void_p, c_size_t, c_void_p]),
     "hmoe_grouped_swiglu": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int32, c_int32,
                                     c_int32, c_int32, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "hmoe_grouped_gemm_mapped": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int32,
+                                         c_int32, c_int32, c_int32, c_int32, c_int32, c_void_p,
+                                         c_void_p, c_size_t, c_void_p]),
     "hmoe_combine_workspace_bytes": (c_size_t, [ShapeP]),
     "hmoe_combine": (c_int, [ShapeP, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                              c_size_t, c_void_p]),

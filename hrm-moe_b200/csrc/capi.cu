@@ -210,8 +210,11 @@ int run_dispatch(const hmoe_shape& s, const int32_t* idx, const void* w, int w_i
 }
 
 int run_grouped(const void* a, const void* b, const int32_t* counts, int64_t M, int N, int K,
-                int G, int dtype, int swiglu, void* out, int* err, cudaStream_t st) {
+                int G, int dtype, int swiglu, void* out, int* err, cudaStream_t st,
+                const int32_t* group_weight = nullptr, int num_weights = 0) {
   GroupedGemmArgs g;
+  g.group_weight = group_weight;
+  g.num_weights = num_weights;
   g.a = a;
   g.b = b;
   g.counts = counts;
@@ -468,7 +471,8 @@ size_t hmoe_grouped_linear_workspace_bytes(int32_t groups) {
 
 static int grouped_common(const void* input, const void* weight, const int32_t* tpe, int64_t M,
                           int32_t N, int32_t K, int32_t G, int32_t dtype, void* output,
-                          void* workspace, size_t workspace_bytes, void* stream, int swiglu) {
+                          void* workspace, size_t workspace_bytes, void* stream, int swiglu,
+                          const int32_t* group_weight = nullptr, int32_t num_weights = 0) {
   if (M < 0 || N <= 0 || K <= 0 || G <= 0)
     return fail(HMOE_EINVAL, "bad grouped GEMM shape M=%lld N=%d K=%d G=%d", (long long)M, N, K, G);
   if (dtype != HMOE_DTYPE_BF16 && dtype != HMOE_DTYPE_F32)
@@ -487,8 +491,10 @@ static int grouped_common(const void* input, const void* weight, const int32_t* 
     HMOE_CUDA(cudaMemsetAsync(err, 0, sizeof(int), static_cast<cudaStream_t>(stream)),
               "reset error word");
   }
+  if (group_weight && num_weights <= 0)
+    return fail(HMOE_EINVAL, "a group->weight map needs the number of weights");
   return run_grouped(input, weight, tpe, M, N, K, G, dtype, swiglu, output, err,
-                     static_cast<cudaStream_t>(stream));
+                     static_cast<cudaStream_t>(stream), group_weight, num_weights);
 }
 
 int hmoe_grouped_linear(const void* input, const void* weight, const int32_t* tokens_per_expert,
@@ -504,6 +510,14 @@ int hmoe_grouped_swiglu(const void* input, const void* w_gate_up,
                         size_t workspace_bytes, void* stream) {
   return grouped_common(input, w_gate_up, tokens_per_expert, M, I, K, groups, dtype, output,
                         workspace, workspace_bytes, stream, 1);
+}
+
+int hmoe_grouped_gemm_mapped(const void* input, const void* weight, const int32_t* group_rows,
+                             const int32_t* group_weight, int64_t M, int32_t N, int32_t K,
+                             int32_t groups, int32_t num_weights, int32_t dtype, int32_t swiglu,
+                             void* output, void* workspace, size_t workspace_bytes, void* stream) {
+  return grouped_common(input, weight, group_rows, M, N, K, groups, dtype, output, workspace,
+                        workspace_bytes, stream, swiglu ? 1 : 0, group_weight, num_weights);
 }
 
 size_t hmoe_combine_workspace_bytes(const hmoe_shape* shape) {

@@ -24,8 +24,8 @@ constexpr int kSMaxGroups = 1024;
 template <bool SWIGLU>
 __global__ void __launch_bounds__(kSThreads)
 grouped_gemm_simt_kernel(const float* __restrict__ A, const float* __restrict__ B,
-                         const int32_t* __restrict__ counts, int G, int64_t M, int N, int K,
-                         int n_tiles, float* __restrict__ out) {
+                         const int32_t* __restrict__ counts, const int32_t* __restrict__ gweight,
+                         int G, int64_t M, int N, int K, int n_tiles, float* __restrict__ out) {
   __shared__ int group_rows[kSMaxGroups + 1];
   __shared__ int tile_prefix[kSMaxGroups + 1];
   __shared__ __align__(16) float As[SK][SM_];
@@ -73,7 +73,7 @@ grouped_gemm_simt_kernel(const float* __restrict__ A, const float* __restrict__ 
   const int nrows = min(SM_, group_rows[g + 1] - row0);
   const int col0 = n * SN;
   const int nw = SWIGLU ? 2 * N : N;
-  const float* Bg = B + static_cast<int64_t>(g) * nw * K;
+  const float* Bg = B + static_cast<int64_t>(gweight ? gweight[g] : g) * nw * K;
 
   const int ty = tid >> 4, tx = tid & 15;
   float acc[4][4], accu[4][4];
@@ -158,10 +158,10 @@ cudaError_t launch_grouped_gemm_simt(const GroupedGemmArgs& a, cudaStream_t stre
   float* out = static_cast<float*>(a.out);
   if (a.swiglu)
     grouped_gemm_simt_kernel<true><<<static_cast<unsigned>(grid), kSThreads, 0, stream>>>(
-        A, B, a.counts, a.G, a.M, a.N, a.K, n_tiles, out);
+        A, B, a.counts, a.group_weight, a.G, a.M, a.N, a.K, n_tiles, out);
   else
     grouped_gemm_simt_kernel<false><<<static_cast<unsigned>(grid), kSThreads, 0, stream>>>(
-        A, B, a.counts, a.G, a.M, a.N, a.K, n_tiles, out);
+        A, B, a.counts, a.group_weight, a.G, a.M, a.N, a.K, n_tiles, out);
   return cudaGetLastError();
 }
 

@@ -67,6 +67,7 @@ struct SmemCtl {
   int pad_;
   int group_rows[kMaxGroups + 1];   // exclusive prefix of rows
   int tile_prefix[kMaxGroups + 1];  // exclusive prefix of 128-row blocks
+  int group_w[kMaxGroups];          // weight (expert) index of each group
 };
 
 constexpr size_t kSmemBytes =
@@ -75,6 +76,7 @@ static_assert(kSmemBytes <= 232448, "shared memory budget of one sm_100 CTA");
 
 struct KParams {
   const int32_t* counts;
+  const int32_t* group_weight;  // [G] weight index per group, or null (= g)
   int G;
   int64_t M;
   int N;                    // output columns
@@ -182,6 +184,7 @@ grouped_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
       const int c = max(0, p.counts[g]);
       ctl.group_rows[g] = rr;
       ctl.tile_prefix[g] = tr;
+      ctl.group_w[g] = p.group_weight ? p.group_weight[g] : g;
       rr += c;
       tr += cdiv(c, BM);
     }
@@ -229,7 +232,7 @@ grouped_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
       for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
         int g, row0, nrows, n;
         decode_tile(ctl, G, p.n_tiles, tile, g, row0, nrows, n);
-        const int rb0 = g * p.b_rows_per_group + n * p.out_cols_per_tile;
+        const int rb0 = ctl.group_w[g] * p.b_rows_per_group + n * p.out_cols_per_tile;
         const int rb1 = rb0 + p.b_second_off;
         for (int kb = 0; kb < nkb; ++kb) {
           if (!mbar_wait_bounded(smem_u32(&ctl.empty[stage]), phase ^ 1u, abort, p.err, lim)) {
@@ -435,17 +438,19 @@ cudaError_t ensure_smem_attr() {
 cudaError_t launch_grouped_gemm_sm100(const GroupedGemmArgs& a, cudaStream_t stream) {
   if (a.M == 0 || a.G == 0) return cudaSuccess;
   if (a.G > kMaxGroups || a.K % 8 != 0 || a.N % 8 != 0) return cudaErrorInvalidValue;
-  const int nw = a.swiglu ? 2 * a.N : a.N;          // rows of B per group
+  const int nw = a.swiglu ? 2 * a.N : a.N;          // rows of B per weight
+  const int nweights = a.num_weights > 0 ? a.num_weights : a.G;
   CUtensorMap ma, mb, mc;
   if (!make_map(&ma, a.a, static_cast<uint64_t>(a.M), static_cast<uint64_t>(a.K), BM, BK,
                 CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !make_map(&mb, a.b, static_cast<uint64_t>(a.G) * nw, static_cast<uint64_t>(a.K), BNH, BK,
+      !make_map(&mb, a.b, static_cast<uint64_t>(nweights) * nw, static_cast<uint64_t>(a.K), BNH, BK,
                 CU_TENSOR_MAP_SWIZZLE_128B) ||
       !make_map(&mc, a.out, static_cast<uint64_t>(a.M), static_cast<uint64_t>(a.N), 32, 32,
                 CU_TENSOR_MAP_SWIZZLE_64B))
     return cudaErrorInvalidValue;
   KParams p;
   p.counts = a.counts;
+  p.group_weight = a.group_weight;
   p.G = a.G;
   p.M = a.M;
   p.N = a.N;

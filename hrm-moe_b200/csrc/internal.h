@@ -60,6 +60,8 @@ struct GroupedGemmArgs {
   const void* a;             // [M, K]
   const void* b;             // [G, Nw, K]  (Nw = 2N for swiglu, N otherwise)
   const int32_t* counts;     // [G] rows per group, device
+  const int32_t* group_weight = nullptr;  // [G] weight index per group (null = g)
+  int num_weights = 0;       // weights in b (0 = G)
   void* out;                 // [M, N]
   int64_t M;
   int N;                     // output columns

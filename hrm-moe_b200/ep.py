@@ -1,0 +1,160 @@
+"""Expert parallelism for the routed MoE FFN over torch.distributed (NCCL).
+
+Mirrors SparseMoEExpertParallel (models/layers.py:383-478): experts are
+sharded contiguously (rank r owns [r*E/R, (r+1)*E/R), layers.py:403-405),
+every rank routes its own tokens, rows travel to the rank that owns their
+expert, the owner runs its local experts, and the outputs travel back.
+
+Differences from the reference, by design:
+* dispatch sorts by *global* expert once (the layer's own stable dispatch).
+  Experts are contiguous per rank, so the sorted rows are already grouped by
+  destination and the send buffer is the gathered row buffer itself;
+* the owner runs its experts straight on the received rows, grouped by
+  (source rank, local expert), with a group -> weight map instead of a
+  second sort (layers.py:462-468 re-sorts);
+* returned rows land at the positions the dispatch gave them, so the combine
+  is the single-GPU combine and the result is bit-identical to one GPU
+  running all experts (the reference re-sorts to match, layers.py:474-476).
+
+Collectives per call: one all_to_all of per-expert counts (E/R per peer),
+one host read of the split sizes (NCCL's variable all_to_all takes host
+splits, as in the reference, layers.py:363-364), then the row all_to_all
+each way.  The compute stages are a parameter so the same orchestration runs
+on CPU ranks (gloo) in tests.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+from . import ops
+
+
+class CudaCompute:
+    """The stages on this GPU, through the C ABI."""
+
+    def router(self, x, w_router, bias, top_k, norm):
+        return ops.router_topk(x, w_router, top_k, norm, bias)
+
+    def dispatch(self, idx, num_experts, x, w):
+        out = ops.dispatch(idx, num_experts, x, w)
+        return out["sort_idx"], out["counts"], out["x_sorted"]
+
+    def local_experts(self, rows, w_gate_up, w_down, group_rows, group_weight):
+        h = ops.grouped_gemm_mapped(rows, w_gate_up, group_rows, group_weight, swiglu=True)
+        return ops.grouped_gemm_mapped(h, w_down, group_rows, group_weight, swiglu=False)
+
+    def combine(self, y_sorted, sort_idx, w, final):
+        return ops.combine(y_sorted, sort_idx, w, final)
+
+
+@dataclass
+class EPStats:
+    send_rows: list
+    recv_rows: list
+
+
+def ep_forward(x: torch.Tensor, w_router: torch.Tensor, w_gate_up_local: torch.Tensor,
+               w_down_local: torch.Tensor, num_experts: int, top_k: int, norm_topk_prob: bool,
+               group=None, router_bias: Optional[torch.Tensor] = None, compute=None,
+               stats: Optional[list] = None, marks: Optional[list] = None) -> torch.Tensor:
+    """Expert-parallel MoE-FFN forward of this rank's tokens x [T, d].
+
+    ``marks`` (optional, 6 CUDA events) are recorded before the router, after
+    dispatch, after the row exchange, after the local experts, after the
+    return exchange and after the combine.
+    """
+    compute = compute or CudaCompute()
+
+    def mark(i):
+        if marks is not None:
+            marks[i].record()
+
+    mark(0)
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    if num_experts % world:
+        raise ValueError(f"num_experts={num_experts} must be divisible by world_size={world}")
+    el = num_experts // world
+    if w_gate_up_local.shape[0] != el or w_down_local.shape[0] != el:
+        raise ValueError(f"rank {rank} holds {w_gate_up_local.shape[0]} experts, expected {el}")
+    T, d = x.shape
+    dev = x.device
+    if T > 0:
+        idx, w = compute.router(x, w_router, router_bias, top_k, norm_topk_prob)
+        sort_idx, counts, x_sorted = compute.dispatch(idx, num_experts, x, w)
+    else:
+        idx = torch.empty((0, top_k), dtype=torch.int32, device=dev)
+        w = torch.empty((0, top_k), dtype=x.dtype, device=dev)
+        sort_idx = torch.empty(0, dtype=torch.int32, device=dev)
+        counts = torch.zeros(num_experts, dtype=torch.int32, device=dev)
+        x_sorted = x.new_empty((0, d))
+    mark(1)
+    # counts of my experts from every source: recv_counts[s * el + e]
+    counts = counts.to(torch.int32).contiguous()
+    recv_counts = torch.empty_like(counts)
+    dist.all_to_all_single(recv_counts, counts, group=group)
+    splits = torch.cat([counts.view(world, el).sum(1), recv_counts.view(world, el).sum(1)])
+    splits = splits.cpu().tolist()
+    send_splits, recv_splits = splits[:world], splits[world:]
+    if stats is not None:
+        stats.append(EPStats(send_splits, recv_splits))
+    recv_rows = x.new_empty((sum(recv_splits), d))
+    dist.all_to_all_single(recv_rows, x_sorted.contiguous(), recv_splits, send_splits, group=group)
+    mark(2)
+    group_weight = torch.arange(world * el, device=dev, dtype=torch.int32) % el
+    if recv_rows.shape[0] > 0:
+        y_rows = compute.local_experts(recv_rows, w_gate_up_local, w_down_local, recv_counts,
+                                       group_weight)
+    else:
+        y_rows = recv_rows
+    mark(3)
+    back = x.new_empty((int(sum(send_splits)), d))
+    dist.all_to_all_single(back, y_rows.contiguous(), send_splits, recv_splits, group=group)
+    mark(4)
+    y = torch.zeros_like(x)
+    if T > 0:
+        compute.combine(back, sort_idx, w, y)
+    mark(5)
+    return y
+
+
+class SparseMoEExpertParallelSwiGLU(torch.nn.Module):
+    """SparseMoESwiGLU(implementation="grouped_ep") with the B200 kernels.
+
+    Parameters follow the reference's expert-parallel layout
+    (models/layers.py:406): ``gate.weight`` [E, d] replicated,
+    ``experts.local_experts.gate_up_weight`` [E/R, 2I, d] and
+    ``experts.local_experts.down_weight`` [E/R, d, I] for this rank's experts.
+    """
+
+    def __init__(self, hidden_size: int, intermediate_size: int, num_experts: int, top_k: int,
+                 norm_topk_prob: bool, group=None, **kwargs):
+        super().__init__()
+        from .layers import LinearInit, SparseMoEGroupedExperts
+        world = dist.get_world_size(group) if dist.is_initialized() else 1
+        if num_experts % world:
+            raise ValueError(f"num_experts={num_experts} must divide world_size={world}")
+        self.group = group
+        self.hidden_size = hidden_size
+        self.num_experts = num_experts
+        self.top_k = top_k
+        self.norm_topk_prob = norm_topk_prob
+        self.gate = LinearInit(hidden_size, num_experts, bias=False, **kwargs)
+        self.experts = torch.nn.Module()
+        self.experts.local_experts = SparseMoEGroupedExperts(hidden_size, intermediate_size,
+                                                             num_experts // world, **kwargs)
+
+    def forward(self, x, moe_context=None, total_seqlen=None, **_seq_info):
+        from .layers import _check_no_grad
+        le = self.experts.local_experts
+        _check_no_grad(x, self.gate.weight, le.gate_up_weight, le.down_weight)
+        shape = x.shape
+        h = x.reshape(-1, self.hidden_size)
+        y = ep_forward(h, self.gate.weight.to(h.dtype), le.gate_up_weight.to(h.dtype),
+                       le.down_weight.to(h.dtype), self.num_experts, self.top_k,
+                       self.norm_topk_prob, group=self.group)
+        return y.reshape(shape)

@@ -183,6 +183,36 @@ def grouped_swiglu(input: torch.Tensor, w_gate_up: torch.Tensor,
     return _grouped(input, w_gate_up, tokens_per_expert, swiglu=True)
 
 
+def grouped_gemm_mapped(input: torch.Tensor, weight: torch.Tensor, group_rows: torch.Tensor,
+                        group_weight: torch.Tensor, swiglu: bool) -> torch.Tensor:
+    """Grouped GEMM where group g uses weight[group_weight[g]].
+
+    The local expert step of the expert-parallel layer
+    (models/layers.py:462-468): received rows are grouped by (source rank,
+    local expert), so several groups share one expert's weight.
+    """
+    M, K = input.shape
+    NW = weight.shape[1]
+    N = NW // 2 if swiglu else NW
+    if M == 0:
+        return input.new_empty((0, N))
+    dev = _require_cuda(input, weight, group_rows, group_weight)
+    if weight.shape[2] != K:
+        raise ValueError(f"grouped GEMM K mismatch: input K={K}, weight K={weight.shape[2]}")
+    code = dtype_code(input.dtype)
+    G = group_rows.numel()
+    rows = group_rows.to(device=dev, dtype=torch.int32).contiguous()
+    gw = group_weight.to(device=dev, dtype=torch.int32).contiguous()
+    input, weight = input.contiguous(), weight.contiguous()
+    out = torch.empty((M, N), dtype=input.dtype, device=dev)
+    lib = _lib.load()
+    ws = _workspace(lib.hmoe_grouped_linear_workspace_bytes(G), dev)
+    _lib.check(lib.hmoe_grouped_gemm_mapped(_ptr(input), _ptr(weight), _ptr(rows), _ptr(gw), M, N,
+                                            K, G, weight.shape[0], code, 1 if swiglu else 0,
+                                            _ptr(out), _ptr(ws), ws.numel(), _stream(dev)))
+    return out
+
+
 # ----------------------------------------------------------------- combine --
 def combine(expert_out: torch.Tensor, sort_idx: torch.Tensor, topk_weight: torch.Tensor,
             final_hidden_states: torch.Tensor) -> torch.Tensor:

@@ -156,6 +156,20 @@ int hmoe_grouped_swiglu(const void* input, const void* w_gate_up,
                         void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Grouped GEMM over groups that reuse weights: group g (group_rows[g] rows,
+ * contiguous in order) is multiplied by weight[group_weight[g]] (of
+ * num_weights).  swiglu = 0: output [M, N] = rows @ W^T with W [N, K];
+ * swiglu = 1: the fused gate_up + SiLU*up with W [2N, K], output [M, N].
+ * This is the local expert computation of the expert-parallel backend
+ * (models/layers.py:462-468), where the received rows arrive grouped by
+ * (source rank, local expert) (layers.py:456-460).
+ */
+int hmoe_grouped_gemm_mapped(const void* input, const void* weight, const int32_t* group_rows,
+                             const int32_t* group_weight, int64_t M, int32_t N, int32_t K,
+                             int32_t groups, int32_t num_weights, int32_t dtype, int32_t swiglu,
+                             void* output, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * Combine (models/layers.py:332-334): for every token t,
  *   final[t] += sum_j topk_weight[t, j] * expert_out[pos(t, j)]
  * where pos is the inverse of sort_idx (sort_idx[pos(t,j)] = t*k + j).

@@ -1,0 +1,64 @@
+"""torchrun worker for the multi-GPU expert-parallel test (tests/test_gpu_ep.py).
+
+Every rank routes its own seeded tokens through ep.ep_forward (NCCL) and
+through the single-GPU layer with all experts; the two must agree bit for
+bit, because the rows meet the same kernels and the combine sees them in the
+same order.  Writes one line per rank to the file named by argv[1].
+"""
+import datetime
+import importlib
+import os
+import sys
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+
+
+def main(out_path):
+    rank = int(os.environ["RANK"])
+    world = int(os.environ["WORLD_SIZE"])
+    local = int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    ok = True
+    msgs = []
+    try:
+        syn = importlib.import_module("hrm-moe_b200.synthetic")
+        ep = importlib.import_module("hrm-moe_b200.ep")
+        ops = importlib.import_module("hrm-moe_b200.ops")
+        for (T, d, E, I, k, skew) in [(1000, 256, 8 * world, 128, 4, False),
+                                       (4096, 1536, 64, 512, 8, False),
+                                       (777, 256, 4 * world, 64, 2, True)]:
+            shape = syn.MoEShape(T + 37 * rank, d, E, I, k, True, "bf16")
+            inp = syn.make_inputs(shape, seed=21, rank=rank)
+            wr = inp.w_router
+            if skew:  # pile the traffic onto the last rank's experts
+                el = E // world
+                wr = syn.round_to_bf16(wr + np.concatenate(
+                    [np.zeros(((world - 1) * el, d), np.float32), np.full((el, d), 0.03, np.float32)]))
+            t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev).bfloat16()
+            el = E // world
+            y_ep = ep.ep_forward(t(inp.x), t(wr), t(inp.w_gate_up[rank * el:(rank + 1) * el]),
+                                 t(inp.w_down[rank * el:(rank + 1) * el]), E, k, True)
+            y_1 = ops.ffn_forward(t(inp.x), t(wr), t(inp.w_gate_up), t(inp.w_down), k, True)
+            torch.cuda.synchronize()
+            same = torch.equal(y_ep, y_1)
+            ok &= same
+            msgs.append(f"T={shape.tokens} E={E} skew={skew}: {'equal' if same else 'DIFFER max %g' % (y_ep.float() - y_1.float()).abs().max().item()}")
+        dist.barrier()
+    except Exception as e:  # report, then leave the group cleanly
+        ok = False
+        msgs.append(f"error {type(e).__name__}: {e}")
+    finally:
+        dist.destroy_process_group()
+    with open(out_path, "a") as f:
+        f.write(f"rank {rank}/{world} {'OK' if ok else 'FAIL'} " + "; ".join(msgs) + "\n")
+
+
+if __name__ == "__main__":
+    main(sys.argv[1])
