@@ -54,6 +54,9 @@ SIGNATURES = {
     "hmoe_ffn_forward": (c_int, [ShapeP, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                  c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p,
                                  c_void_p, c_size_t, c_void_p]),
+    "hmoe_ffn_host_workspace_bytes": (c_size_t, [ShapeP, c_int64]),
+    "hmoe_ffn_forward_host": (c_int, [ShapeP, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                      c_void_p, c_int64, c_void_p, c_size_t, c_void_p]),
     "hmoe_ffn_forward_marked": (c_int, [ShapeP, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                         c_void_p, c_int, c_void_p, c_size_t, c_void_p,
                                         ctypes.POINTER(c_void_p)]),

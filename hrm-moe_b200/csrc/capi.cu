@@ -203,7 +203,7 @@ int run_dispatch(const hmoe_shape& s, const int32_t* idx, const void* w, int w_i
   HMOE_CUDA(launch_hist_rank(idx, s.tokens, s.top_k, s.experts, b.local_rank, b.block_counts,
                              b.err, st), "hist_rank");
   HMOE_CUDA(launch_scan(b.block_counts, nblk, s.experts, b.counts, b.offsets, st), "scan");
-  HMOE_CUDA(launch_permute_gather(idx, b.local_rank, b.block_counts, w, w_is_f32, x, s.tokens,
+  HMOE_CUDA(launch_permute_gather(idx, b.local_rank, b.block_counts, b.counts, w, w_is_f32, x, s.tokens,
                                   s.hidden, s.top_k, s.experts, s.dtype, pos, sort_idx,
                                   sorted_token, sorted_w, x_sorted, st), "permute_gather");
   return HMOE_OK;
@@ -372,6 +372,112 @@ int ffn_forward_impl(const hmoe_shape* shape, const void* x, const void* w_route
 }  // namespace
 
 extern "C" {
+
+// ------------------------------------------------- host-buffer pipeline ----
+namespace {
+struct HostPipe {
+  cudaStream_t in = nullptr, out = nullptr;
+  cudaEvent_t x_ready[2], x_free[2], y_ready[2], y_free[2], done;
+  bool ok = false;
+};
+
+int host_pipe(int dev, HostPipe** out) {
+  static HostPipe pipes[64];
+  static std::mutex mu;
+  if (dev < 0 || dev >= 64) return fail(HMOE_EINVAL, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lock(mu);
+  HostPipe& p = pipes[dev];
+  if (!p.ok) {
+    HMOE_CUDA(cudaStreamCreateWithFlags(&p.in, cudaStreamNonBlocking), "cudaStreamCreate");
+    HMOE_CUDA(cudaStreamCreateWithFlags(&p.out, cudaStreamNonBlocking), "cudaStreamCreate");
+    for (int i = 0; i < 2; ++i) {
+      HMOE_CUDA(cudaEventCreateWithFlags(&p.x_ready[i], cudaEventDisableTiming), "cudaEventCreate");
+      HMOE_CUDA(cudaEventCreateWithFlags(&p.x_free[i], cudaEventDisableTiming), "cudaEventCreate");
+      HMOE_CUDA(cudaEventCreateWithFlags(&p.y_ready[i], cudaEventDisableTiming), "cudaEventCreate");
+      HMOE_CUDA(cudaEventCreateWithFlags(&p.y_free[i], cudaEventDisableTiming), "cudaEventCreate");
+    }
+    HMOE_CUDA(cudaEventCreateWithFlags(&p.done, cudaEventDisableTiming), "cudaEventCreate");
+    p.ok = true;
+  }
+  *out = &p;
+  return HMOE_OK;
+}
+
+hmoe_shape chunk_shape(const hmoe_shape& s, int64_t tokens) {
+  hmoe_shape c = s;
+  c.tokens = tokens;
+  return c;
+}
+}  // namespace
+
+size_t hmoe_ffn_host_workspace_bytes(const hmoe_shape* shape, int64_t chunk_tokens) {
+  if (validate_shape(shape) != HMOE_OK || chunk_tokens <= 0) return 0;
+  const hmoe_shape c = chunk_shape(*shape, chunk_tokens);
+  const size_t row = elem_size(shape->dtype) * shape->hidden;
+  return 4 * align_up(row * chunk_tokens) + hmoe_ffn_workspace_bytes(&c);
+}
+
+int hmoe_ffn_forward_host(const hmoe_shape* shape, const void* x_host, const void* w_router,
+                          const void* router_bias, const void* w_gate_up, const void* w_down,
+                          void* y_host, int64_t chunk_tokens, void* workspace,
+                          size_t workspace_bytes, void* stream) {
+  int rc = validate_shape(shape);
+  if (rc) return rc;
+  const hmoe_shape& s = *shape;
+  if (s.tokens == 0) return HMOE_OK;
+  if (chunk_tokens <= 0) return fail(HMOE_EINVAL, "chunk_tokens must be positive");
+  if (!x_host || !y_host || !w_router || !w_gate_up || !w_down)
+    return fail(HMOE_EINVAL, "x_host, y_host and the weights are required");
+  if ((rc = select_device(w_gate_up))) return rc;
+  const size_t need = hmoe_ffn_host_workspace_bytes(shape, chunk_tokens);
+  if ((rc = check_ws(workspace, workspace_bytes, need))) return rc;
+  int dev = 0;
+  HMOE_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+  HostPipe* hp = nullptr;
+  if ((rc = host_pipe(dev, &hp))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t row = elem_size(s.dtype) * s.hidden;
+  const size_t buf = align_up(row * chunk_tokens);
+  char* base = static_cast<char*>(workspace);
+  char* xb[2] = {base, base + buf};
+  char* yb[2] = {base + 2 * buf, base + 3 * buf};
+  void* ffn_ws = base + 4 * buf;
+  const size_t ffn_bytes = workspace_bytes - 4 * buf;
+  // the buffers start free once the caller's earlier work on `stream` is done
+  for (int i = 0; i < 2; ++i) {
+    HMOE_CUDA(cudaEventRecord(hp->x_free[i], st), "cudaEventRecord");
+    HMOE_CUDA(cudaEventRecord(hp->y_free[i], st), "cudaEventRecord");
+  }
+  const int64_t nchunks = cdiv64(s.tokens, chunk_tokens);
+  for (int64_t c = 0; c < nchunks; ++c) {
+    const int i = static_cast<int>(c & 1);
+    const int64_t t0 = c * chunk_tokens;
+    const int64_t tc = (t0 + chunk_tokens <= s.tokens) ? chunk_tokens : s.tokens - t0;
+    // H2D of this chunk once the compute of chunk c-2 stopped reading the buffer
+    HMOE_CUDA(cudaStreamWaitEvent(hp->in, hp->x_free[i], 0), "cudaStreamWaitEvent");
+    HMOE_CUDA(cudaMemcpyAsync(xb[i], static_cast<const char*>(x_host) + t0 * row, tc * row,
+                              cudaMemcpyHostToDevice, hp->in), "H2D chunk");
+    HMOE_CUDA(cudaEventRecord(hp->x_ready[i], hp->in), "cudaEventRecord");
+    // compute once the rows are in and the D2H of chunk c-2 freed the output
+    HMOE_CUDA(cudaStreamWaitEvent(st, hp->x_ready[i], 0), "cudaStreamWaitEvent");
+    HMOE_CUDA(cudaStreamWaitEvent(st, hp->y_free[i], 0), "cudaStreamWaitEvent");
+    const hmoe_shape cs = chunk_shape(s, tc);
+    rc = hmoe_ffn_forward(&cs, xb[i], w_router, router_bias, w_gate_up, w_down, yb[i], 0, nullptr,
+                          nullptr, nullptr, nullptr, ffn_ws, ffn_bytes, st);
+    if (rc) return rc;
+    HMOE_CUDA(cudaEventRecord(hp->x_free[i], st), "cudaEventRecord");
+    HMOE_CUDA(cudaEventRecord(hp->y_ready[i], st), "cudaEventRecord");
+    // D2H of the result
+    HMOE_CUDA(cudaStreamWaitEvent(hp->out, hp->y_ready[i], 0), "cudaStreamWaitEvent");
+    HMOE_CUDA(cudaMemcpyAsync(static_cast<char*>(y_host) + t0 * row, yb[i], tc * row,
+                              cudaMemcpyDeviceToHost, hp->out), "D2H chunk");
+    HMOE_CUDA(cudaEventRecord(hp->y_free[i], hp->out), "cudaEventRecord");
+  }
+  // the call completes, in stream order, on the caller's stream
+  HMOE_CUDA(cudaEventRecord(hp->done, hp->out), "cudaEventRecord");
+  HMOE_CUDA(cudaStreamWaitEvent(st, hp->done, 0), "cudaStreamWaitEvent");
+  return HMOE_OK;
+}
 
 size_t hmoe_router_workspace_bytes(const hmoe_shape* shape) {
   return plan_bytes(shape, [](Carve& c, const hmoe_shape& s) {

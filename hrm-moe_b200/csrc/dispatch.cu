@@ -10,10 +10,11 @@
 //  1. hist_rank: each block of tokens counts its assignments per expert and
 //     gives every assignment its rank among same-expert assignments of the
 //     block with a smaller flat index (warp __match_any_sync + chunk scan).
-//  2. scan: block counts -> absolute row offset of (expert, block), plus
-//     tokens_per_expert.
-//  3. permute_gather: position = offset(expert, block) + rank; one warp per
-//     token reads its hidden row once and writes it to its k positions.
+//  2. scan (one CTA per expert): block counts -> row offset of (expert,
+//     block) inside the expert, plus tokens_per_expert.
+//  3. permute_gather: position = base(expert) + offset(expert, block) + rank
+//     (each CTA scans the E counts for the bases); one warp per token reads
+//     its hidden row once and writes it to its k positions.
 #include "common.cuh"
 #include "internal.h"
 
@@ -79,48 +80,81 @@ hist_rank_kernel(const int32_t* __restrict__ topk_idx, int64_t T, int k, int E, 
   }
 }
 
-// One CTA: per expert, exclusive scan of its block counts (in place), then
-// an exclusive scan over expert totals, then absolute offsets.
-constexpr int kScanThreads = 1024;
+// One CTA per expert: exclusive scan of the expert's block counts (in place,
+// relative to the expert's first row) and its total -> counts[e].  The
+// expert bases (a scan over E totals) are formed where they are used.
+constexpr int kScanThreads = 256;
+constexpr int kScanPer = 8;  // block counts per thread and pass
 
 __global__ void __launch_bounds__(kScanThreads)
-scan_kernel(int32_t* __restrict__ block_counts, int64_t nblk, int E,
-            int32_t* __restrict__ counts, int32_t* __restrict__ expert_offsets) {
-  __shared__ int32_t totals[kMaxExperts];
-  __shared__ int32_t base[kMaxExperts + 1];
+scan_kernel(int32_t* __restrict__ block_counts, int64_t nblk, int E, int32_t* __restrict__ counts) {
+  __shared__ int32_t warp_tot[kScanThreads / 32];
+  __shared__ int32_t carry_s;
+  const int e = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  for (int e = warp; e < E; e += kScanThreads / 32) {
-    int carry = 0;
-    for (int64_t b0 = 0; b0 < nblk; b0 += 32) {
-      const int64_t b = b0 + lane;
-      const int v = b < nblk ? block_counts[b * E + e] : 0;
-      int incl = v;
+  if (tid == 0) carry_s = 0;
+  __syncthreads();
+  for (int64_t b0 = 0; b0 < nblk; b0 += kScanThreads * kScanPer) {
+    int v[kScanPer];
+    int sum = 0;
 #pragma unroll
-      for (int off = 1; off < 32; off <<= 1) {
-        const int o = __shfl_up_sync(0xffffffffu, incl, off);
-        if (lane >= off) incl += o;
-      }
-      if (b < nblk) block_counts[b * E + e] = carry + incl - v;
-      carry += __shfl_sync(0xffffffffu, incl, 31);
+    for (int i = 0; i < kScanPer; ++i) {
+      const int64_t b = b0 + static_cast<int64_t>(tid) * kScanPer + i;
+      v[i] = b < nblk ? block_counts[b * E + e] : 0;
+      sum += v[i];
     }
-    if (lane == 0) totals[e] = carry;
+    int incl = sum;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int o = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += o;
+    }
+    if (lane == 31) warp_tot[warp] = incl;
+    __syncthreads();
+    int before = carry_s;
+    for (int w = 0; w < warp; ++w) before += warp_tot[w];
+    int run = before + incl - sum;
+#pragma unroll
+    for (int i = 0; i < kScanPer; ++i) {
+      const int64_t b = b0 + static_cast<int64_t>(tid) * kScanPer + i;
+      if (b < nblk) block_counts[b * E + e] = run;
+      run += v[i];
+    }
+    __syncthreads();
+    if (tid == kScanThreads - 1) carry_s = run;
+    __syncthreads();
+  }
+  if (tid == 0) counts[e] = carry_s;
+}
+
+// Exclusive scan of counts[0..E) into smem base[0..E] by warp 0 (E <= 128).
+__device__ __forceinline__ void expert_bases(const int32_t* __restrict__ counts, int E,
+                                             int32_t* base) {
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    int c[4], s = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int e = lane * 4 + i;
+      c[i] = e < E ? counts[e] : 0;
+      s += c[i];
+    }
+    int incl = s;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int o = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += o;
+    }
+    int run = incl - s;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int e = lane * 4 + i;
+      if (e <= E) base[e] = run;
+      run += c[i];
+    }
+    if (lane == 31 && 128 <= E) base[E] = run;
   }
   __syncthreads();
-  if (tid == 0) {
-    int run = 0;
-    for (int e = 0; e < E; ++e) {
-      base[e] = run;
-      run += totals[e];
-    }
-    base[E] = run;
-  }
-  __syncthreads();
-  if (tid < E) {
-    if (counts) counts[tid] = totals[tid];
-  }
-  if (tid <= E && expert_offsets) expert_offsets[tid] = base[tid];
-  const int64_t n = nblk * E;
-  for (int64_t i = tid; i < n; i += kScanThreads) block_counts[i] += base[i % E];
 }
 
 // One warp per token.  Row bytes must be a multiple of 16.
@@ -129,11 +163,14 @@ constexpr int kPermSeg = 8;  // 16-byte chunks per lane held in registers at a t
 
 __global__ void __launch_bounds__(kPermThreads)
 permute_gather_kernel(const int32_t* __restrict__ topk_idx, const int32_t* __restrict__ local_rank,
-                      const int32_t* __restrict__ block_offsets, const void* __restrict__ topk_w,
+                      const int32_t* __restrict__ block_offsets, const int32_t* __restrict__ counts,
+                      const void* __restrict__ topk_w,
                       int topk_w_is_f32, const void* __restrict__ x, int64_t T, int row_chunks,
                       int k, int E, int tblk, int dtype, int32_t* __restrict__ pos,
                       int32_t* __restrict__ sort_idx, int32_t* __restrict__ sorted_token,
                       void* __restrict__ sorted_w, uint4* __restrict__ x_sorted) {
+  __shared__ int32_t base[kMaxExperts + 1];
+  expert_bases(counts, E, base);
   const int lane = threadIdx.x & 31;
   const int64_t t = static_cast<int64_t>(blockIdx.x) * (kPermThreads / 32) + (threadIdx.x >> 5);
   if (t >= T) return;
@@ -145,7 +182,7 @@ permute_gather_kernel(const int32_t* __restrict__ topk_idx, const int32_t* __res
     const int e = topk_idx[f];
     const int r = local_rank[f];
     if (e >= 0 && e < E && r >= 0) {
-      p = block_offsets[blk * E + e] + r;
+      p = base[e] + block_offsets[blk * E + e] + r;
       if (sort_idx) sort_idx[p] = static_cast<int32_t>(f);
       if (sorted_token) sorted_token[p] = static_cast<int32_t>(t);
       if (sorted_w) {
@@ -205,13 +242,14 @@ cudaError_t launch_hist_rank(const int32_t* topk_idx, int64_t T, int k, int E,
 }
 
 cudaError_t launch_scan(int32_t* block_counts, int64_t nblk, int E, int32_t* counts,
-                        int32_t* expert_offsets, cudaStream_t stream) {
-  scan_kernel<<<1, kScanThreads, 0, stream>>>(block_counts, nblk, E, counts, expert_offsets);
+                        int32_t* /*expert_offsets*/, cudaStream_t stream) {
+  scan_kernel<<<E, kScanThreads, 0, stream>>>(block_counts, nblk, E, counts);
   return cudaGetLastError();
 }
 
 cudaError_t launch_permute_gather(const int32_t* topk_idx, const int32_t* local_rank,
-                                  const int32_t* block_offsets, const void* topk_w,
+                                  const int32_t* block_offsets, const int32_t* counts,
+                                  const void* topk_w,
                                   int topk_w_is_f32, const void* x, int64_t T, int d, int k,
                                   int E, int dtype, int32_t* pos, int32_t* sort_idx,
                                   int32_t* sorted_token, void* sorted_w, void* x_sorted,
@@ -221,7 +259,7 @@ cudaError_t launch_permute_gather(const int32_t* topk_idx, const int32_t* local_
   const int row_chunks = d * es / 16;
   const int64_t blocks = cdiv64(T, kPermThreads / 32);
   permute_gather_kernel<<<static_cast<unsigned>(blocks), kPermThreads, 0, stream>>>(
-      topk_idx, local_rank, block_offsets, topk_w, topk_w_is_f32, x, T, row_chunks, k, E,
+      topk_idx, local_rank, block_offsets, counts, topk_w, topk_w_is_f32, x, T, row_chunks, k, E,
       dispatch_block_tokens(k), dtype, pos, sort_idx, sorted_token, sorted_w,
       static_cast<uint4*>(x_sorted));
   return cudaGetLastError();

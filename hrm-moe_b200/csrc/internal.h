@@ -35,12 +35,14 @@ int64_t dispatch_num_blocks(int64_t T, int k);
 cudaError_t launch_hist_rank(const int32_t* topk_idx, int64_t T, int k, int E,
                              int32_t* local_rank, int32_t* block_counts, int* err,
                              cudaStream_t stream);
-// In place: block_counts -> absolute row offsets; counts[E], expert_offsets[E+1].
+// In place: block_counts -> row offsets inside each expert; counts[E].
+// (expert_offsets is unused and may be null.)
 cudaError_t launch_scan(int32_t* block_counts, int64_t nblk, int E, int32_t* counts,
                         int32_t* expert_offsets, cudaStream_t stream);
 // pos[T*k] and (optionally) sort_idx, sorted_token, sorted weights, x_sorted.
 cudaError_t launch_permute_gather(const int32_t* topk_idx, const int32_t* local_rank,
-                                  const int32_t* block_offsets, const void* topk_w,
+                                  const int32_t* block_offsets, const int32_t* counts,
+                                  const void* topk_w,
                                   int topk_w_is_f32, const void* x, int64_t T, int d, int k,
                                   int E, int dtype, int32_t* pos, int32_t* sort_idx,
                                   int32_t* sorted_token, void* sorted_w, void* x_sorted,

@@ -102,7 +102,7 @@ extern "C" int hmoe_dispatch_noalloc(const hmoe_shape* shape, const int32_t* top
   if ((e = launch_hist_rank(topk_idx, s.tokens, s.top_k, s.experts, local_rank, blocks, nullptr,
                             st)) != cudaSuccess ||
       (e = launch_scan(blocks, nblk, s.experts, cnt, offs, st)) != cudaSuccess ||
-      (e = launch_permute_gather(topk_idx, local_rank, blocks, topk_weight, 0, x, s.tokens,
+      (e = launch_permute_gather(topk_idx, local_rank, blocks, cnt, topk_weight, 0, x, s.tokens,
                                  s.hidden, s.top_k, s.experts, s.dtype, pos, sort_idx,
                                  sorted_token, sorted_weight, x_sorted, st)) != cudaSuccess)
     return report_error(HMOE_EIO, "dispatch_noalloc launch: %s", cudaGetErrorString(e));

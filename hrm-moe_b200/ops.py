@@ -329,6 +329,47 @@ def ffn_forward(x: torch.Tensor, w_router: torch.Tensor, w_gate_up: torch.Tensor
     return (out, routing) if return_routing else out
 
 
+def ffn_forward_host(x_host: torch.Tensor, w_router: torch.Tensor, w_gate_up: torch.Tensor,
+                     w_down: torch.Tensor, top_k: int, norm_topk_prob: bool,
+                     router_bias: Optional[torch.Tensor] = None,
+                     y_host: Optional[torch.Tensor] = None, chunk_tokens: int = 4096,
+                     workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """The layer on host tensors (pinned for overlap), weights on the GPU.
+
+    Copies in, computes and copies out chunk by chunk with the three
+    overlapped (hmoe_ffn_forward_host).  Returns y_host; it is complete when
+    the current CUDA stream of the weights' device reaches this point.
+    """
+    if x_host.is_cuda:
+        raise ValueError("x_host must be a host tensor")
+    if not x_host.is_contiguous() or (y_host is not None and not y_host.is_contiguous()):
+        raise ValueError("x_host and y_host must be contiguous (the copies are asynchronous)")
+    if y_host is not None and y_host.dtype != x_host.dtype:
+        raise TypeError("y_host must have x_host's dtype")
+    T, d = x_host.shape
+    dt = x_host.dtype
+    E = w_router.shape[0]
+    I = w_gate_up.shape[1] // 2
+    dev = _require_cuda(w_router, w_gate_up, w_down, router_bias)
+    if y_host is None:
+        y_host = torch.empty((T, d), dtype=dt, pin_memory=True)
+    if T == 0:
+        return y_host
+    shape = _lib.HmoeShape(T, d, E, I, top_k, dtype_code(dt), 1 if norm_topk_prob else 0)
+    lib = _lib.load()
+    ws_bytes = lib.hmoe_ffn_host_workspace_bytes(ctypes.byref(shape), chunk_tokens)
+    if ws_bytes == 0:
+        raise ValueError(_lib.last_error())
+    if workspace is None or workspace.numel() < ws_bytes:
+        workspace = _workspace(ws_bytes, dev)
+    bias = None if router_bias is None else router_bias.to(dt).contiguous()
+    _lib.check(lib.hmoe_ffn_forward_host(
+        ctypes.byref(shape), _ptr(x_host), _ptr(w_router.to(dt).contiguous()),
+        _ptr(bias), _ptr(w_gate_up.to(dt).contiguous()), _ptr(w_down.to(dt).contiguous()),
+        _ptr(y_host), chunk_tokens, _ptr(workspace), workspace.numel(), _stream(dev)))
+    return y_host
+
+
 def workspace_status(workspace: torch.Tensor) -> None:
     """Raise if kernels flagged an error in ``workspace`` (synchronises)."""
     lib = _lib.load()

@@ -78,6 +78,22 @@ int hmoe_ffn_forward(const hmoe_shape* shape, const void* x, const void* w_route
                      size_t workspace_bytes, void* stream);
 
 /*
+ * hmoe_ffn_forward on HOST buffers: x_host [T, d] in, y_host [T, d] out
+ * (pinned host memory lets the copies overlap), weights on the device.  The
+ * tokens go through in chunks of chunk_tokens: the copy of chunk c+1 in, the
+ * layer on chunk c and the copy of chunk c-1 out run at the same time on two
+ * internal copy streams and `stream`, ordered by events; the call is
+ * complete when `stream` reaches its end.  Calls on one device must not
+ * overlap (the copy streams and events are per device).  Workspace:
+ * hmoe_ffn_host_workspace_bytes(shape, chunk_tokens).
+ */
+size_t hmoe_ffn_host_workspace_bytes(const hmoe_shape* shape, int64_t chunk_tokens);
+int hmoe_ffn_forward_host(const hmoe_shape* shape, const void* x_host, const void* w_router,
+                          const void* router_bias, const void* w_gate_up, const void* w_down,
+                          void* y_host, int64_t chunk_tokens, void* workspace,
+                          size_t workspace_bytes, void* stream);
+
+/*
  * hmoe_ffn_forward with timing marks: phase_events points to 6 cudaEvent_t
  * (NULL entries skipped) recorded on the stream before the router, after
  * the router, after dispatch, after the gate_up GEMM, after the down GEMM

@@ -174,3 +174,17 @@ def test_combine_op_matches_reference_rounding():
         t = sorted_token[p]
         ref[t] = O.round_to_bf16(ref[t] + O.round_to_bf16(expert_out[p] * flat_w[p]))
     assert np.array_equal(to_np(final), ref)
+
+
+@pytest.mark.parametrize("T,chunk", [(10000, 4096), (300, 4096), (4096, 1000)])
+def test_host_buffer_pipeline_matches_device_path(T, chunk):
+    """hmoe_ffn_forward_host (chunked, copies overlapped) == the device path, bit for bit."""
+    ops = get_ops()
+    shape = synthetic().MoEShape(T, 1536, 64, 512, 8, True, "bf16")
+    inp = synthetic().make_inputs(shape, seed=13)
+    w = [to_dev(a, "bf16") for a in (inp.w_router, inp.w_gate_up, inp.w_down)]
+    x_host = torch.from_numpy(inp.x).bfloat16().pin_memory()
+    y_host = ops.ffn_forward_host(x_host, *w, 8, True, chunk_tokens=chunk)
+    torch.cuda.synchronize()
+    y_dev = ops.ffn_forward(x_host.cuda(), *w, 8, True).cpu()
+    assert torch.equal(y_host, y_dev)
