@@ -53,6 +53,9 @@ def parse_args():
                     help="target duration of the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--ep-impl", default="peer", choices=["peer", "nccl"],
+                    help="expert-parallel transport for --gpus > 1: peer memory (the product "
+                         "path) or NCCL all_to_all")
     return ap.parse_args()
 
 
@@ -258,17 +261,32 @@ def b200_arm(args, rank, world, local_rank):
             ctypes.c_void_p(stream.cuda_stream), arr))
 
     ep = None
+    peer = None
     if world > 1:
         # expert parallel: this rank keeps experts [rank*E/N, (rank+1)*E/N)
         ep = importlib.import_module("hrm-moe_b200.ep")
         el = E // world
         w_gate_up = w_gate_up[rank * el:(rank + 1) * el].contiguous()
         w_down = w_down[rank * el:(rank + 1) * el].contiguous()
-        ep_stats = []
+        # rows per (source rank, expert), from one untimed routing pass
+        idx, _ = ops.router_topk(x, w_router, k, shape.norm_topk_prob)
+        cnt = torch.bincount(idx.reshape(-1).long(), minlength=E).to(torch.int64)
+        cnt_all = [torch.empty_like(cnt) for _ in range(world)]
+        dist.all_gather(cnt_all, cnt)
+        cnt_all = torch.stack(cnt_all).view(world, world, el).cpu()  # [src, owner, el]
+        own = cnt_all.sum(2)  # [src, owner]
+        send_rows = float(own[rank].sum() - own[rank, rank])
+        recv_rows = float(own[:, rank].sum() - own[rank, rank])
+        gemm_rows = float(own[:, rank].sum())
+        if args.ep_impl == "peer":
+            peer = ep.PeerExpertParallel(d, I, E, k, shape.norm_topk_prob, max_tokens=T, dtype=dt)
 
-        def step(marks):  # noqa: F811  (EP replaces the single-GPU step)
-            ep.ep_forward(x, w_router, w_gate_up, w_down, E, k, shape.norm_topk_prob,
-                          marks=marks, stats=ep_stats)
+            def step(marks):  # noqa: F811  (EP replaces the single-GPU step)
+                peer.forward(x, w_router, w_gate_up, w_down, y=y, marks=marks)
+        else:
+            def step(marks):  # noqa: F811
+                ep.ep_forward(x, w_router, w_gate_up, w_down, E, k, shape.norm_topk_prob,
+                              marks=marks)
 
     warm_marks = make_events(n_marks)
     for _ in range(args.warmup):
@@ -276,6 +294,8 @@ def b200_arm(args, rank, world, local_rank):
         step(warm_marks)
     torch.cuda.synchronize()
     ops.workspace_status(ws)
+    if peer is not None:
+        peer.status()
 
     marks = [make_events(n_marks) for _ in range(args.steps)]
     starts = make_events(args.steps)
@@ -295,10 +315,16 @@ def b200_arm(args, rank, world, local_rank):
         dist.barrier()
     torch.cuda.synchronize()
     ops.workspace_status(ws)
+    if peer is not None:
+        peer.status()
     step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-    phase_names = (["router", "dispatch", "gate_up_gemm", "down_gemm", "combine"] if ep is None
-                   else ["router_dispatch", "a2a_dispatch", "local_experts", "a2a_combine",
-                         "combine"])
+    if ep is None:
+        phase_names = ["router", "dispatch", "gate_up_gemm", "down_gemm", "combine"]
+    elif peer is not None:
+        phase_names = ["router_exchange", "rows_out", "local_experts", "rows_back", "combine"]
+    else:
+        phase_names = ["router_dispatch", "a2a_dispatch", "local_experts", "a2a_combine",
+                       "combine"]
     phase_ms = {n: statistics.mean(m[i].elapsed_time(m[i + 1]) for m in marks)
                 for i, n in enumerate(phase_names)}
     ms = statistics.mean(step_ms)
@@ -338,6 +364,34 @@ def b200_arm(args, rank, world, local_rank):
                "ms_per_step": e2e_ms, "h2d_bytes_per_step": T * d * es,
                "d2h_bytes_per_step": T * d * es,
                "api": f"hmoe_ffn_forward_host (C ABI, pinned host buffers, {chunk}-token chunks)"}
+    elif not args.no_e2e and peer is not None:
+        # every step: pinned host tokens -> device, the peer-memory EP layer,
+        # device -> pinned host output, all on this rank's stream
+        x_host = x.cpu().pin_memory()
+        y_host = torch.empty_like(x_host).pin_memory()
+        x_dev = torch.empty_like(x)
+        e_s, e_e = make_events(args.steps), make_events(args.steps)
+        dist.barrier()
+        for i in range(args.warmup + args.steps):
+            flush.zero_()
+            if i >= args.warmup:
+                e_s[i - args.warmup].record(stream)
+            x_dev.copy_(x_host, non_blocking=True)
+            peer.forward(x_dev, w_router, w_gate_up, w_down, y=y)
+            y_host.copy_(y, non_blocking=True)
+            if i >= args.warmup:
+                e_e[i - args.warmup].record(stream)
+        torch.cuda.synchronize()
+        peer.status()
+        e2e_ms = statistics.mean(s.elapsed_time(e) for s, e in zip(e_s, e_e))
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+        e2e = {"value": world * T / (e2e_ms * 1e-3), "unit": "tokens/s",
+               "ms_per_step": e2e_ms, "h2d_bytes_per_step": T * d * es,
+               "d2h_bytes_per_step": T * d * es,
+               "api": "PeerExpertParallel.forward (hmoe_ep_forward) with pinned host copies "
+                      "in and out on the same stream"}
 
     # ------------------------------------------------------------ roofline
     peaks = measured_peaks()
@@ -352,16 +406,26 @@ def b200_arm(args, rank, world, local_rank):
             "combine": ("hbm", A * d * es + A * (4 + es) + T * d * es),
         }
     else:
-        # rows this rank received / sent per step (mean over the timed steps)
-        recv_rows = statistics.mean(sum(st.recv_rows) for st in ep_stats[-args.steps:])
-        send_rows = statistics.mean(sum(st.send_rows) for st in ep_stats[-args.steps:])
-        algo = {
-            "router_dispatch": ("hbm", T * d * es + E * d * es + T * d * es + A * d * es),
-            "a2a_dispatch": ("nvlink", send_rows * d * es),
-            "local_experts": ("tensor", 2.0 * recv_rows * d * 2 * I + 2.0 * recv_rows * I * d),
-            "a2a_combine": ("nvlink", send_rows * d * es),
-            "combine": ("hbm", A * d * es + A * (4 + es) + T * d * es),
-        }
+        # NVLink bytes: the rows that leave this rank (or arrive), whichever is larger
+        link_rows = max(send_rows, recv_rows)
+        gemm_flops = 2.0 * gemm_rows * d * 2 * I + 2.0 * gemm_rows * I * d
+        combine_bytes = A * d * es + A * (4 + es) + T * d * es
+        if peer is not None:
+            algo = {
+                "router_exchange": ("hbm", T * d * es + E * d * es + T * k * 8),
+                "rows_out": ("nvlink", link_rows * d * es),
+                "local_experts": ("tensor", gemm_flops),
+                "rows_back": ("nvlink", link_rows * d * es),
+                "combine": ("hbm", combine_bytes),
+            }
+        else:
+            algo = {
+                "router_dispatch": ("hbm", T * d * es + E * d * es + T * d * es + A * d * es),
+                "a2a_dispatch": ("nvlink", link_rows * d * es),
+                "local_experts": ("tensor", gemm_flops),
+                "a2a_combine": ("nvlink", link_rows * d * es),
+                "combine": ("hbm", combine_bytes),
+            }
     phases = {}
     for n in phase_names:
         bound, work = algo[n]
@@ -396,6 +460,8 @@ def b200_arm(args, rank, world, local_rank):
                          f"(numpy/OpenBLAS + C router, {os.cpu_count()} host threads)"}
 
     clk = clocks.summary()
+    if peer is not None:
+        peer.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -411,13 +477,17 @@ def b200_arm(args, rank, world, local_rank):
                    "tokens_per_gpu": T, "global_tokens": world * T,
                    "parallelism": ("single GPU" if world == 1 else
                                    f"expert parallel x{world} ({E // world} experts per GPU, "
-                                   "NCCL all_to_all)"),
+                                   + ("rows over NVLink peer memory, no host sync)"
+                                      if peer is not None else "NCCL all_to_all)")),
                    "l2": "256 MiB buffer rewritten before every step (outside the timed events)"},
         "roofline": roofline,
         "phases": phases,
         "cpu_baseline": cpu,
         "e2e": e2e,
-        "gpu_launches": (7 if world == 1 else 8) * args.steps,
+        # ours per step: router (2), dispatch (3), 2 GEMMs, combine; the peer
+        # path adds exchange, two waits and return, its dispatch is 3 kernels
+        # with the row stores; NCCL's own kernels are not counted
+        "gpu_launches": (12 if peer is not None else 8) * args.steps,
         "clocks": clk,
     }
     print(json.dumps(line), flush=True)

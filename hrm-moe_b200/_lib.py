@@ -23,6 +23,7 @@ HMOE_ENOSPC = errno.ENOSPC
 HMOE_ENOSYS = errno.ENOSYS
 HMOE_ETIMEDOUT = errno.ETIMEDOUT
 DTYPE_BF16 = 0
+EP_HANDLE_BYTES = 80  # HMOE_EP_HANDLE_BYTES
 DTYPE_F32 = 1
 
 c_void_p = ctypes.c_void_p
@@ -81,6 +82,19 @@ SIGNATURES = {
     "hmoe_combine": (c_int, [ShapeP, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                              c_size_t, c_void_p]),
     "hmoe_workspace_status": (c_int, [c_void_p, c_void_p]),
+    "hmoe_ep_symmetric_bytes": (c_size_t, [ShapeP, c_int64, c_int32]),
+    "hmoe_ep_workspace_bytes": (c_size_t, [ShapeP, c_int64, c_int32]),
+    "hmoe_ep_symmetric_alloc": (c_int, [c_size_t, ctypes.POINTER(c_void_p), c_void_p]),
+    "hmoe_ep_symmetric_open": (c_int, [c_void_p, ctypes.POINTER(c_void_p)]),
+    "hmoe_ep_symmetric_close": (c_int, [c_void_p]),
+    "hmoe_ep_symmetric_free": (c_int, [c_void_p]),
+    "hmoe_ep_forward": (c_int, [ShapeP, c_int64, c_int32, c_int32, ctypes.POINTER(c_void_p),
+                                ctypes.c_uint32, c_void_p, c_void_p, c_void_p, c_void_p,
+                                c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "hmoe_ep_forward_marked": (c_int, [ShapeP, c_int64, c_int32, c_int32,
+                                       ctypes.POINTER(c_void_p), ctypes.c_uint32, c_void_p,
+                                       c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                       c_size_t, c_void_p, ctypes.POINTER(c_void_p)]),
     "hmoe_dispatch_noalloc": (c_int, [ShapeP, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                       c_void_p, c_void_p, c_void_p, c_void_p]),
 }

@@ -7,6 +7,7 @@
 #include <stdarg.h>
 #include <stdio.h>
 #include <stdlib.h>
+#include <string.h>
 
 #include <mutex>
 #include <string>
@@ -479,6 +480,126 @@ int hmoe_ffn_forward_host(const hmoe_shape* shape, const void* x_host, const voi
   return HMOE_OK;
 }
 
+// ------------------------------------------------- expert parallel (P2P) ----
+size_t hmoe_ep_symmetric_bytes(const hmoe_shape* shape, int64_t max_tokens, int32_t world) {
+  if (validate_shape(shape) != HMOE_OK || max_tokens < 0 || world < 1 || world > 8) return 0;
+  return ep_symmetric_bytes(*shape, max_tokens, world);
+}
+
+size_t hmoe_ep_workspace_bytes(const hmoe_shape* shape, int64_t max_tokens, int32_t world) {
+  if (validate_shape(shape) != HMOE_OK || max_tokens < 0 || world < 1 || world > 8) return 0;
+  return ep_workspace_bytes(*shape, max_tokens, world);
+}
+
+// The exchanged handle: the region's cudaIpcMemHandle_t, then the UUID of
+// the GPU that owns it (so that open can refuse a region of its own GPU).
+static_assert(sizeof(cudaIpcMemHandle_t) + sizeof(cudaUUID_t) == HMOE_EP_HANDLE_BYTES,
+              "handle layout");
+
+static int current_uuid(cudaUUID_t* out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  cudaDeviceProp prop;
+  if (e == cudaSuccess) e = cudaGetDeviceProperties(&prop, dev);
+  if (e != cudaSuccess) return cuda_fail(e, "device UUID");
+  *out = prop.uuid;
+  return HMOE_OK;
+}
+
+int hmoe_ep_symmetric_alloc(size_t bytes, void** ptr, void* handle) {
+  if (!ptr || !handle || bytes == 0) return fail(HMOE_EINVAL, "bad arguments");
+  cudaUUID_t uuid;
+  int rc = current_uuid(&uuid);
+  if (rc) return rc;
+  void* p = nullptr;
+  HMOE_CUDA(cudaMalloc(&p, bytes), "cudaMalloc(symmetric region)");
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaMemset(p, 0, bytes);
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return cuda_fail(e, "symmetric region");
+  }
+  memcpy(handle, &h, sizeof(h));
+  memcpy(static_cast<char*>(handle) + sizeof(h), &uuid, sizeof(uuid));
+  *ptr = p;
+  return HMOE_OK;
+}
+
+int hmoe_ep_symmetric_open(const void* handle, void** peer_ptr) {
+  if (!handle || !peer_ptr) return fail(HMOE_EINVAL, "bad arguments");
+  // The exchange kernels of different ranks wait on one another, so each
+  // rank needs its own GPU: two of them sharing one could wait forever.
+  cudaUUID_t mine;
+  int rc = current_uuid(&mine);
+  if (rc) return rc;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  if (memcmp(static_cast<const char*>(handle) + sizeof(h), &mine, sizeof(mine)) == 0)
+    return fail(HMOE_EINVAL, "peer region lives on this GPU: every rank needs its own GPU");
+  HMOE_CUDA(cudaIpcOpenMemHandle(peer_ptr, h, cudaIpcMemLazyEnablePeerAccess),
+            "cudaIpcOpenMemHandle");
+  return HMOE_OK;
+}
+
+int hmoe_ep_symmetric_close(void* peer_ptr) {
+  HMOE_CUDA(cudaIpcCloseMemHandle(peer_ptr), "cudaIpcCloseMemHandle");
+  return HMOE_OK;
+}
+
+int hmoe_ep_symmetric_free(void* ptr) {
+  HMOE_CUDA(cudaFree(ptr), "cudaFree(symmetric region)");
+  return HMOE_OK;
+}
+
+int hmoe_ep_forward_marked(const hmoe_shape* shape, int64_t max_tokens, int32_t rank,
+                           int32_t world, void* const* peer_bases, uint32_t epoch, const void* x,
+                           const void* w_router, const void* router_bias,
+                           const void* w_gate_up_local, const void* w_down_local, void* y,
+                           void* workspace, size_t workspace_bytes, void* stream,
+                           void* const* phase_events) {
+  int rc = validate_shape(shape);
+  if (rc) return rc;
+  const hmoe_shape& s = *shape;
+  if (world < 1 || world > 8 || rank < 0 || rank >= world)
+    return fail(HMOE_EINVAL, "rank %d of world %d (1..8 ranks)", rank, world);
+  if (s.experts % world) return fail(HMOE_EINVAL, "experts %d not divisible by world %d", s.experts, world);
+  if (s.tokens > max_tokens) return fail(HMOE_EINVAL, "tokens %lld exceed max_tokens %lld",
+                                         (long long)s.tokens, (long long)max_tokens);
+  if (static_cast<int64_t>(world) * max_tokens * s.top_k >= (1ll << 28))
+    return fail(HMOE_EINVAL, "world * max_tokens * top_k must stay below 2^28");
+  if (!peer_bases || !w_router || !w_gate_up_local || !w_down_local || (s.tokens > 0 && (!x || !y)))
+    return fail(HMOE_EINVAL, "NULL argument");
+  for (int p = 0; p < world; ++p)
+    if (!peer_bases[p]) return fail(HMOE_EINVAL, "peer base %d is NULL", p);
+  if (s.tokens > 0 && (!aligned16(x) || !aligned16(y)))
+    return fail(HMOE_EINVAL, "x and y must be 16-byte aligned");
+  cudaEvent_t marks[6];
+  if (phase_events) {
+    for (int i = 0; i < 6; ++i) {
+      if (!phase_events[i]) return fail(HMOE_EINVAL, "phase event %d is NULL", i);
+      marks[i] = static_cast<cudaEvent_t>(phase_events[i]);
+    }
+  }
+  if ((rc = select_device(w_gate_up_local))) return rc;
+  if ((rc = check_ws(workspace, workspace_bytes, ep_workspace_bytes(s, max_tokens, world)))) return rc;
+  HMOE_CUDA(ep_forward_launch(s, max_tokens, rank, world, peer_bases, epoch, x, w_router,
+                              router_bias, w_gate_up_local, w_down_local, y, workspace,
+                              static_cast<cudaStream_t>(stream), phase_events ? marks : nullptr),
+            "ep_forward");
+  return HMOE_OK;
+}
+
+int hmoe_ep_forward(const hmoe_shape* shape, int64_t max_tokens, int32_t rank, int32_t world,
+                    void* const* peer_bases, uint32_t epoch, const void* x, const void* w_router,
+                    const void* router_bias, const void* w_gate_up_local,
+                    const void* w_down_local, void* y, void* workspace, size_t workspace_bytes,
+                    void* stream) {
+  return hmoe_ep_forward_marked(shape, max_tokens, rank, world, peer_bases, epoch, x, w_router,
+                                router_bias, w_gate_up_local, w_down_local, y, workspace,
+                                workspace_bytes, stream, nullptr);
+}
+
 size_t hmoe_router_workspace_bytes(const hmoe_shape* shape) {
   return plan_bytes(shape, [](Carve& c, const hmoe_shape& s) {
     c.take<int>(sizeof(int));  // error word
@@ -667,6 +788,8 @@ int hmoe_workspace_status(const void* workspace, void* stream) {
   HMOE_CUDA(cudaStreamSynchronize(st), "cudaStreamSynchronize");
   if (word == kDevBadExpert) return fail(HMOE_EINVAL, "an expert id outside [0, experts) was dropped");
   if (word == kDevTimeout) return fail(HMOE_ETIMEDOUT, "a device-side wait gave up");
+  if (word == kDevEpOverflow)
+    return fail(HMOE_EIO, "expert-parallel counts exceeded the symmetric buffers");
   if (word != kDevOk) return fail(HMOE_EIO, "unknown device error word %d", word);
   return HMOE_OK;
 }

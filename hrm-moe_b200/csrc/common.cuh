@@ -15,6 +15,7 @@ constexpr int kDtypeF32 = 1;
 constexpr int kDevOk = 0;
 constexpr int kDevBadExpert = 1;   // an expert id outside [0, E) was dropped
 constexpr int kDevTimeout = 2;     // a bounded wait gave up
+constexpr int kDevEpOverflow = 3;  // peer counts exceed the expert-parallel buffers
 
 // The fixed accumulation order of router logits: k is cut into blocks of
 // kLogitBlock; each block is one fma per k, ascending, from +0, and the block

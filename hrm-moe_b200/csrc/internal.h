@@ -77,6 +77,15 @@ struct GroupedGemmArgs {
 cudaError_t launch_grouped_gemm_sm100(const GroupedGemmArgs& args, cudaStream_t stream);
 cudaError_t launch_grouped_gemm_simt(const GroupedGemmArgs& args, cudaStream_t stream);
 
+// ep_p2p.cu -------------------------------------------------------------
+size_t ep_symmetric_bytes(const ::hmoe_shape& s, int64_t max_tokens, int world);
+size_t ep_workspace_bytes(const ::hmoe_shape& s, int64_t max_tokens, int world);
+cudaError_t ep_forward_launch(const ::hmoe_shape& s, int64_t max_tokens, int rank, int world,
+                              void* const* peer_bases, uint32_t epoch, const void* x,
+                              const void* w_router, const void* bias, const void* w_gate_up,
+                              const void* w_down, void* y, void* workspace, cudaStream_t st,
+                              const cudaEvent_t* marks);  // 6 events or nullptr
+
 // capi.cu ---------------------------------------------------------------
 int num_sms_for_current_device();
 // Entry-point plumbing for files other than capi.cu: set hmoe_last_error()

@@ -1,4 +1,4 @@
-"""Expert parallelism for the routed MoE FFN over torch.distributed (NCCL).
+"""Expert parallelism for the routed MoE FFN: peer memory (product) and NCCL.
 
 Mirrors SparseMoEExpertParallel (models/layers.py:383-478): experts are
 sharded contiguously (rank r owns [r*E/R, (r+1)*E/R), layers.py:403-405),
@@ -120,6 +120,126 @@ def ep_forward(x: torch.Tensor, w_router: torch.Tensor, w_gate_up_local: torch.T
         compute.combine(back, sort_idx, w, y)
     mark(5)
     return y
+
+
+class PeerExpertParallel:
+    """Expert parallelism over peer memory (hmoe_ep_forward), no host sync per call.
+
+    Set-up (collective, once): every rank allocates its symmetric region in
+    the library (cudaMalloc + CUDA IPC handle), the handles are exchanged
+    with all_gather_object, and every rank maps its peers' regions (each rank
+    on its own GPU).  Each call then runs entirely on the device: counts,
+    rows and results move by NVLink stores between the mapped regions,
+    ordered by flags carrying the call's epoch.  All ranks must call
+    ``forward`` the same number of times (the epochs advance together).
+    """
+
+    def __init__(self, hidden: int, intermediate: int, num_experts: int, top_k: int,
+                 norm_topk_prob: bool, max_tokens: int, dtype=torch.bfloat16, group=None):
+        import ctypes
+        from . import _lib
+        self._ct = ctypes
+        self._lib = _lib
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if num_experts % self.world:
+            raise ValueError(f"num_experts={num_experts} must be divisible by world_size={self.world}")
+        if self.world > 8:
+            raise ValueError("peer-memory expert parallelism supports up to 8 ranks (one node)")
+        self.hidden, self.intermediate, self.num_experts = hidden, intermediate, num_experts
+        self.top_k, self.norm = top_k, norm_topk_prob
+        self.max_tokens = int(max_tokens)
+        self.dtype = dtype
+        self.device = torch.device("cuda", torch.cuda.current_device())
+        self.epoch = 0
+        lib = _lib.load()
+        shape = ops.make_shape(self.max_tokens, hidden, num_experts, intermediate, top_k, dtype,
+                               norm_topk_prob)
+        nbytes = lib.hmoe_ep_symmetric_bytes(ctypes.byref(shape), self.max_tokens, self.world)
+        if nbytes == 0:
+            raise ValueError(_lib.last_error())
+        self.ws = torch.empty(lib.hmoe_ep_workspace_bytes(ctypes.byref(shape), self.max_tokens,
+                                                          self.world),
+                              dtype=torch.uint8, device=self.device)
+        mine = ctypes.c_void_p()
+        handle = ctypes.create_string_buffer(_lib.EP_HANDLE_BYTES)
+        _lib.check(lib.hmoe_ep_symmetric_alloc(nbytes, ctypes.byref(mine), handle))
+        self._mine = mine
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle.raw, group=group)
+        self._opened = []
+        bases = []
+        for p, h in enumerate(handles):
+            if p == self.rank:
+                bases.append(mine.value)
+                continue
+            ptr = ctypes.c_void_p()
+            _lib.check(lib.hmoe_ep_symmetric_open(
+                ctypes.create_string_buffer(h, _lib.EP_HANDLE_BYTES), ctypes.byref(ptr)))
+            self._opened.append(ptr)
+            bases.append(ptr.value)
+        self._bases = (ctypes.c_void_p * self.world)(*bases)
+        torch.cuda.synchronize()
+        dist.barrier(group=group)
+
+    def forward(self, x, w_router, w_gate_up_local, w_down_local, router_bias=None, y=None,
+                marks=None):
+        """y [T, d] for this rank's tokens x [T, d] (T <= max_tokens).
+
+        ``marks`` (optional, 6 torch.cuda.Event) are recorded before the
+        router, after the count exchange, after the rows have landed, after
+        the local experts, after the results have come back and after the
+        combine.
+        """
+        ct, lib = self._ct, self._lib.load()
+        T, d = x.shape
+        el = self.num_experts // self.world
+        if T > self.max_tokens:
+            raise ValueError(f"{T} tokens exceed max_tokens={self.max_tokens}")
+        if d != self.hidden or x.dtype != self.dtype:
+            raise ValueError(f"x must be [T, {self.hidden}] {self.dtype}, got {tuple(x.shape)} {x.dtype}")
+        want = {"w_router": (w_router, (self.num_experts, d)),
+                "w_gate_up_local": (w_gate_up_local, (el, 2 * self.intermediate, d)),
+                "w_down_local": (w_down_local, (el, d, self.intermediate))}
+        for name, (t, shp) in want.items():
+            if tuple(t.shape) != shp or t.dtype != self.dtype or not t.is_contiguous():
+                raise ValueError(f"{name} must be contiguous {shp} {self.dtype}, got "
+                                 f"{tuple(t.shape)} {t.dtype}")
+        x = x.contiguous()
+        if y is None:
+            y = torch.empty_like(x)
+        self.epoch = (self.epoch + 1) & 0xFFFFFFFF
+        if self.epoch == 0:  # flags start at 0: epoch 0 would pass every wait
+            self.epoch = 1
+        shape = ops.make_shape(T, d, self.num_experts, self.intermediate, self.top_k, x.dtype,
+                               self.norm)
+        p = lambda t: None if t is None else ct.c_void_p(t.data_ptr())
+        ev = None
+        if marks is not None:
+            ev = (ct.c_void_p * 6)(*[ct.c_void_p(m.cuda_event) for m in marks])
+        self._lib.check(lib.hmoe_ep_forward_marked(
+            ct.byref(shape), self.max_tokens, self.rank, self.world, self._bases, self.epoch,
+            p(x), p(w_router), p(router_bias), p(w_gate_up_local), p(w_down_local), p(y),
+            p(self.ws), self.ws.numel(), ct.c_void_p(torch.cuda.current_stream().cuda_stream), ev))
+        return y
+
+    def status(self):
+        """Raise if a device-side wait of an earlier call gave up (synchronises)."""
+        ops.workspace_status(self.ws)
+
+    def close(self):
+        """Collective: unmap the peers' regions and free this rank's."""
+        if self._mine is None:
+            return
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        lib = self._lib.load()
+        for ptr in self._opened:
+            lib.hmoe_ep_symmetric_close(ptr)
+        lib.hmoe_ep_symmetric_free(self._mine)
+        self._mine = None
+        self._opened = []
 
 
 class SparseMoEExpertParallelSwiGLU(torch.nn.Module):

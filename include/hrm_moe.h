@@ -217,10 +217,55 @@ int hmoe_dispatch_noalloc(const hmoe_shape* shape, const int32_t* topk_idx,
                           void* x_sorted, void* stream);
 
 /*
+ * Expert parallelism over peer memory: SparseMoEExpertParallel.forward
+ * (models/layers.py:427-478) without host-driven all_to_all.  Every rank of
+ * a job holds one symmetric region (same size on all ranks) that all ranks
+ * map by CUDA IPC; rank r owns experts [r*E/R, (r+1)*E/R) and passes only its
+ * own experts' weights (w_gate_up_local [E/R, 2I, d], w_down_local
+ * [E/R, d, I]).  The kernels exchange per-expert counts through the regions,
+ * store each routed row straight into its owner's region over NVLink, run the
+ * owner's grouped GEMMs there, copy the results back to their sources and
+ * combine in token order; the result equals one GPU running all experts.
+ * All ranks call hmoe_ep_forward in lockstep with the same, strictly
+ * increasing epoch; every cross-GPU wait is bounded (HMOE_ETIMEDOUT in the
+ * workspace error word).  max_tokens bounds any rank's token count.
+ *
+ * Set-up: hmoe_ep_symmetric_alloc (cudaMalloc + zero; writes a handle of
+ * HMOE_EP_HANDLE_BYTES: the CUDA IPC handle and the owning GPU's UUID),
+ * exchange the handles (any transport), hmoe_ep_symmetric_open each peer's.
+ * Every rank needs its own GPU: open refuses a region of the calling GPU.
+ */
+#define HMOE_EP_HANDLE_BYTES 80
+size_t hmoe_ep_symmetric_bytes(const hmoe_shape* shape, int64_t max_tokens, int32_t world);
+size_t hmoe_ep_workspace_bytes(const hmoe_shape* shape, int64_t max_tokens, int32_t world);
+int hmoe_ep_symmetric_alloc(size_t bytes, void** ptr, void* handle);
+int hmoe_ep_symmetric_open(const void* handle, void** peer_ptr);
+int hmoe_ep_symmetric_close(void* peer_ptr);
+int hmoe_ep_symmetric_free(void* ptr);
+int hmoe_ep_forward(const hmoe_shape* shape, int64_t max_tokens, int32_t rank, int32_t world,
+                    void* const* peer_bases, uint32_t epoch, const void* x, const void* w_router,
+                    const void* router_bias, const void* w_gate_up_local,
+                    const void* w_down_local, void* y, void* workspace, size_t workspace_bytes,
+                    void* stream);
+/*
+ * hmoe_ep_forward that also records six caller-owned cudaEvent_t on the
+ * stream: before the router, after the count exchange, after every peer's
+ * rows have landed, after the local grouped GEMMs, after every result has
+ * come back, and after the combine.  Same kernels, same results.
+ */
+int hmoe_ep_forward_marked(const hmoe_shape* shape, int64_t max_tokens, int32_t rank,
+                           int32_t world, void* const* peer_bases, uint32_t epoch, const void* x,
+                           const void* w_router, const void* router_bias,
+                           const void* w_gate_up_local, const void* w_down_local, void* y,
+                           void* workspace, size_t workspace_bytes, void* stream,
+                           void* const* phase_events);
+
+/*
  * Read (and synchronise the stream for) the error word kernels leave at the
  * start of a workspace used by hmoe_ffn_forward, hmoe_experts_forward,
- * hmoe_dispatch or hmoe_grouped_*: HMOE_OK, HMOE_EINVAL (an expert id was
- * outside [0, E) and was dropped) or HMOE_ETIMEDOUT.  Not for hot loops.
+ * hmoe_dispatch, hmoe_grouped_* or hmoe_ep_forward: HMOE_OK, HMOE_EINVAL (an
+ * expert id was outside [0, E) and was dropped), HMOE_ETIMEDOUT, or HMOE_EIO
+ * (expert-parallel counts beyond the symmetric buffers).  Not for hot loops.
  */
 int hmoe_workspace_status(const void* workspace, void* stream);
 

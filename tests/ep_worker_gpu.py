@@ -46,10 +46,19 @@ def main(out_path):
             y_ep = ep.ep_forward(t(inp.x), t(wr), t(inp.w_gate_up[rank * el:(rank + 1) * el]),
                                  t(inp.w_down[rank * el:(rank + 1) * el]), E, k, True)
             y_1 = ops.ffn_forward(t(inp.x), t(wr), t(inp.w_gate_up), t(inp.w_down), k, True)
+            peer = ep.PeerExpertParallel(d, I, E, k, True, max_tokens=T + 37 * (world - 1))
+            wgu_l = t(inp.w_gate_up[rank * el:(rank + 1) * el])
+            wd_l = t(inp.w_down[rank * el:(rank + 1) * el])
+            for _ in range(3):  # repeated calls reuse the regions
+                y_p2p = peer.forward(t(inp.x), t(wr), wgu_l, wd_l)
             torch.cuda.synchronize()
+            peer.status()
+            peer.close()
             same = torch.equal(y_ep, y_1)
-            ok &= same
-            msgs.append(f"T={shape.tokens} E={E} skew={skew}: {'equal' if same else 'DIFFER max %g' % (y_ep.float() - y_1.float()).abs().max().item()}")
+            same_p = torch.equal(y_p2p, y_1)
+            ok &= same and same_p
+            msgs.append(f"T={shape.tokens} E={E} skew={skew}: nccl {'equal' if same else 'DIFFER'}, "
+                        f"p2p {'equal' if same_p else 'DIFFER max %g' % (y_p2p.float() - y_1.float()).abs().max().item()}")
         dist.barrier()
     except Exception as e:  # report, then leave the group cleanly
         ok = False

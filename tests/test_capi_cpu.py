@@ -58,3 +58,37 @@ def test_workspace_sizes(lib):
     assert ffn < exp + 4 * A * 4 + 64 * 1024  # + routing buffers only
     zero = lib.HmoeShape(0, 1536, 64, 512, 8, 0, 1)
     assert so.hmoe_ffn_workspace_bytes(ctypes.byref(zero)) > 0
+
+
+def test_expert_parallel_arguments(lib):
+    so = lib.load()
+    import re
+    text = lib.HEADER.read_text()
+    assert int(re.search(r"#define HMOE_EP_HANDLE_BYTES (\d+)", text).group(1)) == lib.EP_HANDLE_BYTES
+    s = lib.HmoeShape(4096, 1536, 64, 512, 8, 0, 1)
+    T, d, k = 4096, 1536, 8
+    for world in (2, 8):
+        sym = so.hmoe_ep_symmetric_bytes(ctypes.byref(s), T, world)
+        # every peer's rows can land here, and every own row can come back
+        assert sym >= (world * T * k + T * k) * d * 2 + world * T * k * 4
+        assert sym < (world * T * k + T * k) * d * 2 + world * T * k * 4 + (1 << 20)
+        ws = so.hmoe_ep_workspace_bytes(ctypes.byref(s), T, world)
+        assert ws >= world * T * k * (512 + d) * 2  # activations + outputs of the local GEMMs
+    assert so.hmoe_ep_symmetric_bytes(ctypes.byref(s), T, 9) == 0
+    assert so.hmoe_ep_workspace_bytes(ctypes.byref(s), T, 0) == 0
+    bases = (ctypes.c_void_p * 2)(None, None)
+    args = [None] * 6 + [None, 0, None]
+    # rank outside the world, experts not divisible, too many tokens, NULL peer
+    for rank, world, shape, max_tokens, word in [
+            (2, 2, s, T, b"rank"),
+            (0, 3, s, T, b"divisible"),
+            (0, 2, s, T - 1, b"max_tokens"),
+            (0, 2, s, T, b"NULL")]:
+        rc = so.hmoe_ep_forward(ctypes.byref(shape), max_tokens, rank, world, bases, 1, *args)
+        assert rc == errno.EINVAL, so.hmoe_last_error()
+        assert word in so.hmoe_last_error()
+    big = lib.HmoeShape(1 << 22, 1536, 64, 512, 8, 0, 1)
+    rc = so.hmoe_ep_forward(ctypes.byref(big), 1 << 22, 0, 8, bases, 1, *args)
+    assert rc == errno.EINVAL and b"2^28" in so.hmoe_last_error()
+    assert so.hmoe_ep_symmetric_alloc(0, None, None) == errno.EINVAL
+    assert so.hmoe_ep_symmetric_open(None, None) == errno.EINVAL
