@@ -49,11 +49,16 @@ constexpr int kStageBytes = kABytes + 2 * kBBoxBytes;  // 48 KB
 constexpr int kAccCols = 256;                 // fp32 accumulator columns (MMA N)
 constexpr int kNumAcc = 2;
 constexpr int kTmemCols = kAccCols * kNumAcc; // 512 = all of TMEM
-constexpr int kThreads = 192;
+// Epilogue warps: the SwiGLU tile (exp + divide per output, direct stores)
+// takes two warps per TMEM lane quadrant to hide its latency; the plain tile
+// takes one per quadrant with two TMA staging boxes each.
+template <bool SWIGLU>
+__host__ __device__ constexpr int epi_warps() { return SWIGLU ? 8 : 4; }
+template <bool SWIGLU>
+__host__ __device__ constexpr int num_threads() { return 64 + 32 * epi_warps<SWIGLU>(); }  // + producer, MMA
 constexpr int kMaxGroups = 1024;
-constexpr int kEpiWarps = 4;
 constexpr int kEpiChunkBytes = 32 * 32 * 2;                  // 32 rows x 32 bf16 columns
-constexpr int kEpiBytes = kEpiWarps * 2 * kEpiChunkBytes;    // double-buffered per warp
+constexpr int kEpiBytes = 4 * 2 * kEpiChunkBytes;            // plain tile: 2 boxes per warp
 
 struct SmemCtl {
   uint64_t full[kStages];
@@ -104,7 +109,10 @@ __device__ __forceinline__ void decode_tile(const SmemCtl& ctl, int G, int n_til
   nrows = min(BM, ctl.group_rows[g + 1] - row0);
 }
 
-// 32 accumulator columns of one row -> 16 packed bf16x2 words.
+// 32 accumulator columns of one row -> 16 packed bf16x2 words.  The
+// conversion/transcendental pipe is the scarce one here (SiLU's exp and
+// divide use it), so the intermediate roundings run on the integer pipe and
+// the final one is a paired conversion.
 template <bool SWIGLU>
 __device__ __forceinline__ void epi_pack(const uint32_t (&a)[32], const uint32_t (&b)[32],
                                          uint32_t (&packed)[16]) {
@@ -114,19 +122,19 @@ __device__ __forceinline__ void epi_pack(const uint32_t (&a)[32], const uint32_t
     if (SWIGLU) {
       // gate_up is a bf16 tensor in the reference, F.silu returns bf16 and
       // the product is rounded again (models/layers.py:326-329).
-      const float g0 = round_bf16(__uint_as_float(a[2 * i]));
-      const float g1 = round_bf16(__uint_as_float(a[2 * i + 1]));
-      const float u0 = round_bf16(__uint_as_float(b[2 * i]));
-      const float u1 = round_bf16(__uint_as_float(b[2 * i + 1]));
-      const float s0 = round_bf16(g0 / (1.0f + expf(-g0)));
-      const float s1 = round_bf16(g1 / (1.0f + expf(-g1)));
+      const float g0 = round_bf16_alu(__uint_as_float(a[2 * i]));
+      const float g1 = round_bf16_alu(__uint_as_float(a[2 * i + 1]));
+      const float u0 = round_bf16_alu(__uint_as_float(b[2 * i]));
+      const float u1 = round_bf16_alu(__uint_as_float(b[2 * i + 1]));
+      const float s0 = round_bf16_alu(g0 / (1.0f + expf(-g0)));
+      const float s1 = round_bf16_alu(g1 / (1.0f + expf(-g1)));
       v0 = s0 * u0;
       v1 = s1 * u1;
     } else {
       v0 = __uint_as_float(a[2 * i]);
       v1 = __uint_as_float(a[2 * i + 1]);
     }
-    packed[i] = pack_bf16x2(v0, v1);
+    packed[i] = cvt_bf16x2(v0, v1);
   }
 }
 
@@ -149,7 +157,7 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
 }
 
 template <bool SWIGLU>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(num_threads<SWIGLU>(), 1)
 grouped_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
                           const __grid_constant__ CUtensorMap tmB,
                           const __grid_constant__ CUtensorMap tmC, const KParams p) {
@@ -200,7 +208,7 @@ grouped_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
       }
       for (int a = 0; a < kNumAcc; ++a) {
         mbar_init(smem_u32(&ctl.acc_full[a]), 1);
-        mbar_init(smem_u32(&ctl.acc_empty[a]), 4);
+        mbar_init(smem_u32(&ctl.acc_empty[a]), epi_warps<SWIGLU>());
       }
       mbar_init(smem_u32(&ctl.drain), 1);
       ctl.abort = 0;
@@ -292,12 +300,16 @@ grouped_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    // Each warp owns a 32-lane TMEM quadrant (= 32 rows).  Per 32-column
-    // chunk it packs bf16 values into one of two 2 KiB staging buffers and a
-    // single lane issues a TMA tensor store of the 32x32 box, so global
-    // writes are whole lines and run asynchronously.  A quadrant that
-    // crosses the end of its group (or of A) stores its valid rows directly.
+    // Each warp reads one 32-lane TMEM quadrant (= 32 rows); with two warps
+    // per quadrant (SwiGLU) they take alternate 32-column chunks.  The plain
+    // tile packs each chunk into one of the warp's two 2 KiB staging boxes
+    // and one lane issues a TMA tensor store of the 32x32 box, so global
+    // writes are whole lines and run asynchronously.  A quadrant that crosses
+    // the end of its group (or of A) stores its valid rows directly, and so
+    // does the SwiGLU tile (half the bytes over a 3x longer mainloop).
+    constexpr int kStride = epi_warps<SWIGLU>() / 4;
     const int quad = warp & 3;                 // TMEM lanes this warp may read
+    const int first = (warp - 2) >> 2;         // first chunk of this warp
     const int r_in_tile = quad * 32 + lane;
     const uint32_t stg = sbase + kStages * kStageBytes + (warp - 2) * 2 * kEpiChunkBytes;
     int acc = 0, buf = 0;
@@ -316,7 +328,7 @@ grouped_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
       uint16_t* orow = p.out + grow * p.N;
       constexpr int kChunks = SWIGLU ? BNH / 32 : kAccCols / 32;
 #pragma unroll 1
-      for (int c = 0; c < kChunks; ++c) {
+      for (int c = first; c < kChunks; c += kStride) {
         uint32_t packed[16];
         {
           uint32_t ra[32];
@@ -334,9 +346,6 @@ grouped_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
         const int col0 = n * p.out_cols_per_tile + c * 32;
         if (col0 >= p.N) continue;
         if (quad_full && !SWIGLU) {
-          // the down projection writes 64 KiB per tile: TMA stores keep the
-          // epilogue off the critical path; the SwiGLU tile (32 KiB per 3x
-          // longer mainloop) is cheaper with direct stores
           if (lane == 0) bulk_wait_group_read<1>();  // the store that last used `buf` read it
           __syncwarp();
           // 64-byte swizzle (matches the store map): 16-byte piece c of row r
@@ -358,7 +367,6 @@ grouped_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
         } else if (row_ok) {
           store_row_direct(packed, orow, col0, p.N);
         }
-        (void)buf;
       }
       tc_fence_before();
       __syncwarp();
@@ -468,10 +476,10 @@ cudaError_t launch_grouped_gemm_sm100(const GroupedGemmArgs& a, cudaStream_t str
   cudaError_t e;
   if (a.swiglu) {
     if ((e = ensure_smem_attr<true>()) != cudaSuccess) return e;
-    grouped_gemm_sm100_kernel<true><<<grid, kThreads, kSmemBytes, stream>>>(ma, mb, mc, p);
+    grouped_gemm_sm100_kernel<true><<<grid, num_threads<true>(), kSmemBytes, stream>>>(ma, mb, mc, p);
   } else {
     if ((e = ensure_smem_attr<false>()) != cudaSuccess) return e;
-    grouped_gemm_sm100_kernel<false><<<grid, kThreads, kSmemBytes, stream>>>(ma, mb, mc, p);
+    grouped_gemm_sm100_kernel<false><<<grid, num_threads<false>(), kSmemBytes, stream>>>(ma, mb, mc, p);
   }
   return cudaGetLastError();
 }
