@@ -36,9 +36,19 @@ METRIC = "MoE-FFN fwd tokens/s (XL 64x8 bf16)"
 L2_FLUSH_BYTES = 256 << 20
 # measured peer copy bandwidth per direction per GPU on this pool (NVLink 5)
 NVLINK_GBS = 770.0
-# DRAM bytes per launch of the dominant kernel from `ncu` (see profiles/);
-# None until a capture of the current kernel exists.
-NCU_TRAFFIC_BYTES = {}
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per forward of
+# each phase's kernels, from one ncu capture of this workload on one B200
+# (profiles/grouped_gemm_xl64_t16384_full.md, profiles/hbm_kernels_xl64_t16384.md).
+# Keyed by (config, tokens per GPU); other workloads report null.
+NCU_TRAFFIC_BYTES = {
+    ("cfg2_xl64_bf16", 16384): {
+        "router": 50.594e6 + 0.085e6 + 1.313e6,            # router_tc + fix-up
+        "dispatch": 0.534e6 + 0.039e6 + 51.425e6 + 344.296e6,  # hist + scan + permute
+        "gate_up_gemm": 604.103e6 + 119.270e6,
+        "down_gemm": 234.991e6 + 352.724e6,
+        "combine": 403.713e6 + 42.385e6,
+    },
+}
 
 
 def parse_args():
@@ -449,7 +459,10 @@ def b200_arm(args, rank, world, local_rank):
                 "peak": peak_of[dp["bound"]],
                 "unit": dp["unit"], "frac": dp["frac"],
                 "peak_source": f"{peaks['source']} (burst)" if dp["bound"] == "tensor" else peaks["source"],
-                "traffic": NCU_TRAFFIC_BYTES.get(dom),
+                "traffic": (NCU_TRAFFIC_BYTES.get((args.config, T), {}).get(dom)
+                            if world == 1 else None),
+                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum per launch, "
+                                  "one capture of this workload (profiles/)",
                 "algorithmic": algo[dom][1]}
 
     cpu = None

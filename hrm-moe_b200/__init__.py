@@ -8,10 +8,12 @@ Python host side.
     layers.SparseMoESwiGLU(..., implementation="grouped_b200")
     ops.ffn_forward / router_topk / dispatch / grouped_linear /
         grouped_swiglu / combine / experts_forward
+    torch_ops: torch.ops.hrm_moe.ffn_forward / grouped_linear
+    ep.PeerExpertParallel / ep.ep_forward (expert parallelism)
 """
 from . import synthetic  # noqa: F401  (numpy only)
 
-__all__ = ["layers", "ops", "synthetic", "build", "load_library"]
+__all__ = ["layers", "ops", "torch_ops", "ep", "synthetic", "build", "load_library"]
 
 
 def build(verbose: bool = False):
@@ -26,7 +28,7 @@ def load_library():
 
 
 def __getattr__(name):
-    if name in ("layers", "ops", "ep"):
+    if name in ("layers", "ops", "ep", "torch_ops"):
         import importlib
         return importlib.import_module(f"{__name__}.{name}")
     raise AttributeError(name)
