@@ -331,7 +331,8 @@ def b200_arm(args, rank, world, local_rank):
     if ep is None:
         phase_names = ["router", "dispatch", "gate_up_gemm", "down_gemm", "combine"]
     elif peer is not None:
-        phase_names = ["router_exchange", "rows_out", "local_experts", "rows_back", "combine"]
+        phase_names = ["router_exchange", "rows_out", "gate_up_gemm", "down_gemm_and_return",
+                       "combine"]
     else:
         phase_names = ["router_dispatch", "a2a_dispatch", "local_experts", "a2a_combine",
                        "combine"]
@@ -424,8 +425,10 @@ def b200_arm(args, rank, world, local_rank):
             algo = {
                 "router_exchange": ("hbm", T * d * es + E * d * es + T * k * 8),
                 "rows_out": ("nvlink", link_rows * d * es),
-                "local_experts": ("tensor", gemm_flops),
-                "rows_back": ("nvlink", link_rows * d * es),
+                "gate_up_gemm": ("tensor", 2.0 * gemm_rows * d * 2 * I),
+                # one kernel: the down GEMM whose epilogue stores the rows back
+                # over NVLink; its target is the slower of the two
+                "down_gemm_and_return": ("fused", (2.0 * gemm_rows * I * d, link_rows * d * es)),
                 "combine": ("hbm", combine_bytes),
             }
         else:
@@ -444,6 +447,13 @@ def b200_arm(args, rank, world, local_rank):
             ach = work / sec / 1e12
             phases[n] = {"ms": phase_ms[n], "bound": "tensor", "achieved": ach,
                          "unit": "TFLOP/s", "frac": ach / peaks["bf16_tflops"]}
+        elif bound == "fused":
+            flops, link_bytes = work
+            target = max(flops / (peaks["bf16_tflops"] * 1e12), link_bytes / (NVLINK_GBS * 1e9))
+            phases[n] = {"ms": phase_ms[n], "bound": "tensor+nvlink",
+                         "achieved": target / sec, "unit": "fraction of max(GEMM, NVLink) time",
+                         "frac": target / sec, "tflops": flops / sec / 1e12,
+                         "nvlink_gbs": link_bytes / sec / 1e9}
         elif bound == "nvlink":
             ach = work / sec / 1e9
             phases[n] = {"ms": phase_ms[n], "bound": "nvlink", "achieved": ach, "unit": "GB/s",
@@ -454,7 +464,8 @@ def b200_arm(args, rank, world, local_rank):
                          "frac": ach / peaks["hbm_gbs"]}
     dom = max(phase_names, key=lambda n: phase_ms[n])
     dp = phases[dom]
-    peak_of = {"tensor": peaks["bf16_tflops"], "hbm": peaks["hbm_gbs"], "nvlink": NVLINK_GBS}
+    peak_of = {"tensor": peaks["bf16_tflops"], "hbm": peaks["hbm_gbs"], "nvlink": NVLINK_GBS,
+               "tensor+nvlink": 1.0}
     roofline = {"kernel": dom, "bound": dp["bound"], "achieved": dp["achieved"],
                 "peak": peak_of[dp["bound"]],
                 "unit": dp["unit"], "frac": dp["frac"],
@@ -498,9 +509,9 @@ def b200_arm(args, rank, world, local_rank):
         "cpu_baseline": cpu,
         "e2e": e2e,
         # ours per step: router (2), dispatch (3), 2 GEMMs, combine; the peer
-        # path adds exchange, two waits and return, its dispatch is 3 kernels
+        # path adds exchange and two waits (the return runs inside the down GEMM)
         # with the row stores; NCCL's own kernels are not counted
-        "gpu_launches": (12 if peer is not None else 8) * args.steps,
+        "gpu_launches": (11 if peer is not None else 8) * args.steps,
         "clocks": clk,
     }
     print(json.dumps(line), flush=True)

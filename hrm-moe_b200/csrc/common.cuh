@@ -28,6 +28,16 @@ constexpr unsigned long long kWaitLimitNs = 2000000000ull;
 __host__ __device__ inline int64_t cdiv64(int64_t a, int64_t b) { return (a + b - 1) / b; }
 __host__ __device__ inline int cdiv(int a, int b) { return (a + b - 1) / b; }
 
+// ------------------------------------------------- system-scope flags ----
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 // ---------------------------------------------------------------- bf16 ----
 __device__ __forceinline__ float bf16_bits_to_f32(uint32_t b16) {
   return __uint_as_float(b16 << 16);

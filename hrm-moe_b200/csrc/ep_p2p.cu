@@ -19,10 +19,13 @@
 //                order), with the row's origin alongside; the last CTA raises
 //                the "dispatched" flag at every peer.
 //   ep_wait      bounded wait for a flag from every peer.
-//   (local grouped GEMMs on the receive buffer: El groups, plain counts)
-//   ep_return    copies each computed row back to its source rank, at the
-//                position the source's own dispatch gave it; raises
-//                "returned" at every peer.
+//   (gate_up grouped GEMM on the receive buffer: El groups, plain counts)
+//   down GEMM    bf16: the grouped GEMM's epilogue stores each result row
+//                straight back into its source rank's region, at the position
+//                the source's own dispatch gave it, so the return transfer
+//                runs under the GEMM's math; its last CTA raises "returned"
+//                at every peer.  fp32 layers run the GEMM into local memory
+//                and ep_return copies the rows back.
 //   (the single-GPU combine on the returned rows)
 // A row thus meets exactly the kernels and the order it meets on one GPU, so
 // the result is bit-identical to one GPU running all experts.
@@ -41,7 +44,7 @@ namespace hmoe {
 namespace {
 
 constexpr int kEpMaxRanks = 8;
-constexpr uint32_t kSrcShift = 28;  // recv_src = (src << 28) | source position
+constexpr uint32_t kSrcShift = kEpSrcShift;  // recv_src = (src << 28) | source position
 constexpr uint32_t kPosMask = (1u << kSrcShift) - 1u;
 
 enum FlagKind { kFlagCounts = 0, kFlagDispatched = 1, kFlagReturned = 2 };
@@ -54,20 +57,12 @@ struct EpOffsets {
   size_t flags, mailbox, recv_src, recv_rows, y_back;
 };
 
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
 __device__ __forceinline__ int read_err(const int* err) {
   return *reinterpret_cast<const volatile int*>(err);
 }
 
-__device__ __forceinline__ uint32_t* flag_ptr(char* base, const EpOffsets& o, int kind, int src) {
+__host__ __device__ __forceinline__ uint32_t* flag_ptr(char* base, const EpOffsets& o, int kind,
+                                                       int src) {
   return reinterpret_cast<uint32_t*>(base + o.flags) + kind * kEpMaxRanks + src;
 }
 
@@ -332,7 +327,7 @@ struct EpWs {
   int32_t* recv_total;
   unsigned* done;  // 2 counters
   void* h;         // [max_recv, I]
-  void* y_recv;    // [max_recv, d]
+  void* y_recv;    // [max_recv, d], fp32 layers only (bf16 returns from the GEMM)
   size_t total;
 };
 
@@ -361,7 +356,7 @@ static EpWs ep_ws(char* base, const hmoe_shape& s, int64_t max_tokens, int world
   w.recv_total = reinterpret_cast<int32_t*>(take(sizeof(int32_t)));
   w.done = reinterpret_cast<unsigned*>(take(sizeof(unsigned) * 2));
   w.h = take(es * s.intermediate * max_recv);
-  w.y_recv = take(es * s.hidden * max_recv);
+  w.y_recv = take(s.dtype == kDtypeBF16 ? 0 : es * s.hidden * max_recv);
   w.total = off;
   return w;
 }
@@ -439,19 +434,33 @@ cudaError_t ep_forward_launch(const hmoe_shape& s, int64_t max_tokens, int rank,
   g.err = w.err;
   g.sm_limit = 0;
   e = s.dtype == kDtypeBF16 ? launch_grouped_gemm_sm100(g, st) : launch_grouped_gemm_simt(g, st);
-  if (e != cudaSuccess) return e;
+  if (e != cudaSuccess || (e = mark(3)) != cudaSuccess) return e;
   g.a = w.h;
   g.b = w_down;
-  g.out = w.y_recv;
   g.N = s.hidden;
   g.K = s.intermediate;
   g.swiglu = 0;
-  e = s.dtype == kDtypeBF16 ? launch_grouped_gemm_sm100(g, st) : launch_grouped_gemm_simt(g, st);
-  if (e != cudaSuccess || (e = mark(3)) != cudaSuccess) return e;
-  ep_return_kernel<<<num_sms_for_current_device() * 4, kEpThreads, 0, st>>>(
-      static_cast<const uint4*>(w.y_recv), w.recv_total, row_chunks, rank, world, peers, o, epoch,
-      max_recv, static_cast<int64_t>(max_tokens) * s.top_k, &w.done[1], w.err);
-  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  if (s.dtype == kDtypeBF16) {
+    // down projection fused with the return: rows go straight to their source
+    g.out = nullptr;
+    g.scatter_src = reinterpret_cast<const int32_t*>(peers.base[rank] + o.recv_src);
+    g.scatter_world = world;
+    g.scatter_cap = static_cast<int64_t>(max_tokens) * s.top_k;
+    g.done = &w.done[1];
+    g.epoch = epoch;
+    for (int p = 0; p < world; ++p) {
+      g.scatter_base[p] = peers.base[p] + o.y_back;
+      g.flag[p] = flag_ptr(peers.base[p], o, kFlagReturned, rank);
+    }
+    if ((e = launch_grouped_gemm_sm100(g, st)) != cudaSuccess) return e;
+  } else {
+    g.out = w.y_recv;
+    if ((e = launch_grouped_gemm_simt(g, st)) != cudaSuccess) return e;
+    ep_return_kernel<<<num_sms_for_current_device() * 4, kEpThreads, 0, st>>>(
+        static_cast<const uint4*>(w.y_recv), w.recv_total, row_chunks, rank, world, peers, o,
+        epoch, max_recv, static_cast<int64_t>(max_tokens) * s.top_k, &w.done[1], w.err);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
   ep_wait_kernel<<<1, 32, 0, st>>>(kFlagReturned, rank, world, peers, o, epoch, w.err);
   if ((e = cudaGetLastError()) != cudaSuccess || (e = mark(4)) != cudaSuccess) return e;
   if (s.tokens > 0 &&

@@ -52,10 +52,12 @@ constexpr int kTmemCols = kAccCols * kNumAcc; // 512 = all of TMEM
 // Epilogue warps: the SwiGLU tile (exp + divide per output, direct stores)
 // takes two warps per TMEM lane quadrant to hide its latency; the plain tile
 // takes one per quadrant with two TMA staging boxes each.
-template <bool SWIGLU>
+template <bool SWIGLU, bool SCATTER>
 __host__ __device__ constexpr int epi_warps() { return SWIGLU ? 8 : 4; }
-template <bool SWIGLU>
-__host__ __device__ constexpr int num_threads() { return 64 + 32 * epi_warps<SWIGLU>(); }  // + producer, MMA
+template <bool SWIGLU, bool SCATTER>
+__host__ __device__ constexpr int num_threads() {  // + producer, MMA issuer
+  return 64 + 32 * epi_warps<SWIGLU, SCATTER>();
+}
 constexpr int kMaxGroups = 1024;
 constexpr int kEpiChunkBytes = 32 * 32 * 2;                  // 32 rows x 32 bf16 columns
 constexpr int kEpiBytes = 4 * 2 * kEpiChunkBytes;            // plain tile: 2 boxes per warp
@@ -93,6 +95,14 @@ struct KParams {
   uint16_t* out;
   int* err;
   unsigned long long wait_limit_ns;
+  // expert-parallel return (SCATTER): see GroupedGemmArgs
+  const int32_t* scatter_src;
+  char* scatter_base[8];
+  int scatter_world;
+  int64_t scatter_cap;
+  unsigned* done;
+  uint32_t* flag[8];
+  uint32_t epoch;
 };
 
 __device__ __forceinline__ void decode_tile(const SmemCtl& ctl, int G, int n_tiles, int tile,
@@ -150,14 +160,23 @@ __device__ __forceinline__ void store_row_direct(const uint32_t (&packed)[16], u
   }
 }
 
+__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z),
                "r"(v.w)
                : "memory");
 }
 
-template <bool SWIGLU>
-__global__ void __launch_bounds__(num_threads<SWIGLU>(), 1)
+template <bool SWIGLU, bool SCATTER>
+__global__ void __launch_bounds__(num_threads<SWIGLU, SCATTER>(), 1)
 grouped_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
                           const __grid_constant__ CUtensorMap tmB,
                           const __grid_constant__ CUtensorMap tmC, const KParams p) {
@@ -208,7 +227,7 @@ grouped_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
       }
       for (int a = 0; a < kNumAcc; ++a) {
         mbar_init(smem_u32(&ctl.acc_full[a]), 1);
-        mbar_init(smem_u32(&ctl.acc_empty[a]), epi_warps<SWIGLU>());
+        mbar_init(smem_u32(&ctl.acc_empty[a]), epi_warps<SWIGLU, SCATTER>());
       }
       mbar_init(smem_u32(&ctl.drain), 1);
       ctl.abort = 0;
@@ -307,7 +326,7 @@ grouped_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
     // writes are whole lines and run asynchronously.  A quadrant that crosses
     // the end of its group (or of A) stores its valid rows directly, and so
     // does the SwiGLU tile (half the bytes over a 3x longer mainloop).
-    constexpr int kStride = epi_warps<SWIGLU>() / 4;
+    constexpr int kStride = epi_warps<SWIGLU, SCATTER>() / 4;
     const int quad = warp & 3;                 // TMEM lanes this warp may read
     const int first = (warp - 2) >> 2;         // first chunk of this warp
     const int r_in_tile = quad * 32 + lane;
@@ -322,10 +341,65 @@ grouped_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
       const uint32_t trow = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
                             static_cast<uint32_t>(acc * kAccCols);
       const int64_t grow = static_cast<int64_t>(row0) + r_in_tile;
-      const bool row_ok = r_in_tile < nrows && grow < p.M;
+      bool row_ok = r_in_tile < nrows && grow < p.M;
       const bool quad_full = (quad + 1) * 32 <= nrows &&
                              static_cast<int64_t>(row0) + (quad + 1) * 32 <= p.M;
       uint16_t* orow = p.out + grow * p.N;
+      if (SCATTER && row_ok) {
+        // the row goes back to the rank it came from, at the position that
+        // rank's dispatch gave it (peer memory over NVLink)
+        const uint32_t v = static_cast<uint32_t>(p.scatter_src[grow]);
+        const int src = static_cast<int>(v >> kEpSrcShift);
+        const int64_t pos = v & ((1u << kEpSrcShift) - 1u);
+        if (src < p.scatter_world && pos < p.scatter_cap) {
+          orow = reinterpret_cast<uint16_t*>(p.scatter_base[src]) + pos * p.N;
+        } else {
+          record_error(p.err, kDevEpOverflow);
+          row_ok = false;
+        }
+      }
+      if constexpr (SCATTER) {
+        // Rows go to scattered destinations (often another GPU), so each
+        // store instruction must write few, long pieces: 64 columns of the
+        // warp's 32 rows are packed into a 4 KiB box (row r at r*128, its
+        // 16-byte piece j at slot j ^ (r & 7), so both passes are free of
+        // bank conflicts), then read back so that 8 lanes write one row's
+        // 128 contiguous bytes: 4 rows per instruction.
+        const uint32_t box = stg;  // 4 KiB of this warp's staging
+        const unsigned long long my_row =
+            row_ok ? reinterpret_cast<unsigned long long>(orow) : 0ull;
+#pragma unroll 1
+        for (int c2 = 0; c2 < kAccCols / 64; ++c2) {
+          uint32_t pa[16], pb[16];
+          {
+            uint32_t ra[32], rb[32];
+            tmem_ld_32cols(trow + c2 * 64, ra);
+            tmem_ld_32cols(trow + c2 * 64 + 32, rb);
+            tc_wait_ld();
+            epi_pack<false>(ra, ra, pa);
+            epi_pack<false>(rb, rb, pb);
+          }
+          const int col0 = n * p.out_cols_per_tile + c2 * 64;
+          __syncwarp();  // the previous pass has read the box
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            st_shared_v4(box + lane * 128 + ((j ^ (lane & 7)) << 4),
+                         make_uint4(pa[4 * j], pa[4 * j + 1], pa[4 * j + 2], pa[4 * j + 3]));
+            st_shared_v4(box + lane * 128 + (((j + 4) ^ (lane & 7)) << 4),
+                         make_uint4(pb[4 * j], pb[4 * j + 1], pb[4 * j + 2], pb[4 * j + 3]));
+          }
+          __syncwarp();
+          const int j = lane & 7;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int r = i * 4 + (lane >> 3);
+            const unsigned long long dst = __shfl_sync(0xffffffffu, my_row, r);
+            const uint4 v = ld_shared_v4(box + r * 128 + ((j ^ (r & 7)) << 4));
+            if (dst != 0ull && col0 + j * 8 + 8 <= p.N)
+              *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(dst) + col0 + j * 8) = v;
+          }
+        }
+      } else {
       constexpr int kChunks = SWIGLU ? BNH / 32 : kAccCols / 32;
 #pragma unroll 1
       for (int c = first; c < kChunks; c += kStride) {
@@ -368,6 +442,7 @@ grouped_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
           store_row_direct(packed, orow, col0, p.N);
         }
       }
+      }  // !SCATTER
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&ctl.acc_empty[acc]));
@@ -378,11 +453,19 @@ grouped_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
   }
 
   // --------------------------------------------------------------- teardown
+  if (SCATTER) __threadfence_system();  // this thread's peer stores, before the count
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
+  }
+  if (SCATTER && threadIdx.x == 0 && p.done) {
+    const unsigned prev = atomicAdd(p.done, 1u);
+    if (prev == gridDim.x - 1 && (!p.err || *reinterpret_cast<volatile int*>(p.err) == kDevOk)) {
+      __threadfence_system();
+      for (int r = 0; r < p.scatter_world; ++r) st_release_sys(p.flag[r], p.epoch);
+    }
   }
 }
 
@@ -421,7 +504,7 @@ bool make_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, 
   return r == CUDA_SUCCESS;
 }
 
-template <bool SWIGLU>
+template <bool SWIGLU, bool SCATTER>
 cudaError_t ensure_smem_attr() {
   // once per device: opt in to the large dynamic shared memory carve-out
   static int done[64] = {0};
@@ -432,7 +515,7 @@ cudaError_t ensure_smem_attr() {
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   std::lock_guard<std::mutex> lock(mu);
   if (!done[dev]) {
-    e = cudaFuncSetAttribute(grouped_gemm_sm100_kernel<SWIGLU>,
+    e = cudaFuncSetAttribute(grouped_gemm_sm100_kernel<SWIGLU, SCATTER>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(kSmemBytes));
     if (e != cudaSuccess) return e;
@@ -446,16 +529,23 @@ cudaError_t ensure_smem_attr() {
 cudaError_t launch_grouped_gemm_sm100(const GroupedGemmArgs& a, cudaStream_t stream) {
   if (a.M == 0 || a.G == 0) return cudaSuccess;
   if (a.G > kMaxGroups || a.K % 8 != 0 || a.N % 8 != 0) return cudaErrorInvalidValue;
+  const bool scatter = a.scatter_src != nullptr;
+  if (scatter && (a.swiglu || a.scatter_world < 1 || a.scatter_world > 8))
+    return cudaErrorInvalidValue;
   const int nw = a.swiglu ? 2 * a.N : a.N;          // rows of B per weight
   const int nweights = a.num_weights > 0 ? a.num_weights : a.G;
   CUtensorMap ma, mb, mc;
   if (!make_map(&ma, a.a, static_cast<uint64_t>(a.M), static_cast<uint64_t>(a.K), BM, BK,
                 CU_TENSOR_MAP_SWIZZLE_128B) ||
       !make_map(&mb, a.b, static_cast<uint64_t>(nweights) * nw, static_cast<uint64_t>(a.K), BNH, BK,
-                CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !make_map(&mc, a.out, static_cast<uint64_t>(a.M), static_cast<uint64_t>(a.N), 32, 32,
-                CU_TENSOR_MAP_SWIZZLE_64B))
+                CU_TENSOR_MAP_SWIZZLE_128B))
     return cudaErrorInvalidValue;
+  if (scatter) {
+    mc = ma;  // the scatter epilogue stores rows directly; the store map is unused
+  } else if (!make_map(&mc, a.out, static_cast<uint64_t>(a.M), static_cast<uint64_t>(a.N), 32, 32,
+                       CU_TENSOR_MAP_SWIZZLE_64B)) {
+    return cudaErrorInvalidValue;
+  }
   KParams p;
   p.counts = a.counts;
   p.group_weight = a.group_weight;
@@ -470,16 +560,31 @@ cudaError_t launch_grouped_gemm_sm100(const GroupedGemmArgs& a, cudaStream_t str
   p.out = static_cast<uint16_t*>(a.out);
   p.err = a.err;
   p.wait_limit_ns = kWaitLimitNs;
+  p.scatter_src = a.scatter_src;
+  p.scatter_world = a.scatter_world;
+  p.scatter_cap = a.scatter_cap;
+  p.done = a.done;
+  p.epoch = a.epoch;
+  for (int i = 0; i < 8; ++i) {
+    p.scatter_base[i] = a.scatter_base[i];
+    p.flag[i] = a.flag[i];
+  }
   const int sms = a.sm_limit > 0 ? a.sm_limit : num_sms_for_current_device();
   const int64_t max_tiles = (cdiv64(a.M, BM) + a.G) * p.n_tiles;
   const int grid = static_cast<int>(max_tiles < sms ? max_tiles : sms);
   cudaError_t e;
   if (a.swiglu) {
-    if ((e = ensure_smem_attr<true>()) != cudaSuccess) return e;
-    grouped_gemm_sm100_kernel<true><<<grid, num_threads<true>(), kSmemBytes, stream>>>(ma, mb, mc, p);
+    if ((e = ensure_smem_attr<true, false>()) != cudaSuccess) return e;
+    grouped_gemm_sm100_kernel<true, false>
+        <<<grid, num_threads<true, false>(), kSmemBytes, stream>>>(ma, mb, mc, p);
+  } else if (scatter) {
+    if ((e = ensure_smem_attr<false, true>()) != cudaSuccess) return e;
+    grouped_gemm_sm100_kernel<false, true>
+        <<<grid, num_threads<false, true>(), kSmemBytes, stream>>>(ma, mb, mc, p);
   } else {
-    if ((e = ensure_smem_attr<false>()) != cudaSuccess) return e;
-    grouped_gemm_sm100_kernel<false><<<grid, num_threads<false>(), kSmemBytes, stream>>>(ma, mb, mc, p);
+    if ((e = ensure_smem_attr<false, false>()) != cudaSuccess) return e;
+    grouped_gemm_sm100_kernel<false, false>
+        <<<grid, num_threads<false, false>(), kSmemBytes, stream>>>(ma, mb, mc, p);
   }
   return cudaGetLastError();
 }

@@ -73,7 +73,21 @@ struct GroupedGemmArgs {
   int dtype;
   int* err;                  // device error word (may be null)
   int sm_limit;              // persistent CTAs (0 = all SMs)
+  // Expert-parallel return (plain bf16 GEMM only; `out` unused): output row r
+  // goes to scatter_base[src] + pos * N elements, where src and pos come from
+  // scatter_src[r] = (src << kEpSrcShift) | pos; pos < scatter_cap.  Once every
+  // CTA has fenced its stores, the last one to finish sets *flag[i] = epoch
+  // for i < scatter_world (unless the error word is set); `done` is a zeroed
+  // counter.
+  const int32_t* scatter_src = nullptr;
+  char* scatter_base[8] = {};
+  int scatter_world = 0;
+  int64_t scatter_cap = 0;
+  unsigned* done = nullptr;
+  uint32_t* flag[8] = {};
+  uint32_t epoch = 0;
 };
+constexpr uint32_t kEpSrcShift = 28;  // row origin = (source rank << 28) | source position
 cudaError_t launch_grouped_gemm_sm100(const GroupedGemmArgs& args, cudaStream_t stream);
 cudaError_t launch_grouped_gemm_simt(const GroupedGemmArgs& args, cudaStream_t stream);
 

@@ -189,7 +189,8 @@ class PeerExpertParallel:
 
         ``marks`` (optional, 6 torch.cuda.Event) are recorded before the
         router, after the count exchange, after the rows have landed, after
-        the local experts, after the results have come back and after the
+        the gate_up GEMM, after the down GEMM has stored every result back at
+        its source (bf16: the return runs inside that GEMM) and after the
         combine.
         """
         ct, lib = self._ct, self._lib.load()

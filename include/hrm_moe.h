@@ -250,8 +250,9 @@ int hmoe_ep_forward(const hmoe_shape* shape, int64_t max_tokens, int32_t rank, i
 /*
  * hmoe_ep_forward that also records six caller-owned cudaEvent_t on the
  * stream: before the router, after the count exchange, after every peer's
- * rows have landed, after the local grouped GEMMs, after every result has
- * come back, and after the combine.  Same kernels, same results.
+ * rows have landed, after the gate_up GEMM, after the down GEMM has stored
+ * every result back at its source (bf16: the return runs inside that GEMM),
+ * and after the combine.  Same kernels, same results.
  */
 int hmoe_ep_forward_marked(const hmoe_shape* shape, int64_t max_tokens, int32_t rank,
                            int32_t world, void* const* peer_bases, uint32_t epoch, const void* x,

@@ -31,22 +31,25 @@ def main(out_path):
         syn = importlib.import_module("hrm-moe_b200.synthetic")
         ep = importlib.import_module("hrm-moe_b200.ep")
         ops = importlib.import_module("hrm-moe_b200.ops")
-        for (T, d, E, I, k, skew) in [(1000, 256, 8 * world, 128, 4, False),
-                                       (4096, 1536, 64, 512, 8, False),
-                                       (777, 256, 4 * world, 64, 2, True)]:
-            shape = syn.MoEShape(T + 37 * rank, d, E, I, k, True, "bf16")
+        for (T, d, E, I, k, skew, dtype) in [(1000, 256, 8 * world, 128, 4, False, "bf16"),
+                                              (4096, 1536, 64, 512, 8, False, "bf16"),
+                                              (777, 256, 4 * world, 64, 2, True, "bf16"),
+                                              (300, 128, 2 * world, 64, 2, False, "f32")]:
+            shape = syn.MoEShape(T + 37 * rank, d, E, I, k, True, dtype)
+            tdt = torch.bfloat16 if dtype == "bf16" else torch.float32
             inp = syn.make_inputs(shape, seed=21, rank=rank)
             wr = inp.w_router
             if skew:  # pile the traffic onto the last rank's experts
                 el = E // world
                 wr = syn.round_to_bf16(wr + np.concatenate(
                     [np.zeros(((world - 1) * el, d), np.float32), np.full((el, d), 0.03, np.float32)]))
-            t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev).bfloat16()
+            t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev).to(tdt)
             el = E // world
             y_ep = ep.ep_forward(t(inp.x), t(wr), t(inp.w_gate_up[rank * el:(rank + 1) * el]),
                                  t(inp.w_down[rank * el:(rank + 1) * el]), E, k, True)
             y_1 = ops.ffn_forward(t(inp.x), t(wr), t(inp.w_gate_up), t(inp.w_down), k, True)
-            peer = ep.PeerExpertParallel(d, I, E, k, True, max_tokens=T + 37 * (world - 1))
+            peer = ep.PeerExpertParallel(d, I, E, k, True, max_tokens=T + 37 * (world - 1),
+                                         dtype=tdt)
             wgu_l = t(inp.w_gate_up[rank * el:(rank + 1) * el])
             wd_l = t(inp.w_down[rank * el:(rank + 1) * el])
             for _ in range(3):  # repeated calls reuse the regions
@@ -57,7 +60,7 @@ def main(out_path):
             same = torch.equal(y_ep, y_1)
             same_p = torch.equal(y_p2p, y_1)
             ok &= same and same_p
-            msgs.append(f"T={shape.tokens} E={E} skew={skew}: nccl {'equal' if same else 'DIFFER'}, "
+            msgs.append(f"T={shape.tokens} E={E} {dtype} skew={skew}: nccl {'equal' if same else 'DIFFER'}, "
                         f"p2p {'equal' if same_p else 'DIFFER max %g' % (y_p2p.float() - y_1.float()).abs().max().item()}")
         dist.barrier()
     except Exception as e:  # report, then leave the group cleanly

@@ -73,7 +73,12 @@ def test_expert_parallel_arguments(lib):
         assert sym >= (world * T * k + T * k) * d * 2 + world * T * k * 4
         assert sym < (world * T * k + T * k) * d * 2 + world * T * k * 4 + (1 << 20)
         ws = so.hmoe_ep_workspace_bytes(ctypes.byref(s), T, world)
-        assert ws >= world * T * k * (512 + d) * 2  # activations + outputs of the local GEMMs
+        # bf16: the activations of the local GEMMs only (the down GEMM stores
+        # its rows straight back to their sources)
+        assert world * T * k * 512 * 2 <= ws < world * T * k * (512 + d) * 2
+        f = lib.HmoeShape(4096, 1536, 64, 512, 8, 1, 1)
+        wsf = so.hmoe_ep_workspace_bytes(ctypes.byref(f), T, world)
+        assert wsf >= world * T * k * (512 + d) * 4  # fp32: activations + outputs
     assert so.hmoe_ep_symmetric_bytes(ctypes.byref(s), T, 9) == 0
     assert so.hmoe_ep_workspace_bytes(ctypes.byref(s), T, 0) == 0
     bases = (ctypes.c_void_p * 2)(None, None)
