@@ -131,13 +131,15 @@ __device__ __forceinline__ void epi_pack(const uint32_t (&a)[32], const uint32_t
     float v0, v1;
     if (SWIGLU) {
       // gate_up is a bf16 tensor in the reference, F.silu returns bf16 and
-      // the product is rounded again (models/layers.py:326-329).
+      // the product is rounded again (models/layers.py:326-329).  SiLU uses
+      // the fast exp and divide intrinsics: a few fp32 ulps, far below the
+      // bf16 step the result is rounded to, and half the epilogue's work.
       const float g0 = round_bf16_alu(__uint_as_float(a[2 * i]));
       const float g1 = round_bf16_alu(__uint_as_float(a[2 * i + 1]));
       const float u0 = round_bf16_alu(__uint_as_float(b[2 * i]));
       const float u1 = round_bf16_alu(__uint_as_float(b[2 * i + 1]));
-      const float s0 = round_bf16_alu(g0 / (1.0f + expf(-g0)));
-      const float s1 = round_bf16_alu(g1 / (1.0f + expf(-g1)));
+      const float s0 = round_bf16_alu(__fdividef(g0, 1.0f + __expf(-g0)));
+      const float s1 = round_bf16_alu(__fdividef(g1, 1.0f + __expf(-g1)));
       v0 = s0 * u0;
       v1 = s1 * u1;
     } else {
@@ -320,17 +322,18 @@ grouped_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
   } else {
     // ------------------------------------------------------------ epilogue
     // Each warp reads one 32-lane TMEM quadrant (= 32 rows); with two warps
-    // per quadrant (SwiGLU) they take alternate 32-column chunks.  The plain
-    // tile packs each chunk into one of the warp's two 2 KiB staging boxes
-    // and one lane issues a TMA tensor store of the 32x32 box, so global
-    // writes are whole lines and run asynchronously.  A quadrant that crosses
-    // the end of its group (or of A) stores its valid rows directly, and so
-    // does the SwiGLU tile (half the bytes over a 3x longer mainloop).
+    // per quadrant (SwiGLU) they take alternate 32-column chunks.  Each chunk
+    // is packed into a 2 KiB staging box (two per warp for the plain tile,
+    // one for the SwiGLU tile's eight warps) and one lane issues a TMA tensor
+    // store of the 32x32 box, so global writes are whole lines and run
+    // asynchronously.  A quadrant that crosses the end of its group (or of
+    // A) stores its valid rows directly.
     constexpr int kStride = epi_warps<SWIGLU, SCATTER>() / 4;
     const int quad = warp & 3;                 // TMEM lanes this warp may read
     const int first = (warp - 2) >> 2;         // first chunk of this warp
     const int r_in_tile = quad * 32 + lane;
-    const uint32_t stg = sbase + kStages * kStageBytes + (warp - 2) * 2 * kEpiChunkBytes;
+    constexpr int kBoxes = SWIGLU ? 1 : 2;  // staging boxes per warp (16 KiB in all)
+    const uint32_t stg = sbase + kStages * kStageBytes + (warp - 2) * kBoxes * kEpiChunkBytes;
     int acc = 0, buf = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
@@ -419,8 +422,11 @@ grouped_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
         }
         const int col0 = n * p.out_cols_per_tile + c * 32;
         if (col0 >= p.N) continue;
-        if (quad_full && !SWIGLU) {
-          if (lane == 0) bulk_wait_group_read<1>();  // the store that last used `buf` read it
+        if (quad_full) {
+          if (lane == 0) {  // the store that last used this box has read it
+            if (kBoxes == 2) bulk_wait_group_read<1>();
+            else bulk_wait_group_read<0>();
+          }
           __syncwarp();
           // 64-byte swizzle (matches the store map): 16-byte piece c of row r
           // sits at r*64 + ((c ^ ((r >> 1) & 3)) * 16), so the 8 lanes of each
@@ -437,7 +443,7 @@ grouped_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
             tma_store_2d(&tmC, col0, row0 + quad * 32, stg + buf * kEpiChunkBytes);
             bulk_commit_group();
           }
-          buf ^= 1;
+          buf ^= kBoxes - 1;
         } else if (row_ok) {
           store_row_direct(packed, orow, col0, p.N);
         }
