@@ -331,8 +331,8 @@ def b200_arm(args, rank, world, local_rank):
     if ep is None:
         phase_names = ["router", "dispatch", "gate_up_gemm", "down_gemm", "combine"]
     elif peer is not None:
-        phase_names = ["router_exchange", "rows_out", "gate_up_gemm", "down_gemm_and_return",
-                       "combine"]
+        phase_names = ["router_dispatch", "exchange", "dispatch_and_gate_up",
+                       "down_gemm_and_return", "combine"]
     else:
         phase_names = ["router_dispatch", "a2a_dispatch", "local_experts", "a2a_combine",
                        "combine"]
@@ -423,11 +423,12 @@ def b200_arm(args, rank, world, local_rank):
         combine_bytes = A * d * es + A * (4 + es) + T * d * es
         if peer is not None:
             algo = {
-                "router_exchange": ("hbm", T * d * es + E * d * es + T * k * 8),
-                "rows_out": ("nvlink", link_rows * d * es),
-                "gate_up_gemm": ("tensor", 2.0 * gemm_rows * d * 2 * I),
-                # one kernel: the down GEMM whose epilogue stores the rows back
-                # over NVLink; its target is the slower of the two
+                "router_dispatch": ("hbm", T * d * es + E * d * es + A * 20),
+                "exchange": ("latency", 0),
+                # one kernel each: the gate_up GEMM whose sender warps push the
+                # rows out over NVLink, and the down GEMM whose epilogue stores
+                # them back; each targets the slower of its GEMM and its link
+                "dispatch_and_gate_up": ("fused", (2.0 * gemm_rows * d * 2 * I, link_rows * d * es)),
                 "down_gemm_and_return": ("fused", (2.0 * gemm_rows * I * d, link_rows * d * es)),
                 "combine": ("hbm", combine_bytes),
             }
@@ -447,6 +448,9 @@ def b200_arm(args, rank, world, local_rank):
             ach = work / sec / 1e12
             phases[n] = {"ms": phase_ms[n], "bound": "tensor", "achieved": ach,
                          "unit": "TFLOP/s", "frac": ach / peaks["bf16_tflops"]}
+        elif bound == "latency":
+            phases[n] = {"ms": phase_ms[n], "bound": "latency", "achieved": None, "unit": None,
+                         "frac": None}
         elif bound == "fused":
             flops, link_bytes = work
             target = max(flops / (peaks["bf16_tflops"] * 1e12), link_bytes / (NVLINK_GBS * 1e9))
@@ -462,7 +466,7 @@ def b200_arm(args, rank, world, local_rank):
             ach = work / sec / 1e9
             phases[n] = {"ms": phase_ms[n], "bound": "hbm", "achieved": ach, "unit": "GB/s",
                          "frac": ach / peaks["hbm_gbs"]}
-    dom = max(phase_names, key=lambda n: phase_ms[n])
+    dom = max((n for n in phase_names if phases[n]["bound"] != "latency"), key=lambda n: phase_ms[n])
     dp = phases[dom]
     peak_of = {"tensor": peaks["bf16_tflops"], "hbm": peaks["hbm_gbs"], "nvlink": NVLINK_GBS,
                "tensor+nvlink": 1.0}
@@ -509,9 +513,10 @@ def b200_arm(args, rank, world, local_rank):
         "cpu_baseline": cpu,
         "e2e": e2e,
         # ours per step: router (2), dispatch (3), 2 GEMMs, combine; the peer
-        # path adds exchange and two waits (the return runs inside the down GEMM)
-        # with the row stores; NCCL's own kernels are not counted
-        "gpu_launches": (11 if peer is not None else 8) * args.steps,
+        # path adds the exchange and one wait (the row push runs inside the
+        # gate_up GEMM, the return inside the down GEMM); NCCL's own kernels
+        # are not counted
+        "gpu_launches": (10 if peer is not None else 8) * args.steps,
         "clocks": clk,
     }
     print(json.dumps(line), flush=True)

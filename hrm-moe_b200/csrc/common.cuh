@@ -38,6 +38,17 @@ __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
+// Add to a counter another GPU (or this one) waits on: earlier stores of this
+// thread become visible before the new value does.
+__device__ __forceinline__ void red_release_sys_add(uint32_t* p, uint32_t v) {
+  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Order generic-proxy global writes (seen through an acquire) before this
+// thread's later async-proxy (TMA) reads of global memory.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- bf16 ----
 __device__ __forceinline__ float bf16_bits_to_f32(uint32_t b16) {
   return __uint_as_float(b16 << 16);

@@ -54,7 +54,7 @@ struct Peers {
 };
 
 struct EpOffsets {
-  size_t flags, mailbox, recv_src, recv_rows, y_back;
+  size_t flags, mailbox, arrived, recv_src, recv_rows, y_back;
 };
 
 __device__ __forceinline__ int read_err(const int* err) {
@@ -114,6 +114,11 @@ ep_exchange_kernel(const int32_t* __restrict__ counts, int E, int me, int world,
   __shared__ int32_t cnt[kEpMaxRanks][128];
   const int El = E / world;
   char* mine = peers.base[me];
+  // No peer sends rows of this call before it has seen this rank's counts
+  // flag, and every row of the previous call has landed (the previous
+  // gate_up GEMM waited for them): the arrival counters can restart here.
+  for (int el = threadIdx.x; el < El; el += blockDim.x)
+    reinterpret_cast<uint32_t*>(mine + o.arrived)[el] = 0;
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
     tab.send_base[e] = -1;
     if (e < El) tab.recv_count[e] = 0;
@@ -295,6 +300,8 @@ EpOffsets ep_offsets(int64_t max_tokens, int d, int E, int k, int world, int es)
   off = al(off + sizeof(uint32_t) * 3 * kEpMaxRanks);
   o.mailbox = off;
   off = al(off + sizeof(int32_t) * kEpMaxRanks * E);
+  o.arrived = off;  // rows landed per local expert (fused dispatch)
+  off = al(off + sizeof(uint32_t) * 128);
   o.recv_src = off;
   off = al(off + sizeof(int32_t) * max_recv);
   o.recv_rows = off;
@@ -319,6 +326,7 @@ struct EpWs {
   float* topk_w;
   void* router_scratch;
   int32_t* local_rank;
+  int32_t* sorted_token;  // [A] token of each expert-sorted row (fused dispatch)
   int32_t* block_counts;
   int32_t* counts;
   int32_t* pos;
@@ -347,6 +355,7 @@ static EpWs ep_ws(char* base, const hmoe_shape& s, int64_t max_tokens, int world
   w.topk_w = reinterpret_cast<float*>(take(sizeof(float) * A));
   w.router_scratch = take(router_tc_scratch_bytes(s.tokens));
   w.local_rank = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * A));
+  w.sorted_token = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * A));
   w.block_counts = reinterpret_cast<int32_t*>(
       take(sizeof(int32_t) * dispatch_num_blocks(s.tokens, s.top_k) * s.experts));
   w.counts = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * s.experts));
@@ -406,20 +415,19 @@ cudaError_t ep_forward_launch(const hmoe_shape& s, int64_t max_tokens, int rank,
   } else if ((e = cudaMemsetAsync(w.counts, 0, sizeof(int32_t) * s.experts, st)) != cudaSuccess) {
     return e;
   }
+  const bool fused = s.dtype == kDtypeBF16;
+  if (fused && s.tokens > 0) {
+    // positions for the combine and the token of each sorted row for the senders
+    if ((e = launch_permute_gather(w.topk_idx, w.local_rank, w.block_counts, w.counts, nullptr, 1,
+                                   nullptr, s.tokens, s.hidden, s.top_k, s.experts, s.dtype, w.pos,
+                                   nullptr, w.sorted_token, nullptr, nullptr, st)) != cudaSuccess)
+      return e;
+  }
+  if (fused && (e = mark(1)) != cudaSuccess) return e;
   EpTables tab{w.send_base, w.recv_count, w.recv_total};
   ep_exchange_kernel<<<1, 256, 0, st>>>(w.counts, s.experts, rank, world, peers, o, epoch,
                                         max_recv, tab, w.err);
-  if ((e = cudaGetLastError()) != cudaSuccess || (e = mark(1)) != cudaSuccess) return e;
-  const unsigned disp_grid =
-      static_cast<unsigned>(s.tokens > 0 ? cdiv64(s.tokens, kEpThreads / 32) : 1);
-  ep_dispatch_kernel<<<disp_grid, kEpThreads, 0, st>>>(
-      w.topk_idx, w.local_rank, w.block_counts, w.counts, w.send_base,
-      static_cast<const uint4*>(x), s.tokens, row_chunks, s.top_k, s.experts,
-      dispatch_block_tokens(s.top_k), rank, world, peers, o, epoch, max_recv, w.pos, &w.done[0],
-      w.err);
-  if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  ep_wait_kernel<<<1, 32, 0, st>>>(kFlagDispatched, rank, world, peers, o, epoch, w.err);
-  if ((e = cudaGetLastError()) != cudaSuccess || (e = mark(2)) != cudaSuccess) return e;
+  if ((e = cudaGetLastError()) != cudaSuccess || (e = mark(fused ? 2 : 1)) != cudaSuccess) return e;
   GroupedGemmArgs g;
   g.a = peers.base[rank] + o.recv_rows;
   g.b = w_gate_up;
@@ -433,14 +441,47 @@ cudaError_t ep_forward_launch(const hmoe_shape& s, int64_t max_tokens, int rank,
   g.dtype = s.dtype;
   g.err = w.err;
   g.sm_limit = 0;
-  e = s.dtype == kDtypeBF16 ? launch_grouped_gemm_sm100(g, st) : launch_grouped_gemm_simt(g, st);
-  if (e != cudaSuccess || (e = mark(3)) != cudaSuccess) return e;
+  if (fused) {
+    // one kernel: sender warps store every routed row into its owner's
+    // receive buffer while the GEMM runs each group as soon as it is complete
+    g.push_x = x;
+    g.push_sorted_token = w.sorted_token;
+    g.push_counts = w.counts;
+    g.push_send_base = w.send_base;
+    for (int p = 0; p < world; ++p) {
+      g.push_rows[p] = peers.base[p] + o.recv_rows;
+      g.push_src[p] = reinterpret_cast<int32_t*>(peers.base[p] + o.recv_src);
+      g.push_arrived[p] = reinterpret_cast<uint32_t*>(peers.base[p] + o.arrived);
+    }
+    g.arrived = reinterpret_cast<const uint32_t*>(peers.base[rank] + o.arrived);
+    g.push_A = s.tokens * s.top_k;
+    g.push_cap = max_recv;
+    g.push_E = s.experts;
+    g.push_El = El;
+    g.push_world = world;
+    g.push_me = rank;
+    if ((e = launch_grouped_gemm_sm100(g, st)) != cudaSuccess) return e;
+    g.push_x = nullptr;
+  } else {
+    const unsigned disp_grid =
+        static_cast<unsigned>(s.tokens > 0 ? cdiv64(s.tokens, kEpThreads / 32) : 1);
+    ep_dispatch_kernel<<<disp_grid, kEpThreads, 0, st>>>(
+        w.topk_idx, w.local_rank, w.block_counts, w.counts, w.send_base,
+        static_cast<const uint4*>(x), s.tokens, row_chunks, s.top_k, s.experts,
+        dispatch_block_tokens(s.top_k), rank, world, peers, o, epoch, max_recv, w.pos, &w.done[0],
+        w.err);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    ep_wait_kernel<<<1, 32, 0, st>>>(kFlagDispatched, rank, world, peers, o, epoch, w.err);
+    if ((e = cudaGetLastError()) != cudaSuccess || (e = mark(2)) != cudaSuccess) return e;
+    if ((e = launch_grouped_gemm_simt(g, st)) != cudaSuccess) return e;
+  }
+  if ((e = mark(3)) != cudaSuccess) return e;
   g.a = w.h;
   g.b = w_down;
   g.N = s.hidden;
   g.K = s.intermediate;
   g.swiglu = 0;
-  if (s.dtype == kDtypeBF16) {
+  if (fused) {
     // down projection fused with the return: rows go straight to their source
     g.out = nullptr;
     g.scatter_src = reinterpret_cast<const int32_t*>(peers.base[rank] + o.recv_src);

@@ -54,9 +54,10 @@ constexpr int kTmemCols = kAccCols * kNumAcc; // 512 = all of TMEM
 // takes one per quadrant with two TMA staging boxes each.
 template <bool SWIGLU, bool SCATTER>
 __host__ __device__ constexpr int epi_warps() { return SWIGLU ? 8 : 4; }
-template <bool SWIGLU, bool SCATTER>
-__host__ __device__ constexpr int num_threads() {  // + producer, MMA issuer
-  return 64 + 32 * epi_warps<SWIGLU, SCATTER>();
+constexpr int kPushWarps = 4;  // row senders of the fused expert-parallel dispatch
+template <bool SWIGLU, bool SCATTER, bool PUSH>
+__host__ __device__ constexpr int num_threads() {  // + producer, MMA issuer (+ senders)
+  return 64 + 32 * epi_warps<SWIGLU, SCATTER>() + (PUSH ? 32 * kPushWarps : 0);
 }
 constexpr int kMaxGroups = 1024;
 constexpr int kEpiChunkBytes = 32 * 32 * 2;                  // 32 rows x 32 bf16 columns
@@ -75,6 +76,11 @@ struct SmemCtl {
   int group_rows[kMaxGroups + 1];   // exclusive prefix of rows
   int tile_prefix[kMaxGroups + 1];  // exclusive prefix of 128-row blocks
   int group_w[kMaxGroups];          // weight (expert) index of each group
+  // fused dispatch: the send order is (local expert, owner) so that every
+  // owner's first groups fill first; vstart is the prefix of rows over it
+  int push_vstart[129];
+  int push_vexp[128];
+  int push_ebase[128];              // first sorted position of each expert here
 };
 
 constexpr size_t kSmemBytes =
@@ -103,6 +109,18 @@ struct KParams {
   unsigned* done;
   uint32_t* flag[8];
   uint32_t epoch;
+  // fused expert-parallel dispatch (PUSH): see GroupedGemmArgs
+  const uint4* push_x;
+  const int32_t* push_sorted_token;
+  const int32_t* push_counts;
+  const int32_t* push_send_base;
+  uint4* push_rows[8];
+  int32_t* push_src[8];
+  uint32_t* push_arrived[8];
+  const uint32_t* arrived;
+  int64_t push_A;
+  int64_t push_cap;
+  int push_E, push_El, push_world, push_me, push_row_chunks;
 };
 
 __device__ __forceinline__ void decode_tile(const SmemCtl& ctl, int G, int n_tiles, int tile,
@@ -177,8 +195,97 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
                : "memory");
 }
 
-template <bool SWIGLU, bool SCATTER>
-__global__ void __launch_bounds__(num_threads<SWIGLU, SCATTER>(), 1)
+// Sender warps: this rank's rows in send order, dealt out round-robin in
+// chunks of kPushChunk rows, so that all senders advance one frontier through
+// the owners' groups and each group completes as early as it can.  Each row
+// is read from x once and stored into its owner's receive buffer with its
+// origin; after each run of one expert's rows within a chunk the warp fences
+// and adds the run to the owner's arrival counter.  Sends nothing once the
+// call has failed (the owners' waits then run out and report it).
+constexpr int kPushChunk = 16;
+
+// Copy up to two rows (a null source skips its row), 16 bytes per lane at a
+// time, with every load of a 4 KiB span issued before its stores.
+__device__ __forceinline__ void push_copy_rows2(const uint4* const (&src)[2], uint4* const (&dst)[2],
+                                                int rc, int lane) {
+  for (int c0 = 0; c0 < rc; c0 += 256) {
+    uint4 buf[2][8];
+#pragma unroll
+    for (int r = 0; r < 2; ++r)
+#pragma unroll
+      for (int s = 0; s < 8; ++s) {
+        const int c = c0 + lane + 32 * s;
+        if (src[r] && c < rc) buf[r][s] = __ldg(src[r] + c);
+      }
+#pragma unroll
+    for (int r = 0; r < 2; ++r)
+#pragma unroll
+      for (int s = 0; s < 8; ++s) {
+        const int c = c0 + lane + 32 * s;
+        if (dst[r] && c < rc) dst[r][c] = buf[r][s];
+      }
+  }
+}
+
+__device__ __forceinline__ void push_rows(const KParams& p, const SmemCtl& ctl, int pw, int npw,
+                                          int lane) {
+  if (*reinterpret_cast<volatile const int*>(p.err) != kDevOk) return;
+  const int64_t A = p.push_A;
+  const int rc = p.push_row_chunks;  // 16-byte pieces per row
+  const int64_t nch = (A + kPushChunk - 1) / kPushChunk;
+  for (int64_t ch = pw; ch < nch; ch += npw) {
+    int64_t v = ch * kPushChunk;
+    const int64_t vend = min(A, v + kPushChunk);
+    int lo = 0, hi = p.push_E;  // the segment holding v: vstart[lo] <= v < vstart[hi]
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (ctl.push_vstart[mid] <= v) lo = mid; else hi = mid;
+    }
+    for (int i = lo; v < vend && i < p.push_E; ++i) {
+      const int64_t seg_end = min(vend, static_cast<int64_t>(ctl.push_vstart[i + 1]));
+      if (v >= seg_end) continue;
+      const int e = ctl.push_vexp[i];
+      const int o = e / p.push_El, el = e - o * p.push_El;
+      const int64_t sb = p.push_send_base[e];
+      if (sb < 0) return;  // the exchange failed
+      const int64_t vs = ctl.push_vstart[i];
+      const int eb = ctl.push_ebase[e];
+      uint4* rows = p.push_rows[o];
+      int32_t* srcs = p.push_src[o];
+      for (int64_t vv = v; vv < seg_end; vv += 2) {
+        // two rows in flight: both rows' loads are issued before either store
+        const uint4* src[2];
+        uint4* dst[2];
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          src[r] = nullptr;
+          dst[r] = nullptr;
+          const int64_t rel = vv + r - vs;
+          const int64_t q = sb + rel;
+          if (vv + r >= seg_end) continue;
+          if (q >= p.push_cap) {
+            if (lane == 0) record_error(p.err, kDevEpOverflow);
+            continue;
+          }
+          const int pos = eb + static_cast<int>(rel);
+          src[r] = p.push_x + static_cast<int64_t>(p.push_sorted_token[pos]) * rc;
+          dst[r] = rows + q * rc;
+          if (lane == 0)
+            srcs[q] = static_cast<int32_t>((static_cast<uint32_t>(p.push_me) << kEpSrcShift) |
+                                           static_cast<uint32_t>(pos));
+        }
+        push_copy_rows2(src, dst, rc, lane);
+      }
+      __threadfence_system();
+      __syncwarp();
+      if (lane == 0) red_release_sys_add(p.push_arrived[o] + el, static_cast<uint32_t>(seg_end - v));
+      v = seg_end;
+    }
+  }
+}
+
+template <bool SWIGLU, bool SCATTER, bool PUSH>
+__global__ void __launch_bounds__(num_threads<SWIGLU, SCATTER, PUSH>(), 1)
 grouped_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
                           const __grid_constant__ CUtensorMap tmB,
                           const __grid_constant__ CUtensorMap tmC, const KParams p) {
@@ -222,6 +329,21 @@ grouped_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
       ctl.tile_prefix[G] = tin;
       ctl.num_m_tiles = tin;
     }
+    if (PUSH && lane == 0) {
+      int run = 0;
+      for (int e = 0; e < p.push_E; ++e) {
+        ctl.push_ebase[e] = run;
+        run += max(0, p.push_counts[e]);
+      }
+      int vrun = 0;
+      for (int i = 0; i < p.push_E; ++i) {
+        const int e = (i % p.push_world) * p.push_El + i / p.push_world;
+        ctl.push_vexp[i] = e;
+        ctl.push_vstart[i] = vrun;
+        vrun += max(0, p.push_counts[e]);
+      }
+      ctl.push_vstart[p.push_E] = vrun;
+    }
     if (lane == 0) {
       for (int s = 0; s < kStages; ++s) {
         mbar_init(smem_u32(&ctl.full[s]), 1);
@@ -258,11 +380,29 @@ grouped_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
       int stage = 0;
       uint32_t phase = 0, pending = 0, pend_phase = 0;
       bool ok = true;
+      int ready = -1;  // groups [0, ready] have all their rows (fused dispatch)
       for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
         int g, row0, nrows, n;
         decode_tile(ctl, G, p.n_tiles, tile, g, row0, nrows, n);
         const int rb0 = ctl.group_w[g] * p.b_rows_per_group + n * p.out_cols_per_tile;
         const int rb1 = rb0 + p.b_second_off;
+        if (PUSH && g > ready) {
+          // every source's rows of this group have landed (bounded wait)
+          const uint32_t want = static_cast<uint32_t>(max(0, p.counts[g]));
+          const unsigned long long t0 = global_timer_ns();
+          while (static_cast<int32_t>(ld_acquire_sys(p.arrived + g) - want) < 0) {
+            if (*abort) { ok = false; break; }
+            if (global_timer_ns() - t0 > lim) {
+              *abort = 1;
+              record_error(p.err, kDevTimeout);
+              ok = false;
+              break;
+            }
+          }
+          if (!ok) break;
+          fence_proxy_async_global();  // the rows were written by plain stores
+          ready = g;
+        }
         for (int kb = 0; kb < nkb; ++kb) {
           if (!mbar_wait_bounded(smem_u32(&ctl.empty[stage]), phase ^ 1u, abort, p.err, lim)) {
             ok = false;
@@ -319,7 +459,7 @@ grouped_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
       tc_commit(smem_u32(&ctl.drain));
       mbar_wait_bounded(smem_u32(&ctl.drain), 0, &never, p.err, lim);
     }
-  } else {
+  } else if (warp < 2 + epi_warps<SWIGLU, SCATTER>()) {
     // ------------------------------------------------------------ epilogue
     // Each warp reads one 32-lane TMEM quadrant (= 32 rows); with two warps
     // per quadrant (SwiGLU) they take alternate 32-column chunks.  Each chunk
@@ -456,6 +596,10 @@ grouped_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
     }
     if (lane == 0) bulk_wait_group_all();  // stores complete before the CTA exits
     __syncwarp();
+  } else if (PUSH) {
+    // ------------------------------------------------------------- senders
+    const int pw = blockIdx.x * kPushWarps + (warp - 2 - epi_warps<SWIGLU, SCATTER>());
+    push_rows(p, ctl, pw, gridDim.x * kPushWarps, lane);
   }
 
   // --------------------------------------------------------------- teardown
@@ -510,7 +654,7 @@ bool make_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, 
   return r == CUDA_SUCCESS;
 }
 
-template <bool SWIGLU, bool SCATTER>
+template <bool SWIGLU, bool SCATTER, bool PUSH>
 cudaError_t ensure_smem_attr() {
   // once per device: opt in to the large dynamic shared memory carve-out
   static int done[64] = {0};
@@ -521,7 +665,7 @@ cudaError_t ensure_smem_attr() {
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   std::lock_guard<std::mutex> lock(mu);
   if (!done[dev]) {
-    e = cudaFuncSetAttribute(grouped_gemm_sm100_kernel<SWIGLU, SCATTER>,
+    e = cudaFuncSetAttribute(grouped_gemm_sm100_kernel<SWIGLU, SCATTER, PUSH>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(kSmemBytes));
     if (e != cudaSuccess) return e;
@@ -578,19 +722,49 @@ cudaError_t launch_grouped_gemm_sm100(const GroupedGemmArgs& a, cudaStream_t str
   const int sms = a.sm_limit > 0 ? a.sm_limit : num_sms_for_current_device();
   const int64_t max_tiles = (cdiv64(a.M, BM) + a.G) * p.n_tiles;
   const int grid = static_cast<int>(max_tiles < sms ? max_tiles : sms);
+  const bool push = a.push_x != nullptr;
+  if (push && (!a.swiglu || scatter || a.push_world < 1 || a.push_world > 8 || a.push_E > 128 ||
+               a.push_E != a.push_world * a.push_El || !a.arrived || (a.K * 2) % 16 != 0))
+    return cudaErrorInvalidValue;
+  p.push_x = static_cast<const uint4*>(a.push_x);
+  p.push_sorted_token = a.push_sorted_token;
+  p.push_counts = a.push_counts;
+  p.push_send_base = a.push_send_base;
+  for (int i = 0; i < 8; ++i) {
+    p.push_rows[i] = reinterpret_cast<uint4*>(a.push_rows[i]);
+    p.push_src[i] = a.push_src[i];
+    p.push_arrived[i] = a.push_arrived[i];
+  }
+  p.arrived = a.arrived;
+  p.push_A = a.push_A;
+  p.push_cap = a.push_cap;
+  p.push_E = a.push_E;
+  p.push_El = a.push_El;
+  p.push_world = a.push_world;
+  p.push_me = a.push_me;
+  p.push_row_chunks = a.K * 2 / 16;
   cudaError_t e;
-  if (a.swiglu) {
-    if ((e = ensure_smem_attr<true, false>()) != cudaSuccess) return e;
-    grouped_gemm_sm100_kernel<true, false>
-        <<<grid, num_threads<true, false>(), kSmemBytes, stream>>>(ma, mb, mc, p);
+  if (a.swiglu && push) {
+    // the producers wait for rows that other CTAs' senders store: every CTA
+    // must be resident at once, which a cooperative launch guarantees
+    if ((e = ensure_smem_attr<true, false, true>()) != cudaSuccess) return e;
+    void* args[] = {&ma, &mb, &mc, &p};
+    e = cudaLaunchCooperativeKernel(
+        reinterpret_cast<const void*>(&grouped_gemm_sm100_kernel<true, false, true>), dim3(grid),
+        dim3(num_threads<true, false, true>()), args, kSmemBytes, stream);
+    if (e != cudaSuccess) return e;
+  } else if (a.swiglu) {
+    if ((e = ensure_smem_attr<true, false, false>()) != cudaSuccess) return e;
+    grouped_gemm_sm100_kernel<true, false, false>
+        <<<grid, num_threads<true, false, false>(), kSmemBytes, stream>>>(ma, mb, mc, p);
   } else if (scatter) {
-    if ((e = ensure_smem_attr<false, true>()) != cudaSuccess) return e;
-    grouped_gemm_sm100_kernel<false, true>
-        <<<grid, num_threads<false, true>(), kSmemBytes, stream>>>(ma, mb, mc, p);
+    if ((e = ensure_smem_attr<false, true, false>()) != cudaSuccess) return e;
+    grouped_gemm_sm100_kernel<false, true, false>
+        <<<grid, num_threads<false, true, false>(), kSmemBytes, stream>>>(ma, mb, mc, p);
   } else {
-    if ((e = ensure_smem_attr<false, false>()) != cudaSuccess) return e;
-    grouped_gemm_sm100_kernel<false, false>
-        <<<grid, num_threads<false, false>(), kSmemBytes, stream>>>(ma, mb, mc, p);
+    if ((e = ensure_smem_attr<false, false, false>()) != cudaSuccess) return e;
+    grouped_gemm_sm100_kernel<false, false, false>
+        <<<grid, num_threads<false, false, false>(), kSmemBytes, stream>>>(ma, mb, mc, p);
   }
   return cudaGetLastError();
 }

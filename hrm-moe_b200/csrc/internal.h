@@ -86,6 +86,24 @@ struct GroupedGemmArgs {
   unsigned* done = nullptr;
   uint32_t* flag[8] = {};
   uint32_t epoch = 0;
+  // Expert-parallel dispatch fused into the (bf16 SwiGLU) GEMM: extra warps
+  // copy this rank's routed rows into their owners' receive buffers, in
+  // expert-sorted order (push_sorted_token[pos] = token of sorted position
+  // pos, push_counts[e] rows of expert e, push_send_base[e] their first row
+  // at the owner; -1 = send nothing), each row's origin into push_src, and
+  // add each finished run to the owner's push_arrived[local expert].  The
+  // GEMM loads a group's tiles only once arrived[g] reaches counts[g].
+  const void* push_x = nullptr;
+  const int32_t* push_sorted_token = nullptr;
+  const int32_t* push_counts = nullptr;
+  const int32_t* push_send_base = nullptr;
+  char* push_rows[8] = {};
+  int32_t* push_src[8] = {};
+  uint32_t* push_arrived[8] = {};
+  const uint32_t* arrived = nullptr;
+  int64_t push_A = 0;
+  int64_t push_cap = 0;
+  int push_E = 0, push_El = 0, push_world = 0, push_me = 0;
 };
 constexpr uint32_t kEpSrcShift = 28;  // row origin = (source rank << 28) | source position
 cudaError_t launch_grouped_gemm_sm100(const GroupedGemmArgs& args, cudaStream_t stream);

@@ -312,8 +312,8 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant_
 // bg) runs the one-fma-per-k chains of blocks bg, bg + nbg, ... for all
 // kFixG tokens at once, the block sums are then added in block order, and
 // one warp per token routes it.
-constexpr int kFixThreads = 256;
-constexpr int kFixG = 4;        // tokens per CTA pass
+constexpr int kFixThreads = 512;  // 64 experts x 8 block lanes (E <= 64), 128 x 4 (E <= 128)
+constexpr int kFixG = 4;          // tokens per CTA pass
 
 template <int NV>
 __global__ void __launch_bounds__(kFixThreads)
@@ -323,7 +323,7 @@ router_fixup_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__
                     int32_t* __restrict__ topk_idx, float* __restrict__ topk_w_f32,
                     void* __restrict__ topk_w_dtype, uint16_t* __restrict__ logits_out) {
   constexpr int EP = NV * 32;
-  constexpr int NBG = kFixThreads / EP;       // block lanes per expert (4 / 2)
+  constexpr int NBG = kFixThreads / EP;       // block lanes per expert (8 / 4)
   extern __shared__ float fsm[];
   const int nb = cdiv(d, kLogitBlock);
   float* xs = fsm;                                        // [kFixG][d]
@@ -349,19 +349,33 @@ router_fixup_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__
     }
     __syncthreads();
     const uint16_t* wr = w + static_cast<int64_t>(min(e, E - 1)) * d;
+    // A block's weights (64 k, 8 vectors) are loaded before its FMAs; the
+    // token values come from shared memory four at a time.
+    constexpr int kVec = kLogitBlock / 8;
     for (int b = bg; b < nb; b += NBG) {
-      const int k0 = b * kLogitBlock, kn = min(kLogitBlock, d - k0);
+      const int k0 = b * kLogitBlock, nvec = min(kLogitBlock, d - k0) / 8;
+      uint4 wb[kVec];
+#pragma unroll
+      for (int c = 0; c < kVec; ++c)
+        wb[c] = c < nvec ? __ldg(reinterpret_cast<const uint4*>(wr + k0) + c) : make_uint4(0, 0, 0, 0);
       float acc[kFixG];
 #pragma unroll
       for (int g = 0; g < kFixG; ++g) acc[g] = 0.0f;
-      for (int c = 0; c < kn / 8; ++c) {
-        const uint4 u = __ldg(reinterpret_cast<const uint4*>(wr + k0) + c);
-        const float wv[8] = {bf16_lo(u.x), bf16_hi(u.x), bf16_lo(u.y), bf16_hi(u.y),
-                             bf16_lo(u.z), bf16_hi(u.z), bf16_lo(u.w), bf16_hi(u.w)};
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
+      for (int c = 0; c < kVec; ++c) {
+        if (c < nvec) {
+          const uint4 u = wb[c];
+          const float wv[8] = {bf16_lo(u.x), bf16_hi(u.x), bf16_lo(u.y), bf16_hi(u.y),
+                               bf16_lo(u.z), bf16_hi(u.z), bf16_lo(u.w), bf16_hi(u.w)};
 #pragma unroll
-          for (int g = 0; g < kFixG; ++g) acc[g] = fmaf(xs[g * d + k0 + c * 8 + j], wv[j], acc[g]);
+          for (int g = 0; g < kFixG; ++g) {
+            const float4* xv = reinterpret_cast<const float4*>(xs + g * d + k0 + c * 8);
+            const float4 xa = xv[0], xb = xv[1];
+            const float xr[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc[g] = fmaf(xr[j], wv[j], acc[g]);
+          }
+        }
       }
 #pragma unroll
       for (int g = 0; g < kFixG; ++g) part[(g * EP + e) * nb + b] = acc[g];

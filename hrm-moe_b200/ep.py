@@ -187,11 +187,11 @@ class PeerExpertParallel:
                 marks=None):
         """y [T, d] for this rank's tokens x [T, d] (T <= max_tokens).
 
-        ``marks`` (optional, 6 torch.cuda.Event) are recorded before the
-        router, after the count exchange, after the rows have landed, after
-        the gate_up GEMM, after the down GEMM has stored every result back at
-        its source (bf16: the return runs inside that GEMM) and after the
-        combine.
+        ``marks`` (optional, 6 torch.cuda.Event) are recorded between the
+        stages (see hmoe_ep_forward_marked): for bf16 before the router, after
+        the router and index-only dispatch, after the count exchange, after
+        the gate_up GEMM with the fused row push, after the down GEMM with the
+        fused return, and after the combine.
         """
         ct, lib = self._ct, self._lib.load()
         T, d = x.shape

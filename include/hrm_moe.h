@@ -249,10 +249,13 @@ int hmoe_ep_forward(const hmoe_shape* shape, int64_t max_tokens, int32_t rank, i
                     void* stream);
 /*
  * hmoe_ep_forward that also records six caller-owned cudaEvent_t on the
- * stream: before the router, after the count exchange, after every peer's
- * rows have landed, after the gate_up GEMM, after the down GEMM has stored
- * every result back at its source (bf16: the return runs inside that GEMM),
- * and after the combine.  Same kernels, same results.
+ * stream.  bf16: before the router, after the router and the index-only
+ * dispatch, after the count exchange, after the gate_up GEMM (whose sender
+ * warps push the rows to their owners while it runs), after the down GEMM
+ * has stored every result back at its source, and after the combine.  fp32:
+ * before the router, after the count exchange, after every peer's rows have
+ * landed, after the gate_up GEMM, after the results are back, and after the
+ * combine.  Same kernels, same results.
  */
 int hmoe_ep_forward_marked(const hmoe_shape* shape, int64_t max_tokens, int32_t rank,
                            int32_t world, void* const* peer_bases, uint32_t epoch, const void* x,
