@@ -54,7 +54,7 @@ constexpr int kTmemCols = kAccCols * kNumAcc; // 512 = all of TMEM
 // takes one per quadrant with two TMA staging boxes each.
 template <bool SWIGLU, bool SCATTER>
 __host__ __device__ constexpr int epi_warps() { return SWIGLU ? 8 : 4; }
-constexpr int kPushWarps = 4;  // row senders of the fused expert-parallel dispatch
+constexpr int kPushWarps = 8;  // row senders of the fused expert-parallel dispatch
 template <bool SWIGLU, bool SCATTER, bool PUSH>
 __host__ __device__ constexpr int num_threads() {  // + producer, MMA issuer (+ senders)
   return 64 + 32 * epi_warps<SWIGLU, SCATTER>() + (PUSH ? 32 * kPushWarps : 0);
@@ -204,26 +204,22 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
 // call has failed (the owners' waits then run out and report it).
 constexpr int kPushChunk = 16;
 
-// Copy up to two rows (a null source skips its row), 16 bytes per lane at a
-// time, with every load of a 4 KiB span issued before its stores.
-__device__ __forceinline__ void push_copy_rows2(const uint4* const (&src)[2], uint4* const (&dst)[2],
-                                                int rc, int lane) {
+// Copy one row, 16 bytes per lane, every load of a 4 KiB span issued before
+// its stores.
+__device__ __forceinline__ void push_copy_row(const uint4* __restrict__ src, uint4* dst, int rc,
+                                              int lane) {
   for (int c0 = 0; c0 < rc; c0 += 256) {
-    uint4 buf[2][8];
+    uint4 buf[8];
 #pragma unroll
-    for (int r = 0; r < 2; ++r)
+    for (int s = 0; s < 8; ++s) {
+      const int c = c0 + lane + 32 * s;
+      if (c < rc) buf[s] = __ldg(src + c);
+    }
 #pragma unroll
-      for (int s = 0; s < 8; ++s) {
-        const int c = c0 + lane + 32 * s;
-        if (src[r] && c < rc) buf[r][s] = __ldg(src[r] + c);
-      }
-#pragma unroll
-    for (int r = 0; r < 2; ++r)
-#pragma unroll
-      for (int s = 0; s < 8; ++s) {
-        const int c = c0 + lane + 32 * s;
-        if (dst[r] && c < rc) dst[r][c] = buf[r][s];
-      }
+    for (int s = 0; s < 8; ++s) {
+      const int c = c0 + lane + 32 * s;
+      if (c < rc) dst[c] = buf[s];
+    }
   }
 }
 
@@ -252,29 +248,19 @@ __device__ __forceinline__ void push_rows(const KParams& p, const SmemCtl& ctl, 
       const int eb = ctl.push_ebase[e];
       uint4* rows = p.push_rows[o];
       int32_t* srcs = p.push_src[o];
-      for (int64_t vv = v; vv < seg_end; vv += 2) {
-        // two rows in flight: both rows' loads are issued before either store
-        const uint4* src[2];
-        uint4* dst[2];
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-          src[r] = nullptr;
-          dst[r] = nullptr;
-          const int64_t rel = vv + r - vs;
-          const int64_t q = sb + rel;
-          if (vv + r >= seg_end) continue;
-          if (q >= p.push_cap) {
-            if (lane == 0) record_error(p.err, kDevEpOverflow);
-            continue;
-          }
-          const int pos = eb + static_cast<int>(rel);
-          src[r] = p.push_x + static_cast<int64_t>(p.push_sorted_token[pos]) * rc;
-          dst[r] = rows + q * rc;
-          if (lane == 0)
-            srcs[q] = static_cast<int32_t>((static_cast<uint32_t>(p.push_me) << kEpSrcShift) |
-                                           static_cast<uint32_t>(pos));
+      for (int64_t vv = v; vv < seg_end; ++vv) {
+        const int64_t rel = vv - vs;
+        const int64_t q = sb + rel;
+        if (q >= p.push_cap) {
+          if (lane == 0) record_error(p.err, kDevEpOverflow);
+          continue;
         }
-        push_copy_rows2(src, dst, rc, lane);
+        const int pos = eb + static_cast<int>(rel);
+        const int t = p.push_sorted_token[pos];
+        push_copy_row(p.push_x + static_cast<int64_t>(t) * rc, rows + q * rc, rc, lane);
+        if (lane == 0)
+          srcs[q] = static_cast<int32_t>((static_cast<uint32_t>(p.push_me) << kEpSrcShift) |
+                                         static_cast<uint32_t>(pos));
       }
       __threadfence_system();
       __syncwarp();
