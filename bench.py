@@ -105,11 +105,24 @@ class ClockSampler:
                  "-lms", "200", "-i", self.gpu_id], stdout=self.f, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
+            return self
+        # nvidia-smi takes a while to start on a many-GPU box: begin the timed
+        # region only once it is sampling.  (Sampling much faster than every
+        # 200 ms delays kernel launches and shows up in the step time.)
+        deadline = time.time() + 10.0
+        while time.time() < deadline and self.proc.poll() is None:
+            self.f.flush()
+            if self.path.stat().st_size > 0:
+                break
+            time.sleep(0.01)
+        self.skip = self.path.read_text().count("\n")  # samples taken before the region
         return self
 
     def __exit__(self, *exc):
         if self.proc is not None:
-            time.sleep(0.25)
+            self.f.flush()
+            self.stop = self.path.read_text().count("\n")  # samples up to the region's end
+            time.sleep(0.1)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -123,7 +136,13 @@ class ClockSampler:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         sm, smax, power, reasons = [], [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.path.read_text().splitlines():
+        lines = self.path.read_text().splitlines()
+        skip, stop = getattr(self, "skip", 0), getattr(self, "stop", len(lines))
+        # the region's own samples; a region shorter than one interval gets the
+        # first sample after it (still this workload's clocks), and says so
+        inside = lines[skip:stop]
+        after = not inside
+        for line in (inside or lines[stop:stop + 1]):
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 9:
                 continue
@@ -140,8 +159,11 @@ class ClockSampler:
         if not sm:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
         loaded = [s for s in sm if s > 0.5 * max(sm)] or sm
-        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(smax),
-                "power_w_max": max(power), "samples": len(sm), "reasons": sorted(reasons)}
+        out = {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(smax),
+               "power_w_max": max(power), "samples": len(sm), "reasons": sorted(reasons)}
+        if after:
+            out["sampled_after_region"] = True
+        return out
 
 
 def gpu_uuid(torch, dev: int) -> str:
