@@ -54,8 +54,8 @@ NCU_TRAFFIC_BYTES = {
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=300)  # >= one 200 ms clock sample at N=1
+    ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--config", default="cfg2_xl64_bf16")
     ap.add_argument("--tokens", type=int, default=0, help="tokens per GPU (default: the config's)")
