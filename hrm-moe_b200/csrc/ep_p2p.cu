@@ -461,7 +461,7 @@ cudaError_t ep_forward_launch(const hmoe_shape& s, int64_t max_tokens, int rank,
     g.push_world = world;
     g.push_me = rank;
     if ((e = launch_grouped_gemm_sm100(g, st)) != cudaSuccess) return e;
-    g.push_x = nullptr;
+    g.arrived = nullptr;  // the down GEMM below does not wait for rows
   } else {
     const unsigned disp_grid =
         static_cast<unsigned>(s.tokens > 0 ? cdiv64(s.tokens, kEpThreads / 32) : 1);

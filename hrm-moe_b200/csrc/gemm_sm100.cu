@@ -708,9 +708,13 @@ cudaError_t launch_grouped_gemm_sm100(const GroupedGemmArgs& a, cudaStream_t str
   const int sms = a.sm_limit > 0 ? a.sm_limit : num_sms_for_current_device();
   const int64_t max_tiles = (cdiv64(a.M, BM) + a.G) * p.n_tiles;
   const int grid = static_cast<int>(max_tiles < sms ? max_tiles : sms);
-  const bool push = a.push_x != nullptr;
+  // fused dispatch: keyed on the arrival counters (a rank with no tokens of
+  // its own still waits for its peers' rows)
+  const bool push = a.arrived != nullptr;
   if (push && (!a.swiglu || scatter || a.push_world < 1 || a.push_world > 8 || a.push_E > 128 ||
-               a.push_E != a.push_world * a.push_El || !a.arrived || (a.K * 2) % 16 != 0))
+               a.push_E != a.push_world * a.push_El || (a.K * 2) % 16 != 0 ||
+               (a.push_A > 0 && (!a.push_x || !a.push_sorted_token || !a.push_counts ||
+                                 !a.push_send_base))))
     return cudaErrorInvalidValue;
   p.push_x = static_cast<const uint4*>(a.push_x);
   p.push_sorted_token = a.push_sorted_token;

@@ -92,7 +92,8 @@ struct GroupedGemmArgs {
   // pos, push_counts[e] rows of expert e, push_send_base[e] their first row
   // at the owner; -1 = send nothing), each row's origin into push_src, and
   // add each finished run to the owner's push_arrived[local expert].  The
-  // GEMM loads a group's tiles only once arrived[g] reaches counts[g].
+  // GEMM loads a group's tiles only once arrived[g] reaches counts[g].  Set
+  // `arrived` to select this mode (push_x may be null when push_A is 0).
   const void* push_x = nullptr;
   const int32_t* push_sorted_token = nullptr;
   const int32_t* push_counts = nullptr;

@@ -31,11 +31,16 @@ def main(out_path):
         syn = importlib.import_module("hrm-moe_b200.synthetic")
         ep = importlib.import_module("hrm-moe_b200.ep")
         ops = importlib.import_module("hrm-moe_b200.ops")
+        # T < 0: rank 0 has no tokens (the others have |T| + 37 * rank)
         for (T, d, E, I, k, skew, dtype) in [(1000, 256, 8 * world, 128, 4, False, "bf16"),
                                               (4096, 1536, 64, 512, 8, False, "bf16"),
                                               (777, 256, 4 * world, 64, 2, True, "bf16"),
-                                              (300, 128, 2 * world, 64, 2, False, "f32")]:
-            shape = syn.MoEShape(T + 37 * rank, d, E, I, k, True, dtype)
+                                              (300, 128, 2 * world, 64, 2, False, "f32"),
+                                              (-200, 256, 4 * world, 64, 4, False, "bf16"),
+                                              (-200, 128, 2 * world, 64, 2, False, "f32")]:
+            tokens = 0 if (T < 0 and rank == 0) else abs(T) + 37 * rank
+            T = abs(T)
+            shape = syn.MoEShape(tokens, d, E, I, k, True, dtype)
             tdt = torch.bfloat16 if dtype == "bf16" else torch.float32
             inp = syn.make_inputs(shape, seed=21, rank=rank)
             wr = inp.w_router
