@@ -49,6 +49,7 @@ struct RCfg {
   static constexpr int kCtlBytes = 256;
   static constexpr size_t kSmem = 1024 + kMainBytes + kCtlBytes;
   static_assert(kStageBytes % 1024 == 0, "stages keep the 1 KiB swizzle alignment");
+  static_assert(kStages <= 8, "RtCtl holds eight stage barriers of each kind");
   static_assert(kSmem <= 232448, "shared memory budget");
 };
 
@@ -312,6 +313,30 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant_
 // bg) runs the one-fma-per-k chains of blocks bg, bg + nbg, ... for all
 // kFixG tokens at once, the block sums are then added in block order, and
 // one warp per token routes it.
+// One warp routes one token from its exact-order logits lrow[0..E) (bias
+// included, not yet rounded): the same selection and weights as every router.
+template <int NV>
+__device__ __forceinline__ void fixup_route_token(const float* lrow, int64_t t, int E, int k,
+                                                  int norm, int lane, int32_t* topk_idx,
+                                                  float* topk_w_f32, void* topk_w_dtype,
+                                                  uint16_t* logits_out) {
+  float r[NV], sel[NV];
+  int id[NV];
+#pragma unroll
+  for (int q = 0; q < NV; ++q) {
+    const int ee = lane + 32 * q;
+    r[q] = ee < E ? round_bf16(lrow[ee]) : -INFINITY;
+    sel[q] = r[q];
+    id[q] = ee < E ? ee : INT_MAX;
+    if (logits_out && ee < E) logits_out[t * E + ee] = static_cast<uint16_t>(f32_to_bf16_bits(r[q]));
+  }
+  float my_v, mx;
+  int my_i;
+  warp_topk<NV>(sel, id, k, lane, my_v, my_i, mx);
+  const float wgt = warp_route_weight<NV, true>(r, E, k, norm, lane, my_v, mx);
+  write_route<true>(t, k, lane, my_i, wgt, topk_idx, topk_w_f32, topk_w_dtype);
+}
+
 constexpr int kFixThreads = 512;  // 64 experts x 8 block lanes (E <= 64), 128 x 4 (E <= 128)
 constexpr int kFixG = 4;          // tokens per CTA pass
 
@@ -389,24 +414,9 @@ router_fixup_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__
       lgt[g * EP + ee] = tot;
     }
     __syncthreads();
-    if (wib < kFixG && tok[wib] >= 0) {
-      const int64_t t = tok[wib];
-      float r[NV], sel[NV];
-      int id[NV];
-#pragma unroll
-      for (int q = 0; q < NV; ++q) {
-        const int ee = lane + 32 * q;
-        r[q] = ee < E ? round_bf16(lgt[wib * EP + ee]) : -INFINITY;
-        sel[q] = r[q];
-        id[q] = ee < E ? ee : INT_MAX;
-        if (logits_out && ee < E) logits_out[t * E + ee] = static_cast<uint16_t>(f32_to_bf16_bits(r[q]));
-      }
-      float my_v, mx;
-      int my_i;
-      warp_topk<NV>(sel, id, k, lane, my_v, my_i, mx);
-      const float wgt = warp_route_weight<NV, true>(r, E, k, norm, lane, my_v, mx);
-      write_route<true>(t, k, lane, my_i, wgt, topk_idx, topk_w_f32, topk_w_dtype);
-    }
+    if (wib < kFixG && tok[wib] >= 0)
+      fixup_route_token<NV>(lgt + wib * EP, tok[wib], E, k, norm, lane, topk_idx, topk_w_f32,
+                            topk_w_dtype, logits_out);
     __syncthreads();
   }
 }
@@ -428,6 +438,135 @@ EncodeTiledFn encode_fn() {
       fn = reinterpret_cast<EncodeTiledFn>(ptr);
   });
   return fn;
+}
+
+// Fix-up for E <= 64 with the whole router weight in shared memory: TMA
+// brings W in [64 expert x 64 k] boxes (128-byte swizzle, the router's own
+// map), so the weights are read from HBM/L2 once per CTA in large copies
+// instead of one 16-byte load per thread and step.  Thread (expert e, token
+// g) then runs every 64-k block of its logit in the exact order (one fma per
+// k from +0, block sums added in ascending order from +0, then the bias), so
+// the result is bit-identical to router_fixup_kernel.  Its 16-byte weight
+// reads sit at e*128 + ((c ^ (e & 7)) * 16): four wavefronts per warp, the
+// minimum for 512 bytes.
+constexpr int kFixSmG = 4;  // tokens per CTA pass
+
+__global__ void __launch_bounds__(64 * kFixSmG)
+router_fixup_wsmem_kernel(const __grid_constant__ CUtensorMap tmW, const uint16_t* __restrict__ x,
+                          const uint16_t* __restrict__ bias, int64_t T, int d, int E, int k, int norm,
+                          const int* __restrict__ fix_count, const int32_t* __restrict__ fix_list,
+                          int32_t* __restrict__ topk_idx, float* __restrict__ topk_w_f32,
+                          void* __restrict__ topk_w_dtype, uint16_t* __restrict__ logits_out,
+                          int* err, unsigned long long wait_limit_ns) {
+  extern __shared__ uint8_t fraw[];
+  uint8_t* wsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(fraw) + 1023) &
+                                            ~static_cast<uintptr_t>(1023));
+  const int nb = cdiv(d, kLogitBlock);
+  float* xs = reinterpret_cast<float*>(wsm + static_cast<size_t>(nb) * 8192);  // [G][d]
+  float* lgt = xs + kFixSmG * d;                                                 // [G][64]
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  const int tid = threadIdx.x, lane = tid & 31, wib = tid >> 5;
+  const int n = *fix_count;
+  if (static_cast<int64_t>(blockIdx.x) * kFixSmG >= n) return;  // nothing listed for this CTA
+  if (tid == 0) {
+    abort_flag = 0;
+    mbar_init(smem_u32(&bar), 1);
+    fence_mbar_init();
+    mbar_arrive_expect_tx(smem_u32(&bar), static_cast<uint32_t>(nb) * 8192u);
+    for (int b = 0; b < nb; ++b) tma_load_2d(smem_u32(wsm + b * 8192), &tmW, b * kLogitBlock, 0, smem_u32(&bar));
+  }
+  __syncthreads();
+  bool have_w = false;
+  const int e = tid & 63, g = tid >> 6;
+  for (int64_t base = static_cast<int64_t>(blockIdx.x) * kFixSmG; base < n;
+       base += static_cast<int64_t>(gridDim.x) * kFixSmG) {
+    int64_t tok[kFixSmG];
+#pragma unroll
+    for (int j = 0; j < kFixSmG; ++j) {
+      const int64_t tt = base + j < n ? fix_list[base + j] : -1;
+      tok[j] = (tt >= 0 && tt < T) ? tt : -1;
+    }
+    // token rows -> fp32 in shared memory; each thread's loads are all issued
+    // before its stores
+    constexpr int kXLoads = 8;
+    const int nx = kFixSmG * (d / 8);
+    for (int i0 = tid; i0 < nx; i0 += blockDim.x * kXLoads) {
+      uint4 u[kXLoads];
+#pragma unroll
+      for (int q = 0; q < kXLoads; ++q) {
+        const int i = i0 + q * blockDim.x;
+        u[q] = make_uint4(0, 0, 0, 0);
+        if (i < nx) {
+          const int j = i / (d / 8), c = i % (d / 8);
+          if (tok[j] >= 0) u[q] = __ldg(reinterpret_cast<const uint4*>(x + tok[j] * d) + c);
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < kXLoads; ++q) {
+        const int i = i0 + q * blockDim.x;
+        if (i < nx) {
+          const int j = i / (d / 8), c = i % (d / 8);
+          float* xr = xs + j * d + c * 8;
+          xr[0] = bf16_lo(u[q].x); xr[1] = bf16_hi(u[q].x); xr[2] = bf16_lo(u[q].y);
+          xr[3] = bf16_hi(u[q].y); xr[4] = bf16_lo(u[q].z); xr[5] = bf16_hi(u[q].z);
+          xr[6] = bf16_lo(u[q].w); xr[7] = bf16_hi(u[q].w);
+        }
+      }
+    }
+    if (!have_w) {  // every thread sees the weights land (bounded)
+      have_w = mbar_wait_bounded(smem_u32(&bar), 0, &abort_flag, err, wait_limit_ns);
+      if (!have_w) return;  // the copies are gone or the error is recorded
+    }
+    __syncthreads();
+    // Four blocks' chains at a time (independent accumulators hide the fma
+    // latency); their sums are added to the total in ascending block order.
+    constexpr int kIl = 4;
+    float tot = 0.0f;
+    for (int b0 = 0; b0 < nb; b0 += kIl) {
+      float acc[kIl];
+      int nvec[kIl];
+#pragma unroll
+      for (int q = 0; q < kIl; ++q) {
+        acc[q] = 0.0f;
+        nvec[q] = b0 + q < nb ? min(kLogitBlock, d - (b0 + q) * kLogitBlock) / 8 : 0;
+      }
+#pragma unroll
+      for (int c = 0; c < kLogitBlock / 8; ++c) {
+#pragma unroll
+        for (int q = 0; q < kIl; ++q) {
+          if (c < nvec[q]) {
+            const uint8_t* box = wsm + (b0 + q) * 8192 + e * 128;
+            const float* xb = xs + g * d + (b0 + q) * kLogitBlock;
+            const uint4 u = *reinterpret_cast<const uint4*>(box + ((c ^ (e & 7)) << 4));
+            const float4 xa = reinterpret_cast<const float4*>(xb + c * 8)[0];
+            const float4 xc = reinterpret_cast<const float4*>(xb + c * 8)[1];
+            float a = acc[q];
+            a = fmaf(xa.x, bf16_lo(u.x), a);
+            a = fmaf(xa.y, bf16_hi(u.x), a);
+            a = fmaf(xa.z, bf16_lo(u.y), a);
+            a = fmaf(xa.w, bf16_hi(u.y), a);
+            a = fmaf(xc.x, bf16_lo(u.z), a);
+            a = fmaf(xc.y, bf16_hi(u.z), a);
+            a = fmaf(xc.z, bf16_lo(u.w), a);
+            a = fmaf(xc.w, bf16_hi(u.w), a);
+            acc[q] = a;
+          }
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < kIl; ++q)
+        if (b0 + q < nb) tot = tot + acc[q];
+    }
+    if (bias && e < E) tot = tot + bf16_bits_to_f32(bias[e]);
+    lgt[g * 64 + e] = tot;
+    __syncthreads();
+    if (wib < kFixSmG && tok[wib] >= 0)
+      fixup_route_token<2>(lgt + wib * 64, tok[wib], E, k, norm, lane, topk_idx, topk_w_f32,
+                           topk_w_dtype, logits_out);
+    __syncthreads();
+  }
+  if (!have_w) mbar_wait_bounded(smem_u32(&bar), 0, &abort_flag, err, wait_limit_ns);
 }
 
 bool map_rows(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
@@ -466,6 +605,9 @@ cudaError_t launch_tc(const void* x, const void* w, const RtParams& p, cudaStrea
       e = cudaFuncSetAttribute(router_fixup_kernel<NV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                232448);
       if (e != cudaSuccess) return e;
+      e = cudaFuncSetAttribute(router_fixup_wsmem_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               232448 - 64);
+      if (e != cudaSuccess) return e;
       done[dev] = 1;
     }
   }
@@ -478,10 +620,19 @@ cudaError_t launch_tc(const void* x, const void* w, const RtParams& p, cudaStrea
       mx, mw, p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  router_fixup_kernel<NV><<<num_sms_for_current_device() * 2, kFixThreads, fix_smem, st>>>(
-      static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(w), p.bias, p.T, p.d, p.E,
-      p.k, p.norm, p.fix_count, p.fix_list, p.topk_idx, p.topk_w_f32, p.topk_w_dtype,
-      p.logits_out);
+  const size_t wsm_smem = 1024 + static_cast<size_t>(cdiv(p.d, kLogitBlock)) * 8192 +
+                          sizeof(float) * (static_cast<size_t>(kFixSmG) * p.d + kFixSmG * 64);
+  if (EPAD == 64 && wsm_smem <= 232448 - 64) {
+    router_fixup_wsmem_kernel<<<num_sms_for_current_device(), 64 * kFixSmG, wsm_smem, st>>>(
+        mw, static_cast<const uint16_t*>(x), p.bias, p.T, p.d, p.E, p.k, p.norm, p.fix_count,
+        p.fix_list, p.topk_idx, p.topk_w_f32, p.topk_w_dtype, p.logits_out, p.err,
+        p.wait_limit_ns);
+  } else {
+    router_fixup_kernel<NV><<<num_sms_for_current_device() * 2, kFixThreads, fix_smem, st>>>(
+        static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(w), p.bias, p.T, p.d, p.E,
+        p.k, p.norm, p.fix_count, p.fix_list, p.topk_idx, p.topk_w_f32, p.topk_w_dtype,
+        p.logits_out);
+  }
   return cudaGetLastError();
 }
 
