@@ -63,6 +63,8 @@ def parse_args():
                     help="target duration of the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--e2e-chunk", type=int, default=4096,
+                    help="tokens per host-copy chunk of the end-to-end measurement")
     ap.add_argument("--no-graph", action="store_true",
                     help="N=1: time eager launches instead of one CUDA graph per step")
     ap.add_argument("--ep-impl", default="peer", choices=["peer", "nccl"],
@@ -411,7 +413,7 @@ def b200_arm(args, rank, world, local_rank):
     if not args.no_e2e and ep is None:
         x_host = x.cpu().pin_memory()
         y_host = torch.empty_like(x_host).pin_memory()
-        chunk = min(T, 4096)
+        chunk = min(T, args.e2e_chunk)
         cs = ops.make_shape(T, d, E, I, k, dt, shape.norm_topk_prob)
         hws = torch.empty(lib.hmoe_ffn_host_workspace_bytes(ctypes.byref(cs), chunk),
                           dtype=torch.uint8, device=dev)

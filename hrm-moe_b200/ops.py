@@ -329,6 +329,69 @@ def ffn_forward(x: torch.Tensor, w_router: torch.Tensor, w_gate_up: torch.Tensor
     return (out, routing) if return_routing else out
 
 
+class CapturedFfn:
+    """The layer forward captured once as a CUDA graph over fixed buffers.
+
+    For serving loops with a fixed token count: the kernels of one forward
+    (router, dispatch, the two grouped GEMMs, combine) are replayed as one
+    graph launch, which removes the per-kernel launch gaps.  ``x_static`` is
+    the graph's input and ``y`` its output; ``__call__(x)`` copies ``x`` into
+    the input (same shape and dtype), replays the graph on the current stream
+    and returns ``y`` (overwritten by the next call).  Same kernels and
+    results as :func:`ffn_forward`.
+    """
+
+    def __init__(self, x: torch.Tensor, w_router: torch.Tensor, w_gate_up: torch.Tensor,
+                 w_down: torch.Tensor, top_k: int, norm_topk_prob: bool,
+                 router_bias: Optional[torch.Tensor] = None):
+        T, d = x.shape
+        if T == 0:
+            raise ValueError("nothing to capture for 0 tokens")
+        dev = _require_cuda(x, w_router, w_gate_up, w_down, router_bias)
+        dt = x.dtype
+        E = w_router.shape[0]
+        I = w_gate_up.shape[1] // 2
+        if tuple(w_gate_up.shape) != (E, 2 * I, d) or tuple(w_down.shape) != (E, d, I):
+            raise ValueError(f"expert weights {tuple(w_gate_up.shape)} / {tuple(w_down.shape)} do "
+                             f"not match hidden size {d} and {E} experts")
+        self.x_static = x.detach().clone().contiguous()
+        self.y = torch.empty_like(self.x_static)
+        self._w = [w_router.to(dt).contiguous(), w_gate_up.to(dt).contiguous(),
+                   w_down.to(dt).contiguous(),
+                   None if router_bias is None else router_bias.to(dt).contiguous()]
+        self._shape = _lib.HmoeShape(T, d, E, I, top_k, dtype_code(dt), 1 if norm_topk_prob else 0)
+        lib = _lib.load()
+        nbytes = lib.hmoe_ffn_workspace_bytes(ctypes.byref(self._shape))
+        if nbytes == 0:
+            raise ValueError(_lib.last_error())
+        self._ws = _workspace(nbytes, dev)
+        self._launch(torch.cuda.current_stream(dev))  # first call: per-device set-up
+        torch.cuda.current_stream(dev).synchronize()
+        cap = torch.cuda.Stream(dev)
+        cap.wait_stream(torch.cuda.current_stream(dev))
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=cap, capture_error_mode="relaxed"):
+            self._launch(cap)
+        torch.cuda.current_stream(dev).wait_stream(cap)
+
+    def _launch(self, stream: torch.cuda.Stream) -> None:
+        wr, wgu, wd, b = self._w
+        lib = _lib.load()
+        _lib.check(lib.hmoe_ffn_forward(
+            ctypes.byref(self._shape), _ptr(self.x_static), _ptr(wr), _ptr(b), _ptr(wgu), _ptr(wd),
+            _ptr(self.y), 0, None, None, None, None, _ptr(self._ws), self._ws.numel(),
+            ctypes.c_void_p(stream.cuda_stream)))
+
+    def __call__(self, x: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if x is not None:
+            if x.shape != self.x_static.shape or x.dtype != self.x_static.dtype:
+                raise ValueError(f"captured for {tuple(self.x_static.shape)} {self.x_static.dtype}, "
+                                 f"got {tuple(x.shape)} {x.dtype}")
+            self.x_static.copy_(x, non_blocking=True)
+        self.graph.replay()
+        return self.y
+
+
 def ffn_forward_host(x_host: torch.Tensor, w_router: torch.Tensor, w_gate_up: torch.Tensor,
                      w_down: torch.Tensor, top_k: int, norm_topk_prob: bool,
                      router_bias: Optional[torch.Tensor] = None,

@@ -42,3 +42,22 @@ def test_grouped_linear_op_matches_ops():
     a = torch.randn(M, 256, generator=g, device="cuda").bfloat16()
     wt = (torch.randn(4, 384, 256, generator=g, device="cuda") * 0.05).bfloat16()
     assert torch.equal(torch.ops.hrm_moe.grouped_linear(a, wt, counts), ops.grouped_linear(a, wt, counts))
+
+
+def test_captured_forward_replays_the_same_kernels():
+    ops = get_ops()
+    syn = synthetic()
+    shape = syn.MoEShape(1000, 1536, 64, 512, 8, True, "bf16")
+    a = syn.make_inputs(shape, seed=41)
+    b = syn.make_inputs(shape, seed=42)
+    w = [to_dev(t, "bf16") for t in (a.w_router, a.w_gate_up, a.w_down)]
+    xa, xb = to_dev(a.x, "bf16"), to_dev(b.x, "bf16")
+    cap = ops.CapturedFfn(xa, *w, 8, True)
+    ya = cap().clone()
+    yb = cap(xb).clone()
+    ya2 = cap(xa).clone()
+    assert torch.equal(ya, ops.ffn_forward(xa, *w, 8, True))
+    assert torch.equal(yb, ops.ffn_forward(xb, *w, 8, True))
+    assert torch.equal(ya2, ya)
+    with pytest.raises(ValueError):
+        cap(xa[:10])
