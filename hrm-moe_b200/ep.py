@@ -250,17 +250,32 @@ class SparseMoEExpertParallelSwiGLU(torch.nn.Module):
     (models/layers.py:406): ``gate.weight`` [E, d] replicated,
     ``experts.local_experts.gate_up_weight`` [E/R, 2I, d] and
     ``experts.local_experts.down_weight`` [E/R, d, I] for this rank's experts.
+
+    ``transport="nccl"`` (default) exchanges rows with NCCL all_to_all, as
+    the reference does.  ``transport="peer"`` runs the fused peer-memory path
+    (:class:`PeerExpertParallel`): it needs ``max_tokens`` (the most tokens any
+    rank passes in one call, the same value on every rank), allocates its
+    regions collectively on the first forward, and must be released with
+    :meth:`close` (collective) before the process group goes away.
     """
 
     def __init__(self, hidden_size: int, intermediate_size: int, num_experts: int, top_k: int,
-                 norm_topk_prob: bool, group=None, **kwargs):
+                 norm_topk_prob: bool, group=None, transport: str = "nccl",
+                 max_tokens: Optional[int] = None, **kwargs):
         super().__init__()
         from .layers import LinearInit, SparseMoEGroupedExperts
         world = dist.get_world_size(group) if dist.is_initialized() else 1
         if num_experts % world:
             raise ValueError(f"num_experts={num_experts} must divide world_size={world}")
+        if transport not in ("nccl", "peer"):
+            raise ValueError(f"transport must be 'nccl' or 'peer', got {transport!r}")
+        if transport == "peer" and not max_tokens:
+            raise ValueError("transport='peer' needs max_tokens")
         self.group = group
+        self.transport = transport
+        self.max_tokens = max_tokens
         self.hidden_size = hidden_size
+        self.intermediate_size = intermediate_size
         self.num_experts = num_experts
         self.top_k = top_k
         self.norm_topk_prob = norm_topk_prob
@@ -268,6 +283,7 @@ class SparseMoEExpertParallelSwiGLU(torch.nn.Module):
         self.experts = torch.nn.Module()
         self.experts.local_experts = SparseMoEGroupedExperts(hidden_size, intermediate_size,
                                                              num_experts // world, **kwargs)
+        self._peer = None
 
     def forward(self, x, moe_context=None, total_seqlen=None, **_seq_info):
         from .layers import _check_no_grad
@@ -275,7 +291,22 @@ class SparseMoEExpertParallelSwiGLU(torch.nn.Module):
         _check_no_grad(x, self.gate.weight, le.gate_up_weight, le.down_weight)
         shape = x.shape
         h = x.reshape(-1, self.hidden_size)
-        y = ep_forward(h, self.gate.weight.to(h.dtype), le.gate_up_weight.to(h.dtype),
-                       le.down_weight.to(h.dtype), self.num_experts, self.top_k,
-                       self.norm_topk_prob, group=self.group)
+        wr, wgu, wd = (self.gate.weight.to(h.dtype), le.gate_up_weight.to(h.dtype),
+                       le.down_weight.to(h.dtype))
+        if self.transport == "peer":
+            if self._peer is None:
+                self._peer = PeerExpertParallel(self.hidden_size, self.intermediate_size,
+                                                self.num_experts, self.top_k, self.norm_topk_prob,
+                                                max_tokens=self.max_tokens, dtype=h.dtype,
+                                                group=self.group)
+            y = self._peer.forward(h, wr.contiguous(), wgu.contiguous(), wd.contiguous())
+        else:
+            y = ep_forward(h, wr, wgu, wd, self.num_experts, self.top_k, self.norm_topk_prob,
+                           group=self.group)
         return y.reshape(shape)
+
+    def close(self):
+        """Release the peer-memory regions (collective; a no-op for NCCL)."""
+        if self._peer is not None:
+            self._peer.close()
+            self._peer = None

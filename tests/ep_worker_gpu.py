@@ -64,6 +64,17 @@ def main(out_path):
             peer.close()
             same = torch.equal(y_ep, y_1)
             same_p = torch.equal(y_p2p, y_1)
+            if T == 4096:  # the module with the peer transport, reference parameter layout
+                mod = ep.SparseMoEExpertParallelSwiGLU(d, I, E, k, True, transport="peer",
+                                                       max_tokens=T + 37 * (world - 1)).to(dev)
+                with torch.no_grad():
+                    mod.gate.weight.copy_(t(wr))
+                    mod.experts.local_experts.gate_up_weight.copy_(wgu_l)
+                    mod.experts.local_experts.down_weight.copy_(wd_l)
+                    y_mod = mod(t(inp.x).unsqueeze(0)).squeeze(0)
+                torch.cuda.synchronize()
+                mod.close()
+                same_p = same_p and torch.equal(y_mod, y_1)
             ok &= same and same_p
             msgs.append(f"T={shape.tokens} E={E} {dtype} skew={skew}: nccl {'equal' if same else 'DIFFER'}, "
                         f"p2p {'equal' if same_p else 'DIFFER max %g' % (y_p2p.float() - y_1.float()).abs().max().item()}")
