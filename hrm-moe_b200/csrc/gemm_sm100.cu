@@ -52,12 +52,13 @@ constexpr int kTmemCols = kAccCols * kNumAcc; // 512 = all of TMEM
 // Epilogue warps: the SwiGLU tile (exp + divide per output, direct stores)
 // takes two warps per TMEM lane quadrant to hide its latency; the plain tile
 // takes one per quadrant with two TMA staging boxes each.
-template <bool SWIGLU, bool SCATTER>
-__host__ __device__ constexpr int epi_warps() { return SWIGLU ? 8 : 4; }
-constexpr int kPushWarps = 8;  // row senders of the fused expert-parallel dispatch
+constexpr int kPushWarps = 8;    // row senders of the fused expert-parallel dispatch
+constexpr int kPushEpiWarps = 8;  // epilogue warps of that kernel
+template <bool SWIGLU, bool SCATTER, bool PUSH = false>
+__host__ __device__ constexpr int epi_warps() { return PUSH ? kPushEpiWarps : (SWIGLU ? 8 : 4); }
 template <bool SWIGLU, bool SCATTER, bool PUSH>
 __host__ __device__ constexpr int num_threads() {  // + producer, MMA issuer (+ senders)
-  return 64 + 32 * epi_warps<SWIGLU, SCATTER>() + (PUSH ? 32 * kPushWarps : 0);
+  return 64 + 32 * epi_warps<SWIGLU, SCATTER, PUSH>() + (PUSH ? 32 * kPushWarps : 0);
 }
 constexpr int kMaxGroups = 1024;
 constexpr int kEpiChunkBytes = 32 * 32 * 2;                  // 32 rows x 32 bf16 columns
@@ -337,7 +338,7 @@ grouped_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
       }
       for (int a = 0; a < kNumAcc; ++a) {
         mbar_init(smem_u32(&ctl.acc_full[a]), 1);
-        mbar_init(smem_u32(&ctl.acc_empty[a]), epi_warps<SWIGLU, SCATTER>());
+        mbar_init(smem_u32(&ctl.acc_empty[a]), epi_warps<SWIGLU, SCATTER, PUSH>());
       }
       mbar_init(smem_u32(&ctl.drain), 1);
       ctl.abort = 0;
@@ -445,7 +446,7 @@ grouped_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
       tc_commit(smem_u32(&ctl.drain));
       mbar_wait_bounded(smem_u32(&ctl.drain), 0, &never, p.err, lim);
     }
-  } else if (warp < 2 + epi_warps<SWIGLU, SCATTER>()) {
+  } else if (warp < 2 + epi_warps<SWIGLU, SCATTER, PUSH>()) {
     // ------------------------------------------------------------ epilogue
     // Each warp reads one 32-lane TMEM quadrant (= 32 rows); with two warps
     // per quadrant (SwiGLU) they take alternate 32-column chunks.  Each chunk
@@ -454,7 +455,7 @@ grouped_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
     // store of the 32x32 box, so global writes are whole lines and run
     // asynchronously.  A quadrant that crosses the end of its group (or of
     // A) stores its valid rows directly.
-    constexpr int kStride = epi_warps<SWIGLU, SCATTER>() / 4;
+    constexpr int kStride = epi_warps<SWIGLU, SCATTER, PUSH>() / 4;
     const int quad = warp & 3;                 // TMEM lanes this warp may read
     const int first = (warp - 2) >> 2;         // first chunk of this warp
     const int r_in_tile = quad * 32 + lane;
@@ -584,7 +585,7 @@ grouped_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
     __syncwarp();
   } else if (PUSH) {
     // ------------------------------------------------------------- senders
-    const int pw = blockIdx.x * kPushWarps + (warp - 2 - epi_warps<SWIGLU, SCATTER>());
+    const int pw = blockIdx.x * kPushWarps + (warp - 2 - epi_warps<SWIGLU, SCATTER, PUSH>());
     push_rows(p, ctl, pw, gridDim.x * kPushWarps, lane);
   }
 
