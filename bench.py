@@ -42,11 +42,11 @@ NVLINK_GBS = 770.0
 # Keyed by (config, tokens per GPU); other workloads report null.
 NCU_TRAFFIC_BYTES = {
     ("cfg2_xl64_bf16", 16384): {
-        "router": 50.594e6 + 0.085e6 + 1.313e6,            # router_tc + fix-up
-        "dispatch": 0.534e6 + 0.039e6 + 51.425e6 + 344.296e6,  # hist + scan + permute
-        "gate_up_gemm": 604.103e6 + 119.270e6,
-        "down_gemm": 234.991e6 + 352.724e6,
-        "combine": 403.713e6 + 42.385e6,
+        "router": 50.594e6 + 0.092e6 + 1.326e6,                # router_tc + fix-up
+        "dispatch": 0.534e6 + 0.039e6 + 51.425e6 + 344.146e6,  # hist + scan + permute
+        "gate_up_gemm": 604.112e6 + 122.201e6,
+        "down_gemm": 234.978e6 + 352.903e6,
+        "combine": 403.712e6 + 42.690e6,
     },
 }
 
