@@ -437,20 +437,19 @@ def b200_arm(args, rank, world, local_rank):
                "d2h_bytes_per_step": T * d * es,
                "api": f"hmoe_ffn_forward_host (C ABI, pinned host buffers, {chunk}-token chunks)"}
     elif not args.no_e2e and peer is not None:
-        # every step: pinned host tokens -> device, the peer-memory EP layer,
-        # device -> pinned host output, all on this rank's stream
+        # every step: pinned host tokens in, the peer-memory EP layer, output
+        # back to pinned host memory, in chunks whose copies overlap the layer
         x_host = x.cpu().pin_memory()
         y_host = torch.empty_like(x_host).pin_memory()
-        x_dev = torch.empty_like(x)
+        chunk = min(T, args.e2e_chunk)
         e_s, e_e = make_events(args.steps), make_events(args.steps)
         dist.barrier()
         for i in range(args.warmup + args.steps):
             flush.zero_()
             if i >= args.warmup:
                 e_s[i - args.warmup].record(stream)
-            x_dev.copy_(x_host, non_blocking=True)
-            peer.forward(x_dev, w_router, w_gate_up, w_down, y=y)
-            y_host.copy_(y, non_blocking=True)
+            peer.forward_host(x_host, w_router, w_gate_up, w_down, y_host=y_host,
+                              chunk_tokens=chunk)
             if i >= args.warmup:
                 e_e[i - args.warmup].record(stream)
         torch.cuda.synchronize()
@@ -462,8 +461,8 @@ def b200_arm(args, rank, world, local_rank):
         e2e = {"value": world * T / (e2e_ms * 1e-3), "unit": "tokens/s",
                "ms_per_step": e2e_ms, "h2d_bytes_per_step": T * d * es,
                "d2h_bytes_per_step": T * d * es,
-               "api": "PeerExpertParallel.forward (hmoe_ep_forward) with pinned host copies "
-                      "in and out on the same stream"}
+               "api": f"PeerExpertParallel.forward_host (pinned host buffers, {chunk}-token "
+                      "chunks, copies overlapped with the layer)"}
 
     # ------------------------------------------------------------ roofline
     peaks = measured_peaks()

@@ -225,6 +225,63 @@ class PeerExpertParallel:
             p(self.ws), self.ws.numel(), ct.c_void_p(torch.cuda.current_stream().cuda_stream), ev))
         return y
 
+    def forward_host(self, x_host, w_router, w_gate_up_local, w_down_local, y_host=None,
+                     chunk_tokens: int = 4096, num_chunks: Optional[int] = None,
+                     router_bias=None):
+        """y_host [T, d] for pinned host tokens x_host [T, d], copies overlapped.
+
+        The tokens go through in chunks of ``chunk_tokens`` (at most
+        ``max_tokens``): chunk c+1 is copied in and chunk c-1 copied out on
+        side streams while chunk c runs.  Each chunk is one :meth:`forward`,
+        so every rank must run the same number of chunks: pass the same
+        ``num_chunks`` on all ranks when their token counts differ (a rank
+        with fewer tokens runs empty chunks).  Returns once y_host is filled.
+        """
+        T, d = x_host.shape
+        if x_host.is_cuda or not x_host.is_pinned():
+            raise ValueError("x_host must be a pinned host tensor")
+        if chunk_tokens <= 0 or chunk_tokens > self.max_tokens:
+            raise ValueError(f"chunk_tokens must be in [1, max_tokens={self.max_tokens}]")
+        n = num_chunks if num_chunks is not None else -(-T // chunk_tokens)
+        if n * chunk_tokens < T:
+            raise ValueError(f"{n} chunks of {chunk_tokens} tokens cannot hold {T} tokens")
+        if y_host is None:
+            y_host = torch.empty_like(x_host).pin_memory()
+        dev = self.device
+        main = torch.cuda.current_stream(dev)
+        s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        xb = [torch.empty((chunk_tokens, d), dtype=x_host.dtype, device=dev) for _ in range(2)]
+        yb = [torch.empty((chunk_tokens, d), dtype=x_host.dtype, device=dev) for _ in range(2)]
+        x_free = [torch.cuda.Event() for _ in range(2)]
+        y_free = [torch.cuda.Event() for _ in range(2)]
+        for e in x_free + y_free:
+            e.record(main)
+        for c in range(n):
+            i = c & 1
+            t0 = min(T, c * chunk_tokens)
+            tc = min(T, t0 + chunk_tokens) - t0
+            ready = torch.cuda.Event()
+            with torch.cuda.stream(s_in):  # the compute of chunk c-2 is done with xb[i]
+                s_in.wait_event(x_free[i])
+                if tc > 0:
+                    xb[i][:tc].copy_(x_host[t0:t0 + tc], non_blocking=True)
+                ready.record(s_in)
+            main.wait_event(ready)
+            main.wait_event(y_free[i])  # the copy-out of chunk c-2 has read yb[i]
+            self.forward(xb[i][:tc], w_router, w_gate_up_local, w_down_local, router_bias,
+                         y=yb[i][:tc])
+            x_free[i].record(main)
+            done = torch.cuda.Event()
+            done.record(main)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(done)
+                if tc > 0:
+                    y_host[t0:t0 + tc].copy_(yb[i][:tc], non_blocking=True)
+                y_free[i].record(s_out)
+        main.wait_stream(s_out)
+        main.synchronize()
+        return y_host
+
     def status(self):
         """Raise if a device-side wait of an earlier call gave up (synchronises)."""
         ops.workspace_status(self.ws)

@@ -64,6 +64,13 @@ def main(out_path):
             peer.close()
             same = torch.equal(y_ep, y_1)
             same_p = torch.equal(y_p2p, y_1)
+            if T == 4096:  # host buffers in overlapped chunks (every rank runs 5 chunks)
+                peer2 = ep.PeerExpertParallel(d, I, E, k, True, max_tokens=1000, dtype=tdt)
+                xh = t(inp.x).cpu().pin_memory()
+                yh = peer2.forward_host(xh, t(wr), wgu_l, wd_l, chunk_tokens=1000, num_chunks=5)
+                peer2.status()
+                peer2.close()
+                same_p = same_p and torch.equal(yh.to(dev), y_1)
             if T == 4096:  # the module with the peer transport, reference parameter layout
                 mod = ep.SparseMoEExpertParallelSwiGLU(d, I, E, k, True, transport="peer",
                                                        max_tokens=T + 37 * (world - 1)).to(dev)
