@@ -10,6 +10,8 @@
 #include <string.h>
 
 #include <mutex>
+#include <cstdlib>
+#include <cstring>
 #include <string>
 
 #include "common.cuh"
@@ -210,6 +212,18 @@ int run_dispatch(const hmoe_shape& s, const int32_t* idx, const void* w, int w_i
   return HMOE_OK;
 }
 
+// Which tcgen05 kernel runs the local grouped GEMMs: the CTA-pair kernel
+// (256-row tiles over two SMs, half the operand traffic per SM) unless
+// HMOE_GEMM_KERNEL=single selects the single-CTA kernel.  Both give the same
+// bits.  Read once per process.
+bool use_cta_pair_gemm() {
+  static const bool pair = [] {
+    const char* v = std::getenv("HMOE_GEMM_KERNEL");
+    return v == nullptr || std::strcmp(v, "single") != 0;
+  }();
+  return pair;
+}
+
 int run_grouped(const void* a, const void* b, const int32_t* counts, int64_t M, int N, int K,
                 int G, int dtype, int swiglu, void* out, int* err, cudaStream_t st,
                 const int32_t* group_weight = nullptr, int num_weights = 0) {
@@ -228,8 +242,9 @@ int run_grouped(const void* a, const void* b, const int32_t* counts, int64_t M, 
   g.dtype = dtype;
   g.err = err;
   g.sm_limit = 0;
-  const cudaError_t e = dtype == kDtypeBF16 ? launch_grouped_gemm_sm100(g, st)
-                                            : launch_grouped_gemm_simt(g, st);
+  const cudaError_t e = dtype != kDtypeBF16 ? launch_grouped_gemm_simt(g, st)
+                        : use_cta_pair_gemm() ? launch_grouped_gemm_pair(g, st)
+                                              : launch_grouped_gemm_sm100(g, st);
   if (e != cudaSuccess) return cuda_fail(e, swiglu ? "grouped_swiglu" : "grouped_linear");
   return HMOE_OK;
 }

@@ -109,6 +109,8 @@ struct GroupedGemmArgs {
 constexpr uint32_t kEpSrcShift = 28;  // row origin = (source rank << 28) | source position
 cudaError_t launch_grouped_gemm_sm100(const GroupedGemmArgs& args, cudaStream_t stream);
 cudaError_t launch_grouped_gemm_simt(const GroupedGemmArgs& args, cudaStream_t stream);
+// bf16, local output only (no scatter / push): CTA pairs, 256-row tiles
+cudaError_t launch_grouped_gemm_pair(const GroupedGemmArgs& args, cudaStream_t stream);
 
 // ep_p2p.cu -------------------------------------------------------------
 size_t ep_symmetric_bytes(const ::hmoe_shape& s, int64_t max_tokens, int world);

@@ -95,3 +95,22 @@ def test_grouped_linear_errors():
     empty = ops.grouped_linear(a[:0], torch.zeros((2, 8, 16), device="cuda", dtype=torch.bfloat16),
                                torch.tensor([0, 0], device="cuda"))
     assert tuple(empty.shape) == (0, 8)
+
+
+def test_cta_pair_and_single_cta_kernels_agree(tmp_path):
+    """The CTA-pair tcgen05 kernel (the default) and the single-CTA kernel
+    (HMOE_GEMM_KERNEL=single, in a child process) give the same bits."""
+    import os
+    import subprocess
+    import sys
+
+    import gemm_kernels_worker_gpu as W
+
+    ours = W.compute()
+    path = tmp_path / "single.pt"
+    env = dict(os.environ, HMOE_GEMM_KERNEL="single")
+    subprocess.run([sys.executable, W.__file__, str(path)], env=env, check=True, timeout=600)
+    other = torch.load(path)
+    assert ours.keys() == other.keys()
+    for key in ours:
+        assert torch.equal(ours[key], other[key]), key
