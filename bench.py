@@ -38,14 +38,14 @@ L2_FLUSH_BYTES = 256 << 20
 NVLINK_GBS = 770.0
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per forward of
 # each phase's kernels, from one ncu capture of this workload on one B200
-# (profiles/grouped_gemm_xl64_t16384_full.md, profiles/hbm_kernels_xl64_t16384.md).
+# (profiles/grouped_gemm_pair_xl64_t16384_full.md, profiles/hbm_kernels_xl64_t16384.md).
 # Keyed by (config, tokens per GPU); other workloads report null.
 NCU_TRAFFIC_BYTES = {
     ("cfg2_xl64_bf16", 16384): {
         "router": 50.594e6 + 0.092e6 + 1.326e6,                # router_tc + fix-up
         "dispatch": 0.534e6 + 0.039e6 + 51.425e6 + 344.146e6,  # hist + scan + permute
-        "gate_up_gemm": 604.112e6 + 122.201e6,
-        "down_gemm": 234.978e6 + 352.903e6,
+        "gate_up_gemm": 604.157e6 + 122.918e6,
+        "down_gemm": 234.981e6 + 353.406e6,
         "combine": 403.712e6 + 42.690e6,
     },
 }
