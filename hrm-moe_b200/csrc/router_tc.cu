@@ -17,11 +17,15 @@
 // next, the last pick against every unpicked expert) holds for all values in
 // those sets; otherwise the token is appended to a fix-up list.
 //
-// router_fixup_kernel: recomputes the listed tokens' logits in the exact
-// order on the CUDA cores (the blocks of k in parallel, four tokens per CTA)
-// and routes them again, overwriting the output.
+// The fix-up kernels recompute the listed tokens' logits in the exact order
+// on the CUDA cores and route them again, overwriting the output:
+// router_fixup_split_kernel (small T: token groups x expert groups over many
+// CTAs, started early by programmatic dependent launch),
+// router_fixup_wsmem_kernel (larger T, E <= 64: the whole weight in shared
+// memory) and router_fixup_kernel (otherwise).
 // The result equals the CUDA-core router's for every token.
 #include <limits.h>
+#include <stdlib.h>
 
 #include <mutex>
 
@@ -72,6 +76,8 @@ struct RtParams {
   uint16_t* logits_out;
   int* fix_count;
   int32_t* fix_list;
+  unsigned* group_done;   // split fix-up: finished expert groups per token group
+  uint16_t* fix_logits;   // split fix-up: rounded logits per fix slot
   int* err;
   unsigned long long wait_limit_ns;
   float cert_rel;
@@ -231,6 +237,14 @@ router_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant_
   volatile int* abort = &ctl.abort;
   int never = 0;
   bool acc_ok = true;
+  // the fix-up grid may start now on the SMs this grid leaves free (it
+  // waits for this grid's completion before it reads the fix list)
+  grid_launch_dependents();
+  // this CTA's 128 tokens own 32 counters of the split fix-up
+  if (p.group_done && threadIdx.x < RBM / 4) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * (RBM / 4) + threadIdx.x;
+    if (i < ((cdiv64(p.T, 4) + 3) & ~static_cast<int64_t>(3))) p.group_done[i] = 0u;
+  }
 
   if (warp == 0) {
     if (lane == 0) {
@@ -440,7 +454,8 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// Fix-up for E <= 64 with the whole router weight in shared memory: TMA
+// Fix-up for E <= 64 with the whole router weight in shared memory (used
+// where the split fix-up below would need more than one round): TMA
 // brings W in [64 expert x 64 k] boxes (128-byte swizzle, the router's own
 // map), so the weights are read from HBM/L2 once per CTA in large copies
 // instead of one 16-byte load per thread and step.  Thread (expert e, token
@@ -569,6 +584,169 @@ router_fixup_wsmem_kernel(const __grid_constant__ CUtensorMap tmW, const uint16_
   if (!have_w) mbar_wait_bounded(smem_u32(&bar), 0, &abort_flag, err, wait_limit_ns);
 }
 
+// Fix-up split over CTAs (d <= 2048, any E <= 128).
+//
+// The fix list is cut into groups of kSplitG tokens and the experts into
+// groups of kSplitE; a work item is one (token group, expert group) and a CTA
+// keeps one expert group for all its items, so it loads that slice of the
+// weight (kSplitE rows) into shared memory once.  The kernel is launched as a
+// programmatic dependent of router_tc_kernel: the slice is loaded before
+// grid_dependency_wait(), while the tensor-core pass still runs, and the fix
+// list only after it.
+//
+// Warp w takes expert e = group * kSplitE + w; lane (token g, eighth h) runs
+// the blocks [h * nbh, (h + 1) * nbh) of that expert's logit for token g: one
+// fma per k from +0 in ascending k within a block.  The block sums are added
+// in ascending block order from +0, handed from eighth to eighth with
+// shuffles, then the bias: the exact-order logit, bit-identical to
+// router_fixup_kernel and to the CUDA-core router (padding past d adds +0
+// products, which leave a block sum unchanged).  The rounded logits go to
+// scratch; the last CTA to finish a token group (a counter per group) routes
+// its tokens, one warp each.
+constexpr int kSplitG = 4;                    // tokens per work item
+constexpr int kSplitE = 8;                    // experts per work item (one warp each)
+constexpr int kSplitH = 8;                    // lanes per (expert, token)
+constexpr int kSplitMaxNbh = 4;               // blocks per lane: d <= 2048
+constexpr int kSplitWRow = kLogitBlock + 8;   // bf16 per weight block in smem (16 B padding)
+constexpr int kSplitXRow = kLogitBlock + 4;   // floats per token block in smem (16 B padding)
+constexpr int kSplitLogitStride = 128;        // rounded logits per fix slot in scratch
+constexpr int kSplitThreads = 32 * kSplitE;
+
+size_t split_smem_bytes(int d) {
+  const size_t nb = static_cast<size_t>(cdiv(d, kLogitBlock));
+  return nb * (kSplitE * kSplitWRow * 2 + kSplitG * kSplitXRow * 4) +
+         kSplitG * kSplitLogitStride * 4;
+}
+
+template <int NV>
+__global__ void __launch_bounds__(kSplitThreads)
+router_fixup_split_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ w,
+                          const uint16_t* __restrict__ bias, int64_t T, int d, int E, int k,
+                          int norm, const int* fix_count, const int32_t* fix_list,
+                          unsigned* group_done, uint16_t* fix_logits, int32_t* topk_idx,
+                          float* topk_w_f32, void* topk_w_dtype, uint16_t* logits_out) {
+  // fix_count, fix_list and group_done are written by the grid this one
+  // depends on (or by other CTAs): they are read (volatile) only after
+  // grid_dependency_wait(), never as read-only data that could be loaded
+  // earlier.
+  extern __shared__ float4 sraw4[];
+  const int nb = cdiv(d, kLogitBlock);
+  const int nbh = cdiv(nb, kSplitH);
+  const int n_eg = cdiv(E, kSplitE);
+  const int eg = static_cast<int>(blockIdx.x) % n_eg;
+  const int lanes_tg = static_cast<int>(gridDim.x) / n_eg;  // the grid is a multiple of n_eg
+  uint16_t* ws = reinterpret_cast<uint16_t*>(sraw4);                   // [kSplitE][nb][72]
+  float* xs = reinterpret_cast<float*>(ws + kSplitE * nb * kSplitWRow);  // [kSplitG][nb][68]
+  float* lg = xs + kSplitG * nb * kSplitXRow;                          // [kSplitG][128]
+  __shared__ int64_t s_tok[kSplitG];
+  __shared__ int s_last;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane / kSplitH, h = lane % kSplitH;
+  const int e = eg * kSplitE + warp;
+  // this CTA's weight slice (zeros past E and d); it does not depend on the
+  // grid before this one
+  // (warp w loads the row of its own expert e)
+  for (int r = lane; r < nb * (kLogitBlock / 8); r += 32) {
+    const int b = r >> 3, c = r & 7;
+    uint4 u = make_uint4(0, 0, 0, 0);
+    if (e < E && r * 8 < d) u = __ldg(reinterpret_cast<const uint4*>(w + static_cast<int64_t>(e) * d) + r);
+    *reinterpret_cast<uint4*>(ws + (warp * nb + b) * kSplitWRow + c * 8) = u;
+  }
+  grid_dependency_wait();  // the tensor-core pass and its fix list are complete
+  const int n = *reinterpret_cast<const volatile int*>(fix_count);
+  const int ngroups = cdiv(n, kSplitG);
+  for (int tg = static_cast<int>(blockIdx.x) / n_eg; tg < ngroups; tg += lanes_tg) {
+    __syncthreads();  // the previous item is finished with xs, lg and s_tok
+    if (tid < kSplitG) {
+      const int slot = tg * kSplitG + tid;
+      const int64_t t = slot < n ? reinterpret_cast<const volatile int32_t*>(fix_list)[slot] : -1;
+      s_tok[tid] = (t >= 0 && t < T) ? t : -1;
+    }
+    __syncthreads();
+    // the group's token rows -> fp32 (zeros past d and for empty slots)
+    // (warp w < kSplitG loads the row of token w)
+    if (warp < kSplitG) {
+      const int64_t t = s_tok[warp];
+      for (int r = lane; r < nb * (kLogitBlock / 8); r += 32) {
+        const int b = r >> 3, c = r & 7;
+        uint4 u = make_uint4(0, 0, 0, 0);
+        if (t >= 0 && r * 8 < d) u = __ldg(reinterpret_cast<const uint4*>(x + t * d) + r);
+        float* xr = xs + (warp * nb + b) * kSplitXRow + c * 8;
+        reinterpret_cast<float4*>(xr)[0] = make_float4(bf16_lo(u.x), bf16_hi(u.x), bf16_lo(u.y), bf16_hi(u.y));
+        reinterpret_cast<float4*>(xr)[1] = make_float4(bf16_lo(u.z), bf16_hi(u.z), bf16_lo(u.w), bf16_hi(u.w));
+      }
+    }
+    __syncthreads();
+    float acc[kSplitMaxNbh];
+#pragma unroll
+    for (int j = 0; j < kSplitMaxNbh; ++j) acc[j] = 0.0f;
+    const int b0 = h * nbh;
+#pragma unroll
+    for (int c = 0; c < kLogitBlock / 8; ++c) {
+#pragma unroll
+      for (int j = 0; j < kSplitMaxNbh; ++j) {
+        const int b = b0 + j;
+        if (j < nbh && b < nb) {
+          const uint4 u = *reinterpret_cast<const uint4*>(ws + (warp * nb + b) * kSplitWRow + c * 8);
+          const float* xb = xs + (g * nb + b) * kSplitXRow + c * 8;
+          const float4 xa = reinterpret_cast<const float4*>(xb)[0];
+          const float4 xc = reinterpret_cast<const float4*>(xb)[1];
+          float a = acc[j];
+          a = fmaf(xa.x, bf16_lo(u.x), a);
+          a = fmaf(xa.y, bf16_hi(u.x), a);
+          a = fmaf(xa.z, bf16_lo(u.y), a);
+          a = fmaf(xa.w, bf16_hi(u.y), a);
+          a = fmaf(xc.x, bf16_lo(u.z), a);
+          a = fmaf(xc.y, bf16_hi(u.z), a);
+          a = fmaf(xc.z, bf16_lo(u.w), a);
+          a = fmaf(xc.w, bf16_hi(u.w), a);
+          acc[j] = a;
+        }
+      }
+    }
+    // ascending block order: eighth h continues the running sum of h - 1
+    // (the eighths of one (expert, token) are adjacent lanes)
+    float run = 0.0f;
+#pragma unroll
+    for (int q = 0; q < kSplitH; ++q) {
+      const float prev = __shfl_up_sync(0xffffffffu, run, 1);
+      if (h == q) {
+        float t = q == 0 ? 0.0f : prev;
+#pragma unroll
+        for (int j = 0; j < kSplitMaxNbh; ++j)
+          if (j < nbh && b0 + j < nb) t = t + acc[j];
+        run = t;
+      }
+    }
+    if (h == kSplitH - 1 && e < E) {
+      float tot = run;
+      if (bias) tot = tot + bf16_bits_to_f32(bias[e]);
+      fix_logits[static_cast<int64_t>(tg * kSplitG + g) * kSplitLogitStride + e] =
+          static_cast<uint16_t>(f32_to_bf16_bits(tot));
+      __threadfence();
+    }
+    __syncthreads();
+    if (tid == 0) {
+      const unsigned prev = atomicAdd(group_done + tg, 1u);
+      s_last = prev == static_cast<unsigned>(n_eg - 1);
+    }
+    __syncthreads();
+    if (s_last) {  // every expert group of this token group is written: route it
+      __threadfence();
+      if (warp < kSplitG) {
+        const int64_t slot = static_cast<int64_t>(tg) * kSplitG + warp;
+        const volatile uint16_t* src = fix_logits + slot * kSplitLogitStride;
+        for (int ee = lane; ee < NV * 32; ee += 32)
+          lg[warp * kSplitLogitStride + ee] = ee < E ? bf16_bits_to_f32(src[ee]) : 0.0f;
+        __syncwarp();
+        if (s_tok[warp] >= 0)
+          fixup_route_token<NV>(lg + warp * kSplitLogitStride, s_tok[warp], E, k, norm, lane,
+                                topk_idx, topk_w_f32, topk_w_dtype, logits_out);
+      }
+    }
+  }
+}
+
 bool map_rows(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return false;
@@ -608,6 +786,10 @@ cudaError_t launch_tc(const void* x, const void* w, const RtParams& p, cudaStrea
       e = cudaFuncSetAttribute(router_fixup_wsmem_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                232448 - 64);
       if (e != cudaSuccess) return e;
+      e = cudaFuncSetAttribute(router_fixup_split_kernel<NV>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(split_smem_bytes(kLogitBlock * kSplitH * kSplitMaxNbh)));
+      if (e != cudaSuccess) return e;
       done[dev] = 1;
     }
   }
@@ -620,10 +802,42 @@ cudaError_t launch_tc(const void* x, const void* w, const RtParams& p, cudaStrea
       mx, mw, p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  const size_t wsm_smem = 1024 + static_cast<size_t>(cdiv(p.d, kLogitBlock)) * 8192 +
+  const int nb = cdiv(p.d, kLogitBlock);
+  // The split fix-up's grid: a multiple of the expert groups, one token group
+  // lane per 128 tokens (a few percent of the tokens go to the fix-up, four
+  // per group), at most four CTAs per SM.  Where that cap would leave the
+  // usual load more than one round per lane, the single-pass kernel with the
+  // whole weight in shared memory is faster.
+  const int n_eg = cdiv(p.E, kSplitE);
+  const int sms = num_sms_for_current_device();
+  const int64_t want = cdiv64(p.T, 128);
+  const int cap = (4 * sms) / n_eg > 1 ? (4 * sms) / n_eg : 1;
+  const size_t wsm_smem = 1024 + static_cast<size_t>(nb) * 8192 +
                           sizeof(float) * (static_cast<size_t>(kFixSmG) * p.d + kFixSmG * 64);
-  if (EPAD == 64 && wsm_smem <= 232448 - 64) {
-    router_fixup_wsmem_kernel<<<num_sms_for_current_device(), 64 * kFixSmG, wsm_smem, st>>>(
+  const bool wsmem_ok = EPAD == 64 && wsm_smem <= 232448 - 64;
+  if (nb <= kSplitH * kSplitMaxNbh && (want <= cap || !wsmem_ok)) {
+    // programmatic dependent launch: the CTAs start (and load their weight
+    // slice) while the tensor-core pass is still running; the loop covers
+    // any fix count
+    const int lanes = static_cast<int>(want < 1 ? 1 : (want > cap ? cap : want));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(lanes * n_eg));
+    cfg.blockDim = dim3(kSplitThreads);
+    cfg.dynamicSmemBytes = split_smem_bytes(p.d);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, router_fixup_split_kernel<NV>, static_cast<const uint16_t*>(x),
+                           static_cast<const uint16_t*>(w), p.bias, p.T, p.d, p.E, p.k, p.norm,
+                           static_cast<const int*>(p.fix_count),
+                           static_cast<const int32_t*>(p.fix_list), p.group_done, p.fix_logits,
+                           p.topk_idx, p.topk_w_f32, p.topk_w_dtype, p.logits_out);
+    if (e != cudaSuccess) return e;
+  } else if (wsmem_ok) {
+    router_fixup_wsmem_kernel<<<sms, 64 * kFixSmG, wsm_smem, st>>>(
         mw, static_cast<const uint16_t*>(x), p.bias, p.T, p.d, p.E, p.k, p.norm, p.fix_count,
         p.fix_list, p.topk_idx, p.topk_w_f32, p.topk_w_dtype, p.logits_out, p.err,
         p.wait_limit_ns);
@@ -638,7 +852,29 @@ cudaError_t launch_tc(const void* x, const void* w, const RtParams& p, cudaStrea
 
 }  // namespace
 
-size_t router_tc_scratch_bytes(int64_t T) { return sizeof(int) * 64 + sizeof(int32_t) * T; }
+// Certification margin, relative to a token's largest |logit|.  The
+// environment variable HMOE_ROUTER_CERT_REL (read once) overrides it; the
+// tests set it to 1 so that no token is certified and every one takes the
+// exact-order fix-up pass.  A larger margin only sends more tokens there.
+static float router_cert_rel() {
+  static const float rel = [] {
+    const char* v = getenv("HMOE_ROUTER_CERT_REL");
+    const float f = v ? static_cast<float>(atof(v)) : 0.0f;
+    return f > kRouterCertRel ? f : kRouterCertRel;
+  }();
+  return rel;
+}
+
+// Scratch: 64 ints of header (the fix count first, zeroed per call), the
+// per-token-group counters of the split fix-up (zeroed by router_tc_kernel),
+// the fix list, then the rounded logits of every fix slot.
+static int64_t align4(int64_t v) { return (v + 3) & ~static_cast<int64_t>(3); }
+static int64_t fix_groups(int64_t T) { return align4(cdiv64(T, kSplitG)); }
+
+size_t router_tc_scratch_bytes(int64_t T) {
+  return sizeof(int) * (64 + fix_groups(T) + align4(T)) +
+         sizeof(uint16_t) * static_cast<size_t>(fix_groups(T)) * kSplitG * kSplitLogitStride;
+}
 
 cudaError_t launch_router_topk_tc(const void* x, const void* w_router, const void* bias,
                                   int64_t T, int d, int E, int k, int norm, int32_t* topk_idx,
@@ -660,10 +896,12 @@ cudaError_t launch_router_topk_tc(const void* x, const void* w_router, const voi
   p.topk_w_dtype = topk_w_dtype;
   p.logits_out = static_cast<uint16_t*>(logits_out);
   p.fix_count = fix_count;
-  p.fix_list = reinterpret_cast<int32_t*>(static_cast<char*>(scratch) + sizeof(int) * 64);
+  p.group_done = reinterpret_cast<unsigned*>(fix_count + 64);
+  p.fix_list = fix_count + 64 + fix_groups(T);
+  p.fix_logits = reinterpret_cast<uint16_t*>(p.fix_list + align4(T));
   p.err = err;
   p.wait_limit_ns = kWaitLimitNs;
-  p.cert_rel = kRouterCertRel;
+  p.cert_rel = router_cert_rel();
   if (k <= 8)
     return E <= 64 ? launch_tc<64, 8>(x, w_router, p, stream)
                    : launch_tc<128, 8>(x, w_router, p, stream);

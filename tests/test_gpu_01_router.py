@@ -122,3 +122,28 @@ def test_router_full_size_exact_e128_near_ties():
     w = (np.round(rng.standard_normal((E, d)).astype(np.float32) * 4) / np.float32(200)).astype(np.float32)
     w = O.round_to_bf16(w)
     _check_against_oracle(x, w, None, k, True, "bf16")
+
+
+def test_router_fixup_pass_is_exact_order(tmp_path):
+    """With HMOE_ROUTER_CERT_REL=1 (child process) no token is certified and
+    the fix-up kernels route every token: their logits must be the
+    exact-order logits bit for bit, and the routing the oracle's."""
+    import os
+    import subprocess
+    import sys
+
+    import torch
+
+    import router_fixup_worker_gpu as W
+
+    path = tmp_path / "fixup.pt"
+    env = dict(os.environ, HMOE_ROUTER_CERT_REL="1")
+    subprocess.run([sys.executable, W.__file__, str(path)], env=env, check=True, timeout=600)
+    res = torch.load(path)
+    for name, x, w, bias, k, norm in W.cases():
+        idx, wt, logits = (t.numpy() for t in res[name])
+        ol = O.router_logits(x, w, bias, "bf16")
+        oidx, ow, _ = O.route(ol, k, norm, "bf16")
+        assert np.array_equal(logits, ol), name
+        assert np.array_equal(idx.astype(np.int64), oidx), name
+        np.testing.assert_allclose(wt, ow, rtol=2 ** -7, atol=0, err_msg=name)
