@@ -337,10 +337,13 @@ def b200_arm(args, rank, world, local_rank):
     starts = make_events(args.steps)
     ends = make_events(args.steps)
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
     with ClockSampler(gpu_uuid(torch, local_rank)) as clocks:
+        # the barrier comes after each rank's sampler has started (that waits
+        # for its first sample), so that the ranks enter the timed steps
+        # together: an expert-parallel step waits for its peers' rows
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
         for i in range(args.steps):
             flush.zero_()
             starts[i].record(stream)
