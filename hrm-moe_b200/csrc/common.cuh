@@ -59,16 +59,6 @@ __device__ __forceinline__ uint32_t f32_to_bf16_bits(float f) {
 __device__ __forceinline__ float round_bf16(float f) {
   return bf16_bits_to_f32(f32_to_bf16_bits(f));
 }
-// round_bf16 on the integer pipe: round to nearest, ties to even, on the
-// bit pattern (a carry out of the mantissa steps the exponent, so values past
-// the largest bf16 become infinity).  NaN stays NaN (quiet bit set).  Same
-// result as the conversion instruction for every non-NaN input; used where
-// the conversion unit is the busy pipe.
-__device__ __forceinline__ float round_bf16_alu(float f) {
-  const uint32_t u = __float_as_uint(f);
-  const uint32_t r = (u + 0x7fffu + ((u >> 16) & 1u)) & 0xffff0000u;
-  return __uint_as_float((u & 0x7fffffffu) > 0x7f800000u ? ((u | 0x00400000u) & 0xffff0000u) : r);
-}
 // two floats -> packed bf16x2 (lo in the low half)
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return f32_to_bf16_bits(lo) | (f32_to_bf16_bits(hi) << 16);

@@ -138,34 +138,29 @@ __device__ __forceinline__ void decode_tile(const SmemCtl& ctl, int G, int n_til
   nrows = min(BM, ctl.group_rows[g + 1] - row0);
 }
 
-// 32 accumulator columns of one row -> 16 packed bf16x2 words.  The
-// conversion/transcendental pipe is the scarce one here (SiLU's exp and
-// divide use it), so the intermediate roundings run on the integer pipe and
-// the final one is a paired conversion.
+// 32 accumulator columns of one row -> 16 packed bf16x2 words.  SwiGLU
+// rounds where the reference does (models/layers.py:326-329: gate_up is a
+// bf16 tensor, F.silu returns bf16, the product is rounded again) with packed
+// instructions: one paired conversion rounds two gate (or up) values, SiLU
+// runs in fp32 on the rounded gate (the fast exp and divide intrinsics: a few
+// fp32 ulps, far below the bf16 step the result is rounded to) and is rounded
+// by another paired conversion, and mul.rn.bf16x2 rounds the product once
+// (the product of two bf16 values is exact in fp32).
 template <bool SWIGLU>
 __device__ __forceinline__ void epi_pack(const uint32_t (&a)[32], const uint32_t (&b)[32],
                                          uint32_t (&packed)[16]) {
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
-    float v0, v1;
     if (SWIGLU) {
-      // gate_up is a bf16 tensor in the reference, F.silu returns bf16 and
-      // the product is rounded again (models/layers.py:326-329).  SiLU uses
-      // the fast exp and divide intrinsics: a few fp32 ulps, far below the
-      // bf16 step the result is rounded to, and half the epilogue's work.
-      const float g0 = round_bf16_alu(__uint_as_float(a[2 * i]));
-      const float g1 = round_bf16_alu(__uint_as_float(a[2 * i + 1]));
-      const float u0 = round_bf16_alu(__uint_as_float(b[2 * i]));
-      const float u1 = round_bf16_alu(__uint_as_float(b[2 * i + 1]));
-      const float s0 = round_bf16_alu(__fdividef(g0, 1.0f + __expf(-g0)));
-      const float s1 = round_bf16_alu(__fdividef(g1, 1.0f + __expf(-g1)));
-      v0 = s0 * u0;
-      v1 = s1 * u1;
+      const uint32_t g = cvt_bf16x2(__uint_as_float(a[2 * i]), __uint_as_float(a[2 * i + 1]));
+      const uint32_t u = cvt_bf16x2(__uint_as_float(b[2 * i]), __uint_as_float(b[2 * i + 1]));
+      const float g0 = bf16_lo(g), g1 = bf16_hi(g);
+      const uint32_t sg = cvt_bf16x2(__fdividef(g0, 1.0f + __expf(-g0)),
+                                     __fdividef(g1, 1.0f + __expf(-g1)));
+      packed[i] = mul_bf16x2(sg, u);
     } else {
-      v0 = __uint_as_float(a[2 * i]);
-      v1 = __uint_as_float(a[2 * i + 1]);
+      packed[i] = cvt_bf16x2(__uint_as_float(a[2 * i]), __uint_as_float(a[2 * i + 1]));
     }
-    packed[i] = cvt_bf16x2(v0, v1);
   }
 }
 

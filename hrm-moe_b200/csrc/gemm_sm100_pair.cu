@@ -165,28 +165,29 @@ __device__ __forceinline__ void decode_pair_tile(const PairCtl& ctl, int G, int 
   grow_end = ctl.group_rows[g + 1];
 }
 
-// 32 accumulator columns of one row -> 16 packed bf16x2 words (the SwiGLU
-// rounding points of models/layers.py:326-329, as the single-CTA kernel).
+// 32 accumulator columns of one row -> 16 packed bf16x2 words.  SwiGLU
+// rounds where the reference does (models/layers.py:326-329: gate_up is a
+// bf16 tensor, F.silu returns bf16, the product is rounded again) with packed
+// instructions: one paired conversion rounds two gate (or up) values, SiLU
+// runs in fp32 on the rounded gate and is rounded by another paired
+// conversion, and mul.rn.bf16x2 rounds the product once (the product of two
+// bf16 values is exact in fp32).  Same code as grouped_gemm_sm100_kernel's
+// epilogue.
 template <bool SWIGLU>
 __device__ __forceinline__ void pair_pack(const uint32_t (&a)[32], const uint32_t (&b)[32],
                                           uint32_t (&packed)[16]) {
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
-    float v0, v1;
     if (SWIGLU) {
-      const float g0 = round_bf16_alu(__uint_as_float(a[2 * i]));
-      const float g1 = round_bf16_alu(__uint_as_float(a[2 * i + 1]));
-      const float u0 = round_bf16_alu(__uint_as_float(b[2 * i]));
-      const float u1 = round_bf16_alu(__uint_as_float(b[2 * i + 1]));
-      const float s0 = round_bf16_alu(__fdividef(g0, 1.0f + __expf(-g0)));
-      const float s1 = round_bf16_alu(__fdividef(g1, 1.0f + __expf(-g1)));
-      v0 = s0 * u0;
-      v1 = s1 * u1;
+      const uint32_t g = cvt_bf16x2(__uint_as_float(a[2 * i]), __uint_as_float(a[2 * i + 1]));
+      const uint32_t u = cvt_bf16x2(__uint_as_float(b[2 * i]), __uint_as_float(b[2 * i + 1]));
+      const float g0 = bf16_lo(g), g1 = bf16_hi(g);
+      const uint32_t sg = cvt_bf16x2(__fdividef(g0, 1.0f + __expf(-g0)),
+                                     __fdividef(g1, 1.0f + __expf(-g1)));
+      packed[i] = mul_bf16x2(sg, u);
     } else {
-      v0 = __uint_as_float(a[2 * i]);
-      v1 = __uint_as_float(a[2 * i + 1]);
+      packed[i] = cvt_bf16x2(__uint_as_float(a[2 * i]), __uint_as_float(a[2 * i + 1]));
     }
-    packed[i] = cvt_bf16x2(v0, v1);
   }
 }
 

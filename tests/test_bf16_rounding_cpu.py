@@ -1,11 +1,10 @@
-"""The integer round-to-nearest-even used for bf16 roundings.
+"""The integer round-to-nearest-even used for bf16 roundings on the host.
 
-The GEMM epilogue rounds on the integer pipe (round_bf16_alu in
-hrm-moe_b200/csrc/common.cuh) and the synthetic inputs use the same
-arithmetic in numpy (synthetic.round_to_bf16).  Both must equal an
-independent conversion (torch's float -> bfloat16) for every non-NaN input:
-here every high-half bit pattern with the low half at and around the tie
-point, at both ends and at random.
+The synthetic inputs round with integer arithmetic in numpy
+(synthetic.round_to_bf16).  That formula must equal an independent
+conversion (torch's float -> bfloat16) for every non-NaN input: here every
+high-half bit pattern with the low half at and around the tie point, at both
+ends and at random.
 """
 import numpy as np
 import torch
@@ -14,7 +13,7 @@ from _helpers import package
 
 
 def _formula(u):
-    # the device helper, restated on uint32 arrays
+    # round to nearest even on the bit pattern, restated on uint32 arrays
     r = (u + np.uint32(0x7FFF) + ((u >> np.uint32(16)) & np.uint32(1))) & np.uint32(0xFFFF0000)
     nan = (u & np.uint32(0x7FFFFFFF)) > np.uint32(0x7F800000)
     return np.where(nan, (u | np.uint32(0x00400000)) & np.uint32(0xFFFF0000), r)
