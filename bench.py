@@ -44,8 +44,8 @@ NCU_TRAFFIC_BYTES = {
     ("cfg2_xl64_bf16", 16384): {
         "router": 50.594e6 + 0.092e6 + 1.326e6,                # router_tc + fix-up
         "dispatch": 0.534e6 + 0.039e6 + 51.425e6 + 344.146e6,  # hist + scan + permute
-        "gate_up_gemm": 604.157e6 + 122.918e6,
-        "down_gemm": 234.981e6 + 353.406e6,
+        "gate_up_gemm": 604.140e6 + 123.425e6,
+        "down_gemm": 235.043e6 + 354.587e6,
         "combine": 403.712e6 + 42.690e6,
     },
 }
