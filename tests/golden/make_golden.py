@@ -22,7 +22,7 @@ Inputs are not stored: every case records its seed and shape and the tests
 regenerate them with ``synthetic.make_inputs`` (plus checksums to catch a
 generator drift).  Usage::
 
-    python tests/golden/make_golden.py [--reference /path/to/HRM-MoE]
+    python tests/golden/make_golden.py --reference /path/to/HRM-MoE [--only NAME ...]
 """
 from __future__ import annotations
 
@@ -157,7 +157,8 @@ def run_reference(layers, inp):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True,
+                    help="checkout of the reference project (XiaoYee/HRM-MoE) to import models/layers.py from")
     ap.add_argument("--only", nargs="*")
     args = ap.parse_args()
     torch.set_num_threads(max(1, torch.get_num_threads()))
