@@ -137,3 +137,43 @@ def test_ep_two_ranks_match_oracle(cfg, tmp_path):
         assert splits[0].sum() == x.shape[0] * k
         total_sent += splits[0].sum()
     assert total_sent == sum(np.load(tmp_path / f"splits{r}.npy")[1].sum() for r in range(world))
+
+
+def _layout_worker(rank, world, port, outdir):
+    sys.path.insert(0, ROOT)
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    dist.init_process_group("gloo", rank=rank, world_size=world, init_method=f"tcp://127.0.0.1:{port}")
+    try:
+        ep = importlib.import_module("hrm-moe_b200.ep")
+        m = ep.SparseMoEExpertParallelSwiGLU(16, 32, 8, 2, True)
+        sd = m.state_dict()
+        shapes = {k: tuple(v.shape) for k, v in sd.items()}
+        # the reference's grouped_ep state_dict of this rank loads unchanged
+        g = torch.Generator().manual_seed(rank)
+        src = {"gate.weight": torch.randn(8, 16, generator=g),
+               "experts.local_experts.gate_up_weight": torch.randn(4, 64, 16, generator=g),
+               "experts.local_experts.down_weight": torch.randn(4, 16, 32, generator=g)}
+        m.load_state_dict(src)
+        same = all(torch.equal(m.state_dict()[k], v) for k, v in src.items())
+        with open(os.path.join(outdir, f"layout{rank}.txt"), "w") as f:
+            f.write(repr((sorted(shapes.items()), same)))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_ep_module_parameter_layout_matches_reference(tmp_path):
+    """SparseMoEExpertParallelSwiGLU keeps the reference's grouped_ep layout
+    (models/layers.py:395-412): the router replicated, E/R experts per rank
+    under experts.local_experts, so its checkpoints load unchanged."""
+    world = 2
+    port = _free_port()
+    mp.start_processes(_layout_worker, args=(world, port, str(tmp_path)), nprocs=world,
+                       start_method="spawn", join=True)
+    import ast
+    want = sorted({"gate.weight": (8, 16), "experts.local_experts.gate_up_weight": (4, 64, 16),
+                   "experts.local_experts.down_weight": (4, 16, 32)}.items())
+    for rank in range(world):
+        shapes, same = ast.literal_eval((tmp_path / f"layout{rank}.txt").read_text())
+        assert shapes == want
+        assert same
