@@ -212,16 +212,22 @@ int run_dispatch(const hmoe_shape& s, const int32_t* idx, const void* w, int w_i
   return HMOE_OK;
 }
 
-// Which tcgen05 kernel runs the local grouped GEMMs: the CTA-pair kernel
-// (256-row tiles over two SMs, half the operand traffic per SM) unless
-// HMOE_GEMM_KERNEL=single selects the single-CTA kernel.  Both give the same
-// bits.  Read once per process.
-bool use_cta_pair_gemm() {
-  static const bool pair = [] {
+// Which tcgen05 kernel runs a local grouped GEMM.  Both give the same bits.
+// The CTA-pair kernel (256-row tiles over two SMs, half the operand traffic
+// per SM) is faster once the groups average more than 192 rows; below that
+// its tiles are mostly padding and the single-CTA kernel's 128-row tiles do
+// half the wasted MMA work (XL layer: single-CTA faster up to T=1024 tokens,
+// pair from T=2048).  HMOE_GEMM_KERNEL=pair or =single (read once per
+// process) forces one kernel.
+bool use_cta_pair_gemm(int64_t M, int G) {
+  static const int forced = [] {
     const char* v = std::getenv("HMOE_GEMM_KERNEL");
-    return v == nullptr || std::strcmp(v, "single") != 0;
+    if (v && std::strcmp(v, "pair") == 0) return 1;
+    if (v && std::strcmp(v, "single") == 0) return 0;
+    return -1;
   }();
-  return pair;
+  if (forced >= 0) return forced == 1;
+  return M > 192 * static_cast<int64_t>(G);
 }
 
 int run_grouped(const void* a, const void* b, const int32_t* counts, int64_t M, int N, int K,
@@ -243,7 +249,7 @@ int run_grouped(const void* a, const void* b, const int32_t* counts, int64_t M, 
   g.err = err;
   g.sm_limit = 0;
   const cudaError_t e = dtype != kDtypeBF16 ? launch_grouped_gemm_simt(g, st)
-                        : use_cta_pair_gemm() ? launch_grouped_gemm_pair(g, st)
+                        : use_cta_pair_gemm(M, G) ? launch_grouped_gemm_pair(g, st)
                                               : launch_grouped_gemm_sm100(g, st);
   if (e != cudaSuccess) return cuda_fail(e, swiglu ? "grouped_swiglu" : "grouped_linear");
   return HMOE_OK;

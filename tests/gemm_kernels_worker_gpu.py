@@ -3,8 +3,8 @@
 ``compute()`` runs a fixed set of seeded bf16 grouped GEMMs (plain and
 SwiGLU, ragged groups with empty and one-row groups) through the package and
 returns their outputs on the host.  Run as a script it saves them with
-torch.save to argv[1]; the test runs it in a child process whose environment
-selects the other tcgen05 kernel (HMOE_GEMM_KERNEL is read once per process).
+torch.save to argv[1]; the test runs it in child processes whose environment
+forces one tcgen05 kernel each (HMOE_GEMM_KERNEL is read once per process).
 """
 import os
 import sys

@@ -98,19 +98,21 @@ def test_grouped_linear_errors():
 
 
 def test_cta_pair_and_single_cta_kernels_agree(tmp_path):
-    """The CTA-pair tcgen05 kernel (the default) and the single-CTA kernel
-    (HMOE_GEMM_KERNEL=single, in a child process) give the same bits."""
+    """The CTA-pair and single-CTA tcgen05 kernels give the same bits: each
+    side runs in a child process that forces one kernel (HMOE_GEMM_KERNEL is
+    read once per process), on every case of the worker."""
     import os
     import subprocess
     import sys
 
     import gemm_kernels_worker_gpu as W
 
-    ours = W.compute()
-    path = tmp_path / "single.pt"
-    env = dict(os.environ, HMOE_GEMM_KERNEL="single")
-    subprocess.run([sys.executable, W.__file__, str(path)], env=env, check=True, timeout=600)
-    other = torch.load(path)
-    assert ours.keys() == other.keys()
-    for key in ours:
-        assert torch.equal(ours[key], other[key]), key
+    outs = {}
+    for kern in ("pair", "single"):
+        path = tmp_path / f"{kern}.pt"
+        env = dict(os.environ, HMOE_GEMM_KERNEL=kern)
+        subprocess.run([sys.executable, W.__file__, str(path)], env=env, check=True, timeout=600)
+        outs[kern] = torch.load(path)
+    assert outs["pair"].keys() == outs["single"].keys()
+    for key in outs["pair"]:
+        assert torch.equal(outs["pair"][key], outs["single"][key]), key
