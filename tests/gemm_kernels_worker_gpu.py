@@ -20,6 +20,8 @@ for p in (ROOT, os.path.join(ROOT, "tests")):
 CASES = [
     # M, N, K, G, zeros
     (1, 256, 64, 1, 0),
+    (512, 512, 1536, 64, 3),     # decode-sized: about 8 rows per group
+    (2048, 1536, 512, 64, 0),    # about 32 rows per group
     (777, 64, 16, 7, 2),
     (3000, 1280, 448, 16, 3),
     (131072, 512, 1536, 64, 0),
