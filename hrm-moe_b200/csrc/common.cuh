@@ -59,10 +59,6 @@ __device__ __forceinline__ uint32_t f32_to_bf16_bits(float f) {
 __device__ __forceinline__ float round_bf16(float f) {
   return bf16_bits_to_f32(f32_to_bf16_bits(f));
 }
-// two floats -> packed bf16x2 (lo in the low half)
-__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
-  return f32_to_bf16_bits(lo) | (f32_to_bf16_bits(hi) << 16);
-}
 __device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 // Two floats -> bf16x2 with one paired conversion (round to nearest even each).
