@@ -56,8 +56,17 @@ def parse_args():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=300)  # >= one 200 ms clock sample at N=1
     ap.add_argument("--warmup", type=int, default=20)
-    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference", "reference-gpu"],
+                    help="b200: this build; reference: the reference's CPU path (oracle port) "
+                         "on the host cores; reference-gpu: the reference's own grouped_triton "
+                         "module on this GPU, imported from baseline/_ref (see "
+                         "--prepare-reference)")
+    ap.add_argument("--prepare-reference", metavar="CHECKOUT",
+                    help="copy CHECKOUT/models (the reference's MoE layer and its Triton "
+                         "grouped GEMM) into baseline/_ref/ for --impl reference-gpu, and exit")
     ap.add_argument("--config", default="cfg2_xl64_bf16")
+    ap.add_argument("--dead-experts", type=int, default=0,
+                    help="cfg4: experts whose router bias is -inf (no token reaches them)")
     ap.add_argument("--tokens", type=int, default=0, help="tokens per GPU (default: the config's)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="target duration of the CPU baseline sample")
@@ -71,6 +80,16 @@ def parse_args():
                     help="expert-parallel transport for --gpus > 1: peer memory (the product "
                          "path) or NCCL all_to_all")
     return ap.parse_args()
+
+
+def workload_name(config: str, shape, tokens: int, dead_experts: int = 0) -> str:
+    bias = ""
+    if config.startswith("cfg4"):
+        bias = ", router bias for Zipf(1.2) expert load" + (
+            f", {dead_experts} dead experts" if dead_experts else "")
+    return (f"{config}: XL {shape.experts}x{shape.top_k} MoE-FFN layer forward "
+            f"(T={tokens} tokens per GPU, d={shape.hidden}, E={shape.experts}, "
+            f"I={shape.intermediate}, top-{shape.top_k}{bias})")
 
 
 def dist_env():
@@ -178,7 +197,16 @@ def gpu_uuid(torch, dev: int) -> str:
 
 
 # ------------------------------------------------------------- CPU timing --
-def cpu_oracle_tokens_per_s(shape, target_s: float, seed: int = 0, max_tokens: int = 16384):
+def config_router_bias(syn, config: str, shape, dead_experts: int):
+    """cfg4's Zipf(1.2) router bias in the layer dtype (float32 array), else None."""
+    if not config.startswith("cfg4"):
+        return None
+    b = syn.zipf_router_bias(shape.experts, 4, dead_experts=dead_experts)
+    return syn.round_to_bf16(b) if shape.dtype == "bf16" else b
+
+
+def cpu_oracle_tokens_per_s(shape, target_s: float, seed: int = 0, max_tokens: int = 16384,
+                            bias=None):
     """Time the CPU port of the reference path (oracle) on a bounded sample."""
     from oracle import moe_oracle as O
     syn = importlib.import_module("hrm-moe_b200.synthetic")
@@ -189,7 +217,7 @@ def cpu_oracle_tokens_per_s(shape, target_s: float, seed: int = 0, max_tokens: i
                            shape.norm_topk_prob, shape.dtype)
         x = syn.make_hidden(sub, seed)
         t0 = time.perf_counter()
-        O.moe_forward(x, w_r, w_gu, w_d, shape.top_k, shape.norm_topk_prob, shape.dtype)
+        O.moe_forward(x, w_r, w_gu, w_d, shape.top_k, shape.norm_topk_prob, shape.dtype, bias)
         return time.perf_counter() - t0
 
     run(64)  # warm-up (threads, BLAS)
@@ -213,10 +241,11 @@ def reference_arm(args, rank, world):
     sub = syn.MoEShape(sample_T, shape.hidden, shape.experts, shape.intermediate, shape.top_k,
                        shape.norm_topk_prob, shape.dtype)
     x = syn.make_hidden(sub, 0)
+    bias = config_router_bias(syn, args.config, shape, args.dead_experts)
     times = []
     for i in range(args.warmup + args.steps):
         t0 = time.perf_counter()
-        O.moe_forward(x, w_r, w_gu, w_d, shape.top_k, shape.norm_topk_prob, shape.dtype)
+        O.moe_forward(x, w_r, w_gu, w_d, shape.top_k, shape.norm_topk_prob, shape.dtype, bias)
         if i >= args.warmup:
             times.append(time.perf_counter() - t0)
     ms = 1e3 * statistics.mean(times)
@@ -228,8 +257,8 @@ def reference_arm(args, rank, world):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": shape.dtype,
         "data": "synthetic: x~N(0,1), weights~N(0,0.02), numpy PCG64 seed 0",
         "impl": "reference",
-        "config": {"workload": f"{args.config}: XL 64x8 MoE-FFN layer forward, "
-                               f"sample of {sample_T} tokens per step on the host CPU",
+        "config": {"workload": workload_name(args.config, shape, sample_T, args.dead_experts)
+                               + f", a sample of {sample_T} tokens per step on the host CPU",
                    "tokens_per_step": sample_T, "hidden": shape.hidden,
                    "experts": shape.experts, "intermediate": shape.intermediate,
                    "top_k": shape.top_k},
@@ -238,6 +267,153 @@ def reference_arm(args, rank, world):
                                    f"(numpy/OpenBLAS + C, all {cores} host threads)"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------- reference module on the GPU --
+REF_DIR = ROOT / "baseline" / "_ref"
+
+
+def prepare_reference(checkout: str) -> int:
+    """Copy the reference's models/ package into baseline/_ref/ (git-ignored)."""
+    import shutil
+    src = pathlib.Path(checkout) / "models"
+    if not (src / "layers.py").exists():
+        print(f"no models/layers.py under {checkout}", file=sys.stderr)
+        return 2
+    dst = REF_DIR / "models"
+    if dst.exists():
+        shutil.rmtree(dst)
+    shutil.copytree(src, dst, ignore=shutil.ignore_patterns("__pycache__"))
+    print(f"copied {src} -> {dst}")
+    return 0
+
+
+def import_reference_layers():
+    """models.layers from baseline/_ref, with the two FlashAttention modules it
+    imports at module scope stubbed out, as the reference's own equivalence
+    test does (scripts/test_moe_shard_equivalence.py:12-18)."""
+    import types
+    stub = types.ModuleType("models.flash_attention_prefixlm_v2")
+    stub.flash_attn_varlen_prefixlm = None
+    sys.modules.setdefault("models.flash_attention_prefixlm_v2", stub)
+    stub2 = types.ModuleType("flash_attn_interface")
+    stub2.flash_attn_with_kvcache = None
+    sys.modules.setdefault("flash_attn_interface", stub2)
+    sys.path.insert(0, str(REF_DIR))
+    return importlib.import_module("models.layers"), importlib.import_module("models.moe_profile")
+
+
+def reference_gpu_arm(args, rank, world, local_rank):
+    """The reference's own SparseMoESwiGLU(implementation="grouped_triton") on
+    this GPU (its Triton grouped GEMMs, models/moe_triton_grouped_gemm.py:113-184,
+    autotuned, 16 SMs of margin as its README runs them), same workload and
+    weights as the b200 arm, and the same tokens through this build for a
+    same-box comparison of routing and output."""
+    if rank != 0:
+        return 0
+    if not (REF_DIR / "models" / "layers.py").exists():
+        print(json.dumps({"impl": "reference-gpu", "unavailable":
+                          "baseline/_ref/models is absent (bench.py --prepare-reference CHECKOUT)"}))
+        return 0
+    os.environ.setdefault("HRM_MOE_TRITON_AUTOTUNE", "1")
+    os.environ.setdefault("HRM_MOE_TRITON_SM_MARGIN", "16")
+    import torch
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    layers, prof = import_reference_layers()
+    ops = importlib.import_module("hrm-moe_b200.ops")
+    syn = importlib.import_module("hrm-moe_b200.synthetic")
+    base = syn.CONFIGS[args.config]
+    T = args.tokens or base.tokens
+    shape = syn.MoEShape(T, base.hidden, base.experts, base.intermediate, base.top_k,
+                         base.norm_topk_prob, base.dtype)
+    d, E, I, k = shape.hidden, shape.experts, shape.intermediate, shape.top_k
+    dt = torch.bfloat16
+    g = torch.Generator(device=dev).manual_seed(1234)
+    wg = torch.Generator(device=dev).manual_seed(1000)
+    w_router = (torch.randn((E, d), generator=g, device=dev) * 0.02).to(dt)
+    w_gate_up = (torch.randn((E, 2 * I, d), generator=g, device=dev) * 0.02).to(dt)
+    w_down = (torch.randn((E, d, I), generator=g, device=dev) * 0.02).to(dt)
+    x = torch.randn((T, d), generator=wg, device=dev).to(dt)
+    zb = config_router_bias(syn, args.config, shape, args.dead_experts)
+    bias = None if zb is None else torch.from_numpy(zb).to(dev).to(dt)
+    mod = layers.SparseMoESwiGLU(d, I, E, k, shape.norm_topk_prob,
+                                 implementation="grouped_triton")
+    if bias is not None:
+        mod.gate = layers.LinearInit(d, E, bias=True)
+    mod = mod.to(device=dev, dtype=dt)
+    with torch.no_grad():
+        mod.gate.weight.copy_(w_router)
+        if bias is not None:
+            mod.gate.bias.copy_(bias)
+        mod.experts.gate_up_weight.copy_(w_gate_up)
+        mod.experts.down_weight.copy_(w_down)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    prof._MOE_PROFILE_ENABLED = False
+    with torch.no_grad():
+        for _ in range(max(1, args.warmup)):  # the first call autotunes the Triton kernels
+            flush.zero_()
+            mod(x)
+        torch.cuda.synchronize()
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        with ClockSampler(gpu_uuid(torch, local_rank)) as clocks:
+            for i in range(args.steps):
+                flush.zero_()
+                starts[i].record(stream)
+                y_ref = mod(x)
+                ends[i].record(stream)
+            torch.cuda.synchronize()
+        ms = statistics.mean(a.elapsed_time(b) for a, b in zip(starts, ends))
+        # per-phase times from the reference's own profiler (it synchronises
+        # after each phase, so these steps are not the timed ones above)
+        prof._MOE_PROFILE_ENABLED = True
+        prof.reset_moe_profile()
+        n_prof = min(20, args.steps)
+        for _ in range(n_prof):
+            flush.zero_()
+            mod(x)
+        phases = {n: 1e3 * v / n_prof for n, v in prof.pop_moe_profile().items()}
+        prof._MOE_PROFILE_ENABLED = False
+        # same tokens through this build: routing and output agreement
+        cap = {}
+        h = mod.experts.register_forward_pre_hook(
+            lambda m, a: cap.update(selected=a[1].detach().clone()))
+        y_ref = mod(x)
+        h.remove()
+        y_b200, r = ops.ffn_forward(x, w_router, w_gate_up, w_down, k, shape.norm_topk_prob,
+                                    router_bias=bias, return_routing=True)
+        torch.cuda.synchronize()
+    same_rows = (r["topk_idx"].long() == cap["selected"].long()).all(dim=1)
+    diff = (y_b200.float() - y_ref.float()).abs()[same_rows]
+    max_rel = float(diff.max() / y_ref.float().abs()[same_rows].max()) if same_rows.any() else None
+    gu_flops, dn_flops = shape.gemm_flops()
+    gemm = {}
+    for name, flops in (("gate_up_gemm", gu_flops), ("down_gemm", dn_flops)):
+        if name in phases:
+            gemm[name] = {"ms": phases[name], "tflops": flops / (phases[name] * 1e-3) / 1e12}
+    line = {
+        "metric": METRIC, "value": T / (ms * 1e-3), "unit": "tokens/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "impl": "reference-gpu",
+        "data": "synthetic: x~N(0,1), weights~N(0,0.02) (seeded torch.Generator on device)",
+        "config": {"workload": workload_name(args.config, shape, T, args.dead_experts),
+                   "module": "models.layers.SparseMoESwiGLU(implementation='grouped_triton')",
+                   "env": {k_: os.environ[k_] for k_ in ("HRM_MOE_TRITON_AUTOTUNE",
+                                                         "HRM_MOE_TRITON_SM_MARGIN")},
+                   "l2": "256 MiB buffer rewritten before every step (outside the timed events)"},
+        "phases_ms": phases,
+        "gemms": gemm,
+        "vs_b200_same_inputs": {
+            "rows": T, "rows_same_routing": int(same_rows.sum()),
+            "max_rel_y_on_same_rows": max_rel,
+        },
+        "clocks": clocks.summary(),
     }
     print(json.dumps(line), flush=True)
     return 0
@@ -273,6 +449,13 @@ def b200_arm(args, rank, world, local_rank):
     w_down = (torch.randn((E, d, I), generator=g, device=dev) * 0.02).to(dt)
     x = torch.randn((T, d), generator=wg, device=dev).to(dt)
     y = torch.empty_like(x)
+    # cfg4: a router bias that makes expected expert selection follow
+    # Zipf(1.2) over a seeded permutation (optionally with dead experts)
+    bias = None
+    if args.config.startswith("cfg4"):
+        zb = syn.zipf_router_bias(E, 4, dead_experts=args.dead_experts)
+        bias = torch.from_numpy(zb).to(dev).to(dt)
+    bias_p = ctypes.c_void_p(bias.data_ptr()) if bias is not None else None
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
 
     lib = _lib.load()
@@ -292,7 +475,7 @@ def b200_arm(args, rank, world, local_rank):
         arr = (ctypes.c_void_p * n_marks)(*[ctypes.c_void_p(m.cuda_event) for m in marks])
         _lib.check(lib.hmoe_ffn_forward_marked(
             ctypes.byref(cshape), ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(w_router.data_ptr()),
-            None, ctypes.c_void_p(w_gate_up.data_ptr()), ctypes.c_void_p(w_down.data_ptr()),
+            bias_p, ctypes.c_void_p(w_gate_up.data_ptr()), ctypes.c_void_p(w_down.data_ptr()),
             ctypes.c_void_p(y.data_ptr()), 0, ctypes.c_void_p(ws.data_ptr()), ws.numel(),
             ctypes.c_void_p(stream.cuda_stream), arr))
 
@@ -302,10 +485,13 @@ def b200_arm(args, rank, world, local_rank):
         # expert parallel: this rank keeps experts [rank*E/N, (rank+1)*E/N)
         ep = importlib.import_module("hrm-moe_b200.ep")
         el = E // world
+        # every rank drew all experts' weights from the same seed; the full
+        # set stays until the parity check below has run
+        w_gate_up_full, w_down_full = w_gate_up, w_down
         w_gate_up = w_gate_up[rank * el:(rank + 1) * el].contiguous()
         w_down = w_down[rank * el:(rank + 1) * el].contiguous()
         # rows per (source rank, expert), from one untimed routing pass
-        idx, _ = ops.router_topk(x, w_router, k, shape.norm_topk_prob)
+        idx, _ = ops.router_topk(x, w_router, k, shape.norm_topk_prob, bias)
         cnt = torch.bincount(idx.reshape(-1).long(), minlength=E).to(torch.int64)
         cnt_all = [torch.empty_like(cnt) for _ in range(world)]
         dist.all_gather(cnt_all, cnt)
@@ -318,11 +504,11 @@ def b200_arm(args, rank, world, local_rank):
             peer = ep.PeerExpertParallel(d, I, E, k, shape.norm_topk_prob, max_tokens=T, dtype=dt)
 
             def step(marks):  # noqa: F811  (EP replaces the single-GPU step)
-                peer.forward(x, w_router, w_gate_up, w_down, y=y, marks=marks)
+                peer.forward(x, w_router, w_gate_up, w_down, router_bias=bias, y=y, marks=marks)
         else:
             def step(marks):  # noqa: F811
-                ep.ep_forward(x, w_router, w_gate_up, w_down, E, k, shape.norm_topk_prob,
-                              marks=marks)
+                y.copy_(ep.ep_forward(x, w_router, w_gate_up, w_down, E, k,
+                                      shape.norm_topk_prob, router_bias=bias, marks=marks))
 
     warm_marks = make_events(n_marks)
     for _ in range(args.warmup):
@@ -332,6 +518,31 @@ def b200_arm(args, rank, world, local_rank):
     ops.workspace_status(ws)
     if peer is not None:
         peer.status()
+
+    # ------------------------------------- expert-parallel parity (untimed)
+    # One more expert-parallel step, then each rank runs the single-GPU layer
+    # (all experts, same tokens, same router) and compares: the EP output
+    # must be bit-identical (same kernels, same order per row).
+    ep_parity = None
+    if world > 1:
+        y.zero_()
+        step(warm_marks)
+        y_ref = ops.ffn_forward(x, w_router, w_gate_up_full, w_down_full, k,
+                                shape.norm_topk_prob, router_bias=bias)
+        torch.cuda.synchronize()
+        yd, rd = y.float(), y_ref.float()
+        t = torch.tensor([0.0 if torch.equal(y, y_ref) else 1.0,
+                          float((yd - rd).abs().max()),
+                          float((yd - rd).abs().max() / rd.abs().max().clamp_min(1e-30)),
+                          0.0 if bool(torch.isfinite(yd).all()) else 1.0], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ep_parity = {"bit_exact": bool(t[0].item() == 0.0), "max_abs_diff": float(t[1].item()),
+                     "max_rel": float(t[2].item()), "all_finite": bool(t[3].item() == 0.0),
+                     "tokens_checked": world * T,
+                     "against": "the single-GPU layer (hmoe_ffn_forward, all experts) on each "
+                                "rank's own tokens"}
+        del y_ref, yd, rd, w_gate_up_full, w_down_full
+        torch.cuda.empty_cache()
 
     marks = [make_events(n_marks) for _ in range(args.steps)]
     starts = make_events(args.steps)
@@ -386,7 +597,7 @@ def b200_arm(args, rank, world, local_rank):
         with torch.cuda.graph(graph, stream=cap, capture_error_mode="relaxed"):
             _lib.check(lib.hmoe_ffn_forward(
                 ctypes.byref(cshape), ctypes.c_void_p(x.data_ptr()),
-                ctypes.c_void_p(w_router.data_ptr()), None, ctypes.c_void_p(w_gate_up.data_ptr()),
+                ctypes.c_void_p(w_router.data_ptr()), bias_p, ctypes.c_void_p(w_gate_up.data_ptr()),
                 ctypes.c_void_p(w_down.data_ptr()), ctypes.c_void_p(y.data_ptr()), 0, None, None,
                 None, None, ctypes.c_void_p(ws.data_ptr()), ws.numel(),
                 ctypes.c_void_p(cap.cuda_stream)))
@@ -426,7 +637,8 @@ def b200_arm(args, rank, world, local_rank):
             if i >= args.warmup:
                 e_s[i - args.warmup].record(stream)
             ops.ffn_forward_host(x_host, w_router, w_gate_up, w_down, k, shape.norm_topk_prob,
-                                 y_host=y_host, chunk_tokens=chunk, workspace=hws)
+                                 router_bias=bias, y_host=y_host, chunk_tokens=chunk,
+                                 workspace=hws)
             if i >= args.warmup:
                 e_e[i - args.warmup].record(stream)
         torch.cuda.synchronize()
@@ -452,7 +664,7 @@ def b200_arm(args, rank, world, local_rank):
             if i >= args.warmup:
                 e_s[i - args.warmup].record(stream)
             peer.forward_host(x_host, w_router, w_gate_up, w_down, y_host=y_host,
-                              chunk_tokens=chunk)
+                              chunk_tokens=chunk, router_bias=bias)
             if i >= args.warmup:
                 e_e[i - args.warmup].record(stream)
         torch.cuda.synchronize()
@@ -545,7 +757,9 @@ def b200_arm(args, rank, world, local_rank):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        tps, Ts, secs = cpu_oracle_tokens_per_s(shape, args.cpu_seconds)
+        tps, Ts, secs = cpu_oracle_tokens_per_s(
+            shape, args.cpu_seconds,
+            bias=config_router_bias(syn, args.config, shape, args.dead_experts))
         cpu = {"value": tps, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
                "sample": f"{Ts} tokens of the {args.config} layer in {secs:.1f} s "
                          f"(numpy/OpenBLAS + C router, {os.cpu_count()} host threads)"}
@@ -563,8 +777,7 @@ def b200_arm(args, rank, world, local_rank):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": shape.dtype,
         "data": "synthetic: x~N(0,1), weights~N(0,0.02) (seeded torch.Generator on device)",
-        "config": {"workload": f"{args.config}: XL 64x8 MoE-FFN layer forward "
-                               f"(T={T} tokens per GPU, d={d}, E={E}, I={I}, top-{k})",
+        "config": {"workload": workload_name(args.config, shape, T, args.dead_experts),
                    "tokens_per_gpu": T, "global_tokens": world * T,
                    "parallelism": ("single GPU" if world == 1 else
                                    f"expert parallel x{world} ({E // world} experts per GPU, "
@@ -585,15 +798,21 @@ def b200_arm(args, rank, world, local_rank):
         "gpu_launches": (10 if peer is not None else 8) * args.steps,
         "clocks": clk,
     }
+    if ep_parity is not None:
+        line["ep_parity"] = ep_parity
     print(json.dumps(line), flush=True)
     return 0
 
 
 def main():
     args = parse_args()
+    if args.prepare_reference:
+        return prepare_reference(args.prepare_reference)
     rank, world, local_rank = dist_env()
     if args.impl == "reference":
         return reference_arm(args, rank, world)
+    if args.impl == "reference-gpu":
+        return reference_gpu_arm(args, rank, world, local_rank)
     return b200_arm(args, rank, world, local_rank)
 
 

@@ -190,6 +190,17 @@ int check_ws(void* ws, size_t have, size_t need) {
   return HMOE_OK;
 }
 
+// A call with no tokens still defines tokens_per_expert: E zeros (the
+// reference's bincount(..., minlength=E), models/layers.py:322).
+int zero_counts_if_empty(int32_t* counts, int E, void* stream) {
+  if (!counts) return HMOE_OK;
+  int rc = select_device(counts);
+  if (rc) return rc;
+  HMOE_CUDA(cudaMemsetAsync(counts, 0, sizeof(int32_t) * E, static_cast<cudaStream_t>(stream)),
+            "clear counts");
+  return HMOE_OK;
+}
+
 int sm_margin() {
   static int margin = [] {
     const char* v = getenv("HRM_MOE_B200_SM_MARGIN");
@@ -369,7 +380,7 @@ int ffn_forward_impl(const hmoe_shape* shape, const void* x, const void* w_route
   int rc = validate_shape(shape);
   if (rc) return rc;
   const hmoe_shape& s = *shape;
-  if (s.tokens == 0) return HMOE_OK;
+  if (s.tokens == 0) return zero_counts_if_empty(counts, s.experts, stream);
   if (!x || !w_router || !w_gate_up || !w_down || !y)
     return fail(HMOE_EINVAL, "x, w_router, w_gate_up, w_down and y are required");
   if (!aligned16(x) || !aligned16(w_gate_up) || !aligned16(w_down) || !aligned16(y) ||
@@ -664,7 +675,7 @@ int hmoe_dispatch(const hmoe_shape* shape, const int32_t* topk_idx, const void* 
   int rc = validate_shape(shape);
   if (rc) return rc;
   const hmoe_shape& s = *shape;
-  if (s.tokens == 0) return HMOE_OK;
+  if (s.tokens == 0) return zero_counts_if_empty(counts, s.experts, stream);
   if (!topk_idx) return fail(HMOE_EINVAL, "topk_idx is required");
   if (sorted_weight && !topk_weight) return fail(HMOE_EINVAL, "sorted_weight needs topk_weight");
   if (x_sorted && (!x || !aligned16(x) || !aligned16(x_sorted)))
@@ -696,7 +707,7 @@ int hmoe_experts_forward(const hmoe_shape* shape, const void* hidden, const int3
   int rc = validate_shape(shape);
   if (rc) return rc;
   const hmoe_shape& s = *shape;
-  if (s.tokens == 0) return HMOE_OK;
+  if (s.tokens == 0) return zero_counts_if_empty(counts, s.experts, stream);
   if (!hidden || !topk_idx || !topk_weight || !w_gate_up || !w_down || !final_hidden_states)
     return fail(HMOE_EINVAL, "all tensor arguments are required");
   if (!aligned16(hidden) || !aligned16(w_gate_up) || !aligned16(w_down) ||

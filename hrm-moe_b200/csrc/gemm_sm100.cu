@@ -244,13 +244,13 @@ __device__ __forceinline__ void push_rows(const KParams& p, const SmemCtl& ctl, 
       const int eb = ctl.push_ebase[e];
       uint4* rows = p.push_rows[o];
       int32_t* srcs = p.push_src[o];
-      for (int64_t vv = v; vv < seg_end; ++vv) {
+      // q = sb + (vv - vs) grows with vv: rows from vv = vs + push_cap - sb on
+      // would land beyond the owner's receive buffer and are not stored.
+      const int64_t store_end = min(seg_end, vs + (p.push_cap - sb));
+      if (store_end < seg_end && lane == 0) record_error(p.err, kDevEpOverflow);
+      for (int64_t vv = v; vv < store_end; ++vv) {
         const int64_t rel = vv - vs;
         const int64_t q = sb + rel;
-        if (q >= p.push_cap) {
-          if (lane == 0) record_error(p.err, kDevEpOverflow);
-          continue;
-        }
         const int pos = eb + static_cast<int>(rel);
         const int t = p.push_sorted_token[pos];
         push_copy_row(p.push_x + static_cast<int64_t>(t) * rc, rows + q * rc, rc, lane);
@@ -260,7 +260,11 @@ __device__ __forceinline__ void push_rows(const KParams& p, const SmemCtl& ctl, 
       }
       __threadfence_system();
       __syncwarp();
-      if (lane == 0) red_release_sys_add(p.push_arrived[o] + el, static_cast<uint32_t>(seg_end - v));
+      // Only the rows actually stored count as arrived: after an overflow the
+      // owner's group never completes, so its bounded wait reports a timeout
+      // instead of computing on rows that were never written.
+      if (lane == 0 && store_end > v)
+        red_release_sys_add(p.push_arrived[o] + el, static_cast<uint32_t>(store_end - v));
       v = seg_end;
     }
   }

@@ -15,7 +15,9 @@
 // process exits.  In host code the array's name is only a host-side stand-in,
 // never a device address, so the first call on each device (with that device
 // current) looks the real address up with cudaGetSymbolAddress and caches
-// it; make that first call before any stream capture.  All calls on a device
+// it per CUDA context (a context of its own, or one made after
+// cudaDeviceReset(), gets a fresh lookup); make the first call in each
+// context before any stream capture.  All calls on a device
 // share the array and it keeps the last call's contents; the kernels below
 // write every scratch word they later read, so nothing needs clearing, but
 // two calls that overlap on the GPU (different streams, no ordering between
@@ -42,21 +44,67 @@ constexpr size_t kScratchBytes = align256(kOffOffsets + sizeof(int32_t) * (kMaxE
 
 static __device__ __align__(256) unsigned char g_dispatch_scratch[kScratchBytes];
 
-// Device address of the scratch array on the current device (looked up once).
-int scratch_address(int dev, char** out) {
-  static char* addr[64] = {nullptr};
-  static std::mutex mu;
-  if (dev < 0 || dev >= 64) return hmoe::report_error(HMOE_EINVAL, "device ordinal %d out of range", dev);
-  std::lock_guard<std::mutex> lock(mu);
-  if (!addr[dev]) {
+// Device address of the scratch array in the CUDA context current on the
+// calling thread.  A __device__ symbol has one address per context (each
+// context loads its own copy of the module), so the cache is keyed by the
+// context's unique id (cuCtxGetId), not by the device ordinal: a host that
+// makes its own context current, or a context created after
+// cudaDeviceReset(), gets its own lookup instead of a stale address.
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+typedef CUresult (*CtxGetIdFn)(CUcontext, unsigned long long*);
+
+struct CtxFns {
+  CtxGetCurrentFn get_current = nullptr;
+  CtxGetIdFn get_id = nullptr;
+};
+
+const CtxFns& ctx_fns() {
+  static CtxFns fns;
+  static std::once_flag once;
+  std::call_once(once, [] {
     void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_dispatch_scratch);
-    if (e != cudaSuccess || p == nullptr)
-      return hmoe::report_error(HMOE_EIO, "cudaGetSymbolAddress(dispatch scratch): %s",
-                                cudaGetErrorString(e));
-    addr[dev] = static_cast<char*>(p);
-  }
-  *out = addr[dev];
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess && q == cudaDriverEntryPointSuccess)
+      fns.get_current = reinterpret_cast<CtxGetCurrentFn>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetId", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess && q == cudaDriverEntryPointSuccess)
+      fns.get_id = reinterpret_cast<CtxGetIdFn>(p);
+  });
+  return fns;
+}
+
+int scratch_address(char** out) {
+  constexpr int kSlots = 64;
+  struct Slot {
+    unsigned long long ctx_id;
+    char* addr;
+  };
+  static Slot slots[kSlots] = {};
+  static int next = 0;
+  static std::mutex mu;
+  const CtxFns& f = ctx_fns();
+  if (!f.get_current || !f.get_id)
+    return hmoe::report_error(HMOE_EIO, "cuCtxGetCurrent / cuCtxGetId are not available");
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (f.get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr || f.get_id(ctx, &id) != CUDA_SUCCESS)
+    return hmoe::report_error(HMOE_EIO, "no current CUDA context for the dispatch scratch");
+  std::lock_guard<std::mutex> lock(mu);
+  for (const Slot& s : slots)
+    if (s.addr && s.ctx_id == id) {
+      *out = s.addr;
+      return HMOE_OK;
+    }
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_dispatch_scratch);
+  if (e != cudaSuccess || p == nullptr)
+    return hmoe::report_error(HMOE_EIO, "cudaGetSymbolAddress(dispatch scratch): %s",
+                              cudaGetErrorString(e));
+  slots[next] = Slot{id, static_cast<char*>(p)};
+  next = (next + 1) % kSlots;
+  *out = static_cast<char*>(p);
   return HMOE_OK;
 }
 
@@ -80,7 +128,15 @@ extern "C" int hmoe_dispatch_noalloc(const hmoe_shape* shape, const int32_t* top
   if (nblk > kMaxBlocks)
     return report_error(HMOE_EINVAL, "hmoe_dispatch_noalloc: %lld histogram blocks exceed %lld",
                         static_cast<long long>(nblk), static_cast<long long>(kMaxBlocks));
-  if (s.tokens == 0) return HMOE_OK;
+  if (s.tokens == 0) {
+    // no assignments: tokens_per_expert is E zeros (bincount with minlength=E)
+    if (!counts) return HMOE_OK;
+    if ((rc = make_device_current(counts))) return rc;
+    const cudaError_t e = cudaMemsetAsync(counts, 0, sizeof(int32_t) * s.experts,
+                                          static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return report_error(HMOE_EIO, "clear counts: %s", cudaGetErrorString(e));
+    return HMOE_OK;
+  }
   if (!topk_idx || !sort_idx) return report_error(HMOE_EINVAL, "topk_idx and sort_idx are required");
   if (sorted_weight && !topk_weight)
     return report_error(HMOE_EINVAL, "sorted_weight needs topk_weight");
@@ -88,11 +144,9 @@ extern "C" int hmoe_dispatch_noalloc(const hmoe_shape* shape, const int32_t* top
                    (reinterpret_cast<uintptr_t>(x_sorted) & 15u)))
     return report_error(HMOE_EINVAL, "x_sorted needs 16-byte aligned x and x_sorted");
   if ((rc = make_device_current(topk_idx))) return rc;
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return report_error(HMOE_EIO, "cudaGetDevice: %s", cudaGetErrorString(e));
   char* base = nullptr;
-  if ((rc = scratch_address(dev, &base))) return rc;
+  if ((rc = scratch_address(&base))) return rc;
+  cudaError_t e;
   int32_t* local_rank = reinterpret_cast<int32_t*>(base + kOffRank);
   int32_t* pos = reinterpret_cast<int32_t*>(base + kOffPos);
   int32_t* blocks = reinterpret_cast<int32_t*>(base + kOffBlocks);

@@ -25,10 +25,18 @@ from . import ops
 IMPLEMENTATIONS = ("grouped_b200",)
 
 
+# std of a standard normal folded into (-3, 3) by fmod is 1 / 1.0147626...;
+# the reference scales by this factor so the folded values have std 1.
+_FOLDED_NORMAL_STD_FIX = 1.014762601732121
+
+
 def trunc_normal_(t: Tensor, std: float) -> Tensor:
-    """Truncated normal init at +-2 std (the reference uses a LeCun-style truncated normal)."""
+    """The reference's weight init (models/common.py:10-13): draw N(0, 1), fold
+    values beyond +-3 back with fmod(3), and scale so the result has the given
+    std.  Same distribution as the reference's parameters, so a randomly
+    initialised layer here matches one built there."""
     with torch.no_grad():
-        return nn.init.trunc_normal_(t, mean=0.0, std=std, a=-2 * std, b=2 * std)
+        return t.normal_().fmod_(3.0).mul_(_FOLDED_NORMAL_STD_FIX * std)
 
 
 class LinearInit(nn.Module):

@@ -26,7 +26,9 @@
  *                            (torch.sort(flat, stable=True), layers.py:317)
  *
  * Status codes are errno values; hmoe_last_error() describes the last
- * failure on the calling thread.
+ * failure on the calling thread.  A call with tokens == 0 launches nothing;
+ * where it has a counts output, it writes E zeros there (the reference's
+ * bincount(..., minlength=E)).
  */
 #ifndef HRM_MOE_H
 #define HRM_MOE_H
@@ -201,14 +203,18 @@ int hmoe_combine(const hmoe_shape* shape, const void* expert_out, const int32_t*
  * exists for hosts that cannot give this library device memory for scratch
  * (a plugin host with no CUDA allocator binding, a process whose device
  * memory another framework has reserved up front, a serving loop that must
- * not allocate after start-up).  Same inputs, outputs and results as
- * hmoe_dispatch; the scratch lives in one fixed __device__ array of about
- * 2.3 MiB that every GPU loading the library keeps until exit.  At most
+ * not allocate after start-up).  Same inputs and outputs as hmoe_dispatch,
+ * and the same results while every expert id is in [0, E); the scratch
+ * lives in one fixed __device__ array of about 2.3 MiB that every GPU
+ * loading the library keeps until exit.  At most
  * HMOE_DISPATCH_NOALLOC_MAX_ASSIGNMENTS assignments (tokens * top_k) per
- * call; larger calls fail with HMOE_EINVAL.  The first call on a device
- * looks up the array's device address (make it before any stream capture).
- * Calls share the array: two calls that overlap on the GPU race.  Expert ids
- * outside [0, E) are dropped without an error report.  Allocates nothing.
+ * call; larger calls fail with HMOE_EINVAL.  The first call in each CUDA
+ * context looks up the array's device address there and caches it per
+ * context (make that call before any stream capture).  Calls share the
+ * array: two calls that overlap on the GPU race.  Expert ids outside [0, E)
+ * are dropped without an error report (there is no error word): counts
+ * leave them out, and only the first sum(counts) entries of sort_idx,
+ * sorted_token, sorted_weight and x_sorted are written.  Allocates nothing.
  */
 #define HMOE_DISPATCH_NOALLOC_MAX_ASSIGNMENTS 262144
 int hmoe_dispatch_noalloc(const hmoe_shape* shape, const int32_t* topk_idx,

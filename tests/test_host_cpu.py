@@ -55,3 +55,17 @@ def test_reference_state_dict_loads(tmp_path):
     m = layers.SparseMoESwiGLU(16, 32, 8, 2, True)
     m.load_state_dict(src)
     assert torch.equal(m.experts.down_weight, src["experts.down_weight"])
+
+
+def test_init_matches_reference_distribution():
+    """Parameters are drawn like the reference's trunc_normal_init_
+    (models/common.py:10-13): N(0,1) folded into (-3, 3) by fmod, scaled to
+    the requested std, so fresh layers have the reference's weight scale."""
+    import torch
+    layers = package().layers
+    torch.manual_seed(0)
+    mod = layers.SparseMoESwiGLU(256, 128, 16, 4, True, implementation="grouped_b200")
+    for t, std in ((mod.gate.weight, 256 ** -0.5), (mod.experts.gate_up_weight, 256 ** -0.5),
+                   (mod.experts.down_weight, 128 ** -0.5)):
+        assert abs(float(t.std()) / std - 1.0) < 0.02
+        assert float(t.abs().max()) <= 3.0 * 1.014762601732121 * std * (1 + 1e-6)
