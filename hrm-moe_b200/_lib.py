@@ -75,6 +75,21 @@ SIGNATURES = {
                                     c_int32, c_int32, c_void_p, c_void_p, c_size_t, c_void_p]),
     "hmoe_grouped_swiglu": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int32, c_int32,
                                     c_int32, c_int32, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "hmoe_grouped_linear_backward": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64,
+                                             c_int32, c_int32, c_int32, c_int32, c_void_p,
+                                             c_void_p, c_void_p, c_size_t, c_void_p]),
+    "hmoe_grouped_swiglu_backward": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64,
+                                             c_int32, c_int32, c_int32, c_void_p, c_void_p,
+                                             c_size_t, c_void_p]),
+    "hmoe_ffn_train_saved_bytes": (c_size_t, [ShapeP]),
+    "hmoe_ffn_train_workspace_bytes": (c_size_t, [ShapeP]),
+    "hmoe_ffn_forward_train": (c_int, [ShapeP, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                       c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_size_t,
+                                       c_void_p, c_size_t, c_void_p]),
+    "hmoe_ffn_backward": (c_int, [ShapeP, c_void_p, c_void_p, c_int64, c_void_p, c_void_p,
+                                  c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p,
+                                  c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t,
+                                  c_void_p]),
     "hmoe_grouped_gemm_mapped": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int32,
                                          c_int32, c_int32, c_int32, c_int32, c_int32, c_void_p,
                                          c_void_p, c_size_t, c_void_p]),

@@ -779,6 +779,101 @@ int hmoe_grouped_gemm_mapped(const void* input, const void* weight, const int32_
                         workspace_bytes, stream, swiglu ? 1 : 0, group_weight, num_weights);
 }
 
+int hmoe_grouped_linear_backward(const void* grad_out, const void* input, const void* weight,
+                                 const int32_t* tpe, int64_t M, int32_t N, int32_t K, int32_t G,
+                                 int32_t dtype, void* grad_input, void* grad_weight,
+                                 void* workspace, size_t workspace_bytes, void* stream) {
+  if (M < 0 || N <= 0 || K <= 0 || G <= 0)
+    return fail(HMOE_EINVAL, "bad grouped GEMM shape M=%lld N=%d K=%d G=%d", (long long)M, N, K, G);
+  if (dtype != HMOE_DTYPE_BF16)
+    return fail(HMOE_EINVAL, "the grouped GEMM backward supports bf16 only (dtype %d)", dtype);
+  if (N % 8 != 0 || K % 8 != 0) return fail(HMOE_EINVAL, "N and K must be multiples of 8");
+  if (G > 1024) return fail(HMOE_EINVAL, "at most 1024 groups");
+  if (!tpe) return fail(HMOE_EINVAL, "tokens_per_expert is required");
+  if (grad_input && (!grad_out || !weight || !aligned16(grad_out) || !aligned16(weight) ||
+                     !aligned16(grad_input)))
+    return fail(HMOE_EINVAL, "grad_input needs 16-byte aligned grad_out, weight, grad_input");
+  if (grad_weight && (!aligned16(grad_weight) ||
+                      (M > 0 && (!grad_out || !input || !aligned16(grad_out) || !aligned16(input)))))
+    return fail(HMOE_EINVAL, "grad_weight needs 16-byte aligned grad_out, input, grad_weight");
+  if (!grad_input && !grad_weight) return HMOE_OK;
+  int rc = select_device(tpe);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int* err = nullptr;
+  if (workspace && workspace_bytes >= sizeof(int)) {
+    err = static_cast<int*>(workspace);
+    HMOE_CUDA(cudaMemsetAsync(err, 0, sizeof(int), st), "reset error word");
+  }
+  if (grad_input && M > 0) {
+    GroupedDgradArgs a;
+    a.grad_out = grad_out;
+    a.weight = weight;
+    a.counts = tpe;
+    a.out = grad_input;
+    a.M = M;
+    a.Kc = N;
+    a.Nout = K;
+    a.G = G;
+    a.err = err;
+    a.sm_limit = 0;
+    HMOE_CUDA(launch_grouped_dgrad(a, st), "grouped dgrad");
+  }
+  if (grad_weight) {
+    GroupedWgradArgs a;
+    a.grad_out = grad_out;
+    a.input = input;
+    a.counts = tpe;
+    a.out = grad_weight;
+    a.M = M;
+    a.Mw = N;
+    a.Nw = K;
+    a.G = G;
+    a.err = err;
+    a.sm_limit = 0;
+    HMOE_CUDA(launch_grouped_wgrad(a, st), "grouped wgrad");
+  }
+  return HMOE_OK;
+}
+
+int hmoe_grouped_swiglu_backward(const void* grad_out, const void* w_down, const void* gate_up,
+                                 const int32_t* tpe, int64_t M, int32_t d, int32_t I, int32_t G,
+                                 void* d_gate_up, void* workspace, size_t workspace_bytes,
+                                 void* stream) {
+  if (M < 0 || d <= 0 || I <= 0 || G <= 0)
+    return fail(HMOE_EINVAL, "bad shape M=%lld d=%d I=%d G=%d", (long long)M, d, I, G);
+  if (d % 8 != 0 || I % 8 != 0) return fail(HMOE_EINVAL, "d and I must be multiples of 8");
+  if (G > 1024) return fail(HMOE_EINVAL, "at most 1024 groups");
+  if (M == 0) return HMOE_OK;
+  if (!grad_out || !w_down || !gate_up || !tpe || !d_gate_up)
+    return fail(HMOE_EINVAL, "NULL tensor argument");
+  if (!aligned16(grad_out) || !aligned16(w_down) || !aligned16(gate_up) || !aligned16(d_gate_up))
+    return fail(HMOE_EINVAL, "tensors must be 16-byte aligned");
+  int rc = select_device(grad_out);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int* err = nullptr;
+  if (workspace && workspace_bytes >= sizeof(int)) {
+    err = static_cast<int*>(workspace);
+    HMOE_CUDA(cudaMemsetAsync(err, 0, sizeof(int), st), "reset error word");
+  }
+  GroupedDgradArgs a;
+  a.grad_out = grad_out;
+  a.weight = w_down;
+  a.counts = tpe;
+  a.out = nullptr;
+  a.gate_up = gate_up;
+  a.d_gate_up = d_gate_up;
+  a.M = M;
+  a.Kc = d;
+  a.Nout = I;
+  a.G = G;
+  a.err = err;
+  a.sm_limit = 0;
+  HMOE_CUDA(launch_grouped_dgrad(a, st), "grouped swiglu dgrad");
+  return HMOE_OK;
+}
+
 size_t hmoe_combine_workspace_bytes(const hmoe_shape* shape) {
   return plan_bytes(shape, [](Carve& c, const hmoe_shape& s) {
     c.take<int32_t>(sizeof(int32_t) * s.tokens * s.top_k);
@@ -806,6 +901,323 @@ int hmoe_combine(const hmoe_shape* shape, const void* expert_out, const int32_t*
   HMOE_CUDA(launch_combine(expert_out, pos, topk_weight, 0, nullptr, s.experts, s.tokens, s.hidden,
                            s.top_k, s.dtype, final_hidden_states, final_hidden_states, st),
             "combine");
+  return HMOE_OK;
+}
+
+// ------------------------------------------------------------ training ----
+}  // extern "C"
+
+namespace {
+
+// Activations the backward needs, kept by the training forward.
+struct TrainSaved {
+  uint16_t* logits;     // [T, E]
+  int32_t* topk_idx;    // [A]
+  float* topk_w;        // [A] (rounded to bf16)
+  int32_t* counts;      // [E] rows per expert
+  int32_t* pos;         // [A] sorted position of assignment t*k+j
+  float* aux_counts;    // [E] selections among the aux tokens
+  void* x_sorted;       // [A, d]
+  void* gate_up;        // [A, 2I]
+  void* h;              // [A, I]
+  void* expert_out;     // [A, d] before the routing weight
+};
+
+TrainSaved carve_saved(Carve& c, const hmoe_shape& s) {
+  TrainSaved b;
+  const int64_t A = s.tokens * s.top_k;
+  b.logits = c.take<uint16_t>(sizeof(uint16_t) * s.tokens * s.experts);
+  b.topk_idx = c.take<int32_t>(sizeof(int32_t) * A);
+  b.topk_w = c.take<float>(sizeof(float) * A);
+  b.counts = c.take<int32_t>(sizeof(int32_t) * s.experts);
+  b.pos = c.take<int32_t>(sizeof(int32_t) * A);
+  b.aux_counts = c.take<float>(sizeof(float) * s.experts);
+  b.x_sorted = c.take<void>(2 * A * s.hidden);
+  b.gate_up = c.take<void>(2 * A * 2 * s.intermediate);
+  b.h = c.take<void>(2 * A * s.intermediate);
+  b.expert_out = c.take<void>(2 * A * s.hidden);
+  return b;
+}
+
+// Scratch of the training forward and of the backward (one size for both).
+struct TrainWs {
+  int* err;
+  DispatchBufs d;        // forward
+  void* router_scratch;  // forward
+  float* part_p;         // aux / bias partial sums
+  int* part_c;
+  float* aux_tmp;        // forward: aux loss when the caller wants none
+  int32_t* count_T;      // backward: T, the router GEMMs' one group
+  uint16_t* d_logits;    // backward [T, E]
+  void* d_eo;            // backward [A, d], later d_x_sorted
+  void* d_gu;            // backward [A, 2I]
+  void* dx_router;       // backward [T, d]
+};
+
+TrainWs carve_train_ws(Carve& c, const hmoe_shape& s) {
+  TrainWs b;
+  const int64_t A = s.tokens * s.top_k;
+  const int nb = train_partial_blocks(s.tokens);
+  b.d = carve_dispatch(c, s);
+  b.err = b.d.err;
+  b.router_scratch = c.take<void>(router_tc_scratch_bytes(s.tokens));
+  b.part_p = c.take<float>(sizeof(float) * nb * s.experts);
+  b.part_c = c.take<int>(sizeof(int) * nb * s.experts);
+  b.aux_tmp = c.take<float>(sizeof(float));
+  b.count_T = c.take<int32_t>(sizeof(int32_t));
+  b.d_logits = c.take<uint16_t>(sizeof(uint16_t) * s.tokens * s.experts);
+  b.d_eo = c.take<void>(2 * A * s.hidden);
+  b.d_gu = c.take<void>(2 * A * 2 * s.intermediate);
+  b.dx_router = c.take<void>(2 * s.tokens * s.hidden);
+  return b;
+}
+
+int check_train_shape(const hmoe_shape* shape) {
+  int rc = validate_shape(shape);
+  if (rc) return rc;
+  if (shape->dtype != HMOE_DTYPE_BF16)
+    return fail(HMOE_EINVAL, "the training path supports bf16 only (the reference's Triton "
+                             "backward raises TypeError for other dtypes)");
+  if (shape->experts % 8 != 0)
+    return fail(HMOE_EINVAL, "the training path needs experts to be a multiple of 8 (got %d)",
+                shape->experts);
+  return HMOE_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t hmoe_ffn_train_saved_bytes(const hmoe_shape* shape) {
+  return plan_bytes(shape, [](Carve& c, const hmoe_shape& s) { carve_saved(c, s); });
+}
+
+size_t hmoe_ffn_train_workspace_bytes(const hmoe_shape* shape) {
+  return plan_bytes(shape, [](Carve& c, const hmoe_shape& s) { carve_train_ws(c, s); });
+}
+
+int hmoe_ffn_forward_train(const hmoe_shape* shape, const void* x, const void* w_router,
+                           const void* router_bias, const void* w_gate_up, const void* w_down,
+                           void* y, int64_t aux_tokens, float* aux_loss, float* expert_counts,
+                           void* saved, size_t saved_bytes, void* workspace,
+                           size_t workspace_bytes, void* stream) {
+  int rc = check_train_shape(shape);
+  if (rc) return rc;
+  const hmoe_shape& s = *shape;
+  if (aux_tokens > s.tokens) return fail(HMOE_EINVAL, "aux_tokens exceeds tokens");
+  if (s.tokens == 0) {
+    if (aux_loss && (rc = select_device(aux_loss)) == HMOE_OK)
+      HMOE_CUDA(cudaMemsetAsync(aux_loss, 0, sizeof(float), static_cast<cudaStream_t>(stream)),
+                "clear aux");
+    if (rc) return rc;
+    if (expert_counts && (rc = select_device(expert_counts)) == HMOE_OK)
+      HMOE_CUDA(cudaMemsetAsync(expert_counts, 0, sizeof(float) * s.experts,
+                                static_cast<cudaStream_t>(stream)), "clear counts");
+    return rc;
+  }
+  if (!x || !w_router || !w_gate_up || !w_down || !y)
+    return fail(HMOE_EINVAL, "x, w_router, w_gate_up, w_down and y are required");
+  if (!aligned16(x) || !aligned16(w_gate_up) || !aligned16(w_down) || !aligned16(y) ||
+      !aligned16(w_router))
+    return fail(HMOE_EINVAL, "x, weights and y must be 16-byte aligned");
+  if ((rc = select_device(x))) return rc;
+  if ((rc = check_ws(saved, saved_bytes, hmoe_ffn_train_saved_bytes(shape)))) return rc;
+  if ((rc = check_ws(workspace, workspace_bytes, hmoe_ffn_train_workspace_bytes(shape)))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Carve cs{static_cast<char*>(saved)};
+  const TrainSaved sv = carve_saved(cs, s);
+  Carve cw{static_cast<char*>(workspace)};
+  const TrainWs w = carve_train_ws(cw, s);
+  const int64_t A = s.tokens * s.top_k;
+  HMOE_CUDA(cudaMemsetAsync(w.err, 0, sizeof(int), st), "reset error word");
+  HMOE_CUDA(run_router(s, x, w_router, router_bias, sv.topk_idx, sv.topk_w, nullptr, sv.logits,
+                       w.router_scratch, w.err, st),
+            "router_topk");
+  rc = run_dispatch(s, sv.topk_idx, sv.topk_w, 1, x, w.d, sv.pos, nullptr, nullptr, nullptr,
+                    sv.x_sorted, st);
+  if (rc) return rc;
+  HMOE_CUDA(cudaMemcpyAsync(sv.counts, w.d.counts, sizeof(int32_t) * s.experts,
+                            cudaMemcpyDeviceToDevice, st), "copy counts");
+  {
+    GroupedGemmArgs g;
+    g.a = sv.x_sorted;
+    g.b = w_gate_up;
+    g.counts = sv.counts;
+    g.out = sv.h;
+    g.M = A;
+    g.N = s.intermediate;
+    g.K = s.hidden;
+    g.G = s.experts;
+    g.swiglu = 1;
+    g.dtype = s.dtype;
+    g.err = w.err;
+    g.sm_limit = 0;
+    g.save_gate_up = sv.gate_up;
+    HMOE_CUDA(launch_grouped_gemm_pair(g, st), "grouped swiglu (training)");
+  }
+  rc = run_grouped(sv.h, w_down, sv.counts, A, s.hidden, s.intermediate, s.experts, s.dtype, 0,
+                   sv.expert_out, w.err, st);
+  if (rc) return rc;
+  HMOE_CUDA(launch_combine(sv.expert_out, sv.pos, sv.topk_w, 1, sv.topk_idx, s.experts, s.tokens,
+                           s.hidden, s.top_k, s.dtype, nullptr, y, st), "combine");
+  // aux statistics over the first aux_tokens tokens (none when negative)
+  const int64_t n_aux = aux_tokens < 0 ? 0 : aux_tokens;
+  const int nb = train_partial_blocks(s.tokens);
+  HMOE_CUDA(launch_aux_stats(sv.logits, sv.topk_idx, n_aux, s.experts, s.top_k, w.part_p,
+                             w.part_c, nb, aux_loss ? aux_loss : w.aux_tmp, sv.aux_counts, st),
+            "aux statistics");
+  if (expert_counts)
+    HMOE_CUDA(cudaMemcpyAsync(expert_counts, sv.aux_counts, sizeof(float) * s.experts,
+                              cudaMemcpyDeviceToDevice, st), "copy expert counts");
+  return HMOE_OK;
+}
+
+int hmoe_ffn_backward(const hmoe_shape* shape, const void* grad_y, const float* aux_grad,
+                      int64_t aux_tokens, const void* x, const void* w_router,
+                      const void* router_bias, const void* w_gate_up, const void* w_down,
+                      const void* saved, size_t saved_bytes, void* grad_x, void* grad_w_router,
+                      void* grad_router_bias, void* grad_w_gate_up, void* grad_w_down,
+                      void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_train_shape(shape);
+  if (rc) return rc;
+  const hmoe_shape& s = *shape;
+  if (aux_tokens > s.tokens) return fail(HMOE_EINVAL, "aux_tokens exceeds tokens");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (s.tokens == 0) {
+    // no tokens: every parameter gradient is zero
+    const void* any = grad_w_gate_up ? grad_w_gate_up : grad_w_down ? grad_w_down : grad_w_router;
+    if (!any) return HMOE_OK;
+    if ((rc = select_device(any))) return rc;
+    const size_t E = s.experts, d = s.hidden, I = s.intermediate;
+    if (grad_w_router) HMOE_CUDA(cudaMemsetAsync(grad_w_router, 0, 2 * E * d, st), "zero grad");
+    if (grad_router_bias) HMOE_CUDA(cudaMemsetAsync(grad_router_bias, 0, 2 * E, st), "zero grad");
+    if (grad_w_gate_up) HMOE_CUDA(cudaMemsetAsync(grad_w_gate_up, 0, 2 * E * 2 * I * d, st), "zero grad");
+    if (grad_w_down) HMOE_CUDA(cudaMemsetAsync(grad_w_down, 0, 2 * E * d * I, st), "zero grad");
+    return HMOE_OK;
+  }
+  if (!grad_y || !x || !w_router || !w_gate_up || !w_down || !saved)
+    return fail(HMOE_EINVAL, "grad_y, x, the weights and saved are required");
+  if (!aligned16(grad_y) || !aligned16(x) || !aligned16(w_router) || !aligned16(w_gate_up) ||
+      !aligned16(w_down) || (grad_x && !aligned16(grad_x)) ||
+      (grad_w_router && !aligned16(grad_w_router)) ||
+      (grad_w_gate_up && !aligned16(grad_w_gate_up)) || (grad_w_down && !aligned16(grad_w_down)))
+    return fail(HMOE_EINVAL, "tensors must be 16-byte aligned");
+  if (grad_router_bias && !router_bias)
+    return fail(HMOE_EINVAL, "grad_router_bias needs the layer's router_bias");
+  if ((rc = select_device(grad_y))) return rc;
+  if ((rc = check_ws(const_cast<void*>(saved), saved_bytes, hmoe_ffn_train_saved_bytes(shape))))
+    return rc;
+  if ((rc = check_ws(workspace, workspace_bytes, hmoe_ffn_train_workspace_bytes(shape)))) return rc;
+  Carve cs{static_cast<char*>(const_cast<void*>(saved))};
+  const TrainSaved sv = carve_saved(cs, s);
+  Carve cw{static_cast<char*>(workspace)};
+  const TrainWs w = carve_train_ws(cw, s);
+  const int64_t A = s.tokens * s.top_k;
+  const int E = s.experts, d = s.hidden, I = s.intermediate;
+  HMOE_CUDA(cudaMemsetAsync(w.err, 0, sizeof(int), st), "reset error word");
+  // 1. combine and router backward: d_expert_out rows, d_logits
+  HMOE_CUDA(launch_combine_router_bwd(grad_y, sv.expert_out, sv.pos, sv.topk_idx, sv.topk_w,
+                                      sv.logits, s.tokens, d, s.top_k, E, s.norm_topk_prob,
+                                      aux_grad, sv.aux_counts, aux_tokens < 0 ? 0 : aux_tokens,
+                                      w.d_eo, w.d_logits, w.count_T, st),
+            "combine/router backward");
+  // 2. down projection dgrad fused with the SiLU(gate) * up backward -> d_gate_up
+  {
+    GroupedDgradArgs a;
+    a.grad_out = w.d_eo;
+    a.weight = w_down;  // [E, d, I]: contraction over d
+    a.counts = sv.counts;
+    a.out = nullptr;
+    a.gate_up = sv.gate_up;
+    a.d_gate_up = w.d_gu;
+    a.M = A;
+    a.Kc = d;
+    a.Nout = I;
+    a.G = E;
+    a.err = w.err;
+    a.sm_limit = 0;
+    HMOE_CUDA(launch_grouped_dgrad(a, st), "down dgrad + SwiGLU backward");
+  }
+  // 3. down projection wgrad: d_w_down[e] = d_eo[e]^T @ h[e]
+  if (grad_w_down) {
+    GroupedWgradArgs a;
+    a.grad_out = w.d_eo;
+    a.input = sv.h;
+    a.counts = sv.counts;
+    a.out = grad_w_down;
+    a.M = A;
+    a.Mw = d;
+    a.Nw = I;
+    a.G = E;
+    a.err = w.err;
+    a.sm_limit = 0;
+    HMOE_CUDA(launch_grouped_wgrad(a, st), "down wgrad");
+  }
+  // 4. gate_up dgrad: d_x_sorted = d_gate_up @ w_gate_up[e] (into d_eo's buffer)
+  void* d_xs = w.d_eo;
+  if (grad_x) {
+    GroupedDgradArgs a;
+    a.grad_out = w.d_gu;
+    a.weight = w_gate_up;  // [E, 2I, d]: contraction over 2I
+    a.counts = sv.counts;
+    a.out = d_xs;
+    a.M = A;
+    a.Kc = 2 * I;
+    a.Nout = d;
+    a.G = E;
+    a.err = w.err;
+    a.sm_limit = 0;
+    HMOE_CUDA(launch_grouped_dgrad(a, st), "gate_up dgrad");
+  }
+  // 5. gate_up wgrad: d_w_gate_up[e] = d_gate_up[e]^T @ x_sorted[e]
+  if (grad_w_gate_up) {
+    GroupedWgradArgs a;
+    a.grad_out = w.d_gu;
+    a.input = sv.x_sorted;
+    a.counts = sv.counts;
+    a.out = grad_w_gate_up;
+    a.M = A;
+    a.Mw = 2 * I;
+    a.Nw = d;
+    a.G = E;
+    a.err = w.err;
+    a.sm_limit = 0;
+    HMOE_CUDA(launch_grouped_wgrad(a, st), "gate_up wgrad");
+  }
+  // 6. router: dx_router = d_logits @ w_router, d_w_router = d_logits^T @ x, d_bias
+  if (grad_x) {
+    GroupedDgradArgs a;
+    a.grad_out = w.d_logits;
+    a.weight = w_router;  // [1, E, d]
+    a.counts = w.count_T;
+    a.out = w.dx_router;
+    a.M = s.tokens;
+    a.Kc = E;
+    a.Nout = d;
+    a.G = 1;
+    a.err = w.err;
+    a.sm_limit = 0;
+    HMOE_CUDA(launch_grouped_dgrad(a, st), "router dgrad");
+    HMOE_CUDA(launch_dx(d_xs, sv.pos, w.dx_router, s.tokens, d, s.top_k, grad_x, st), "dx");
+  }
+  if (grad_w_router) {
+    GroupedWgradArgs a;
+    a.grad_out = w.d_logits;
+    a.input = x;
+    a.counts = w.count_T;
+    a.out = grad_w_router;
+    a.M = s.tokens;
+    a.Mw = E;
+    a.Nw = d;
+    a.G = 1;
+    a.err = w.err;
+    a.sm_limit = 0;
+    HMOE_CUDA(launch_grouped_wgrad(a, st), "router wgrad");
+  }
+  if (grad_router_bias)
+    HMOE_CUDA(launch_colsum_bf16(w.d_logits, s.tokens, E, w.part_p,
+                                 train_partial_blocks(s.tokens), grad_router_bias, st),
+              "router bias grad");
   return HMOE_OK;
 }
 

@@ -80,6 +80,7 @@ struct PParams {
   int b_rows_per_group;
   int b_second_off;
   uint16_t* out;
+  uint16_t* save_gu;  // SAVE: the rounded gate and up values, [M, 2N] (training forward)
   int* err;
   unsigned long long wait_limit_ns;
 };
@@ -191,7 +192,11 @@ __device__ __forceinline__ void pair_pack(const uint32_t (&a)[32], const uint32_
   }
 }
 
-template <bool SWIGLU>
+// SAVE (SwiGLU only): the epilogue also stores the bf16 gate and up values
+// it rounded, [rows, 2N] with gate at columns [0, N) and up at [N, 2N) -- the
+// gate_up tensor the reference materialises (layers.py:326-328), which the
+// backward of SiLU(gate) * up needs.
+template <bool SWIGLU, bool SAVE = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<SWIGLU>(), 1)
 grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA,
                          const __grid_constant__ CUtensorMap tmB,
@@ -386,6 +391,25 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA,
             tmem_ld_32cols(trow + PBN + c * 32, ua);
             tc_wait_ld();
             pair_pack<true>(ra, ua, packed);
+            if (SAVE && row_ok) {
+              const int gcol = n * p.out_cols_per_tile + c * 32;
+              uint16_t* srow = p.save_gu + grow * 2 * p.N;
+#pragma unroll
+              for (int c4 = 0; c4 < 4; ++c4) {
+                if (gcol + c4 * 8 + 8 > p.N) continue;
+                uint4 gv, uv;
+                gv.x = cvt_bf16x2(__uint_as_float(ra[8 * c4 + 0]), __uint_as_float(ra[8 * c4 + 1]));
+                gv.y = cvt_bf16x2(__uint_as_float(ra[8 * c4 + 2]), __uint_as_float(ra[8 * c4 + 3]));
+                gv.z = cvt_bf16x2(__uint_as_float(ra[8 * c4 + 4]), __uint_as_float(ra[8 * c4 + 5]));
+                gv.w = cvt_bf16x2(__uint_as_float(ra[8 * c4 + 6]), __uint_as_float(ra[8 * c4 + 7]));
+                uv.x = cvt_bf16x2(__uint_as_float(ua[8 * c4 + 0]), __uint_as_float(ua[8 * c4 + 1]));
+                uv.y = cvt_bf16x2(__uint_as_float(ua[8 * c4 + 2]), __uint_as_float(ua[8 * c4 + 3]));
+                uv.z = cvt_bf16x2(__uint_as_float(ua[8 * c4 + 4]), __uint_as_float(ua[8 * c4 + 5]));
+                uv.w = cvt_bf16x2(__uint_as_float(ua[8 * c4 + 6]), __uint_as_float(ua[8 * c4 + 7]));
+                *reinterpret_cast<uint4*>(srow + gcol + c4 * 8) = gv;
+                *reinterpret_cast<uint4*>(srow + p.N + gcol + c4 * 8) = uv;
+              }
+            }
           } else {
             tc_wait_ld();
             pair_pack<false>(ra, ra, packed);
@@ -473,7 +497,7 @@ bool make_map_p(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <bool SWIGLU>
+template <bool SWIGLU, bool SAVE = false>
 cudaError_t ensure_pair_attr() {
   static int done[64] = {0};
   static std::mutex mu;
@@ -483,7 +507,7 @@ cudaError_t ensure_pair_attr() {
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   std::lock_guard<std::mutex> lock(mu);
   if (!done[dev]) {
-    e = cudaFuncSetAttribute(grouped_gemm_pair_kernel<SWIGLU>,
+    e = cudaFuncSetAttribute(grouped_gemm_pair_kernel<SWIGLU, SAVE>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(kPSmemBytes));
     if (e != cudaSuccess) return e;
@@ -520,6 +544,7 @@ cudaError_t launch_grouped_gemm_pair(const GroupedGemmArgs& a, cudaStream_t stre
   p.b_rows_per_group = nw;
   p.b_second_off = a.swiglu ? a.N : PBN;
   p.out = static_cast<uint16_t*>(a.out);
+  p.save_gu = static_cast<uint16_t*>(a.save_gate_up);
   p.err = a.err;
   p.wait_limit_ns = kWaitLimitNs;
   const int sms = a.sm_limit > 0 ? a.sm_limit : num_sms_for_current_device();
@@ -527,7 +552,11 @@ cudaError_t launch_grouped_gemm_pair(const GroupedGemmArgs& a, cudaStream_t stre
   int pairs = static_cast<int>(max_tiles < sms / 2 ? max_tiles : sms / 2);
   if (pairs < 1) pairs = 1;
   cudaError_t e;
-  if (a.swiglu) {
+  if (a.swiglu && a.save_gate_up) {
+    if ((e = ensure_pair_attr<true, true>()) != cudaSuccess) return e;
+    grouped_gemm_pair_kernel<true, true><<<2 * pairs, pair_threads<true>(), kPSmemBytes, stream>>>(
+        ma, mb, mc, p);
+  } else if (a.swiglu) {
     if ((e = ensure_pair_attr<true>()) != cudaSuccess) return e;
     grouped_gemm_pair_kernel<true><<<2 * pairs, pair_threads<true>(), kPSmemBytes, stream>>>(
         ma, mb, mc, p);

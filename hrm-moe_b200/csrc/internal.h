@@ -73,6 +73,9 @@ struct GroupedGemmArgs {
   int dtype;
   int* err;                  // device error word (may be null)
   int sm_limit;              // persistent CTAs (0 = all SMs)
+  // Training forward (CTA-pair SwiGLU kernel only): also store the rounded
+  // gate and up values, [M, 2N] (gate columns [0, N), up [N, 2N)).
+  void* save_gate_up = nullptr;
   // Expert-parallel return (plain bf16 GEMM only; `out` unused): output row r
   // goes to scatter_base[src] + pos * N elements, where src and pos come from
   // scatter_src[r] = (src << kEpSrcShift) | pos; pos < scatter_cap.  Once every
@@ -111,6 +114,65 @@ cudaError_t launch_grouped_gemm_sm100(const GroupedGemmArgs& args, cudaStream_t 
 cudaError_t launch_grouped_gemm_simt(const GroupedGemmArgs& args, cudaStream_t stream);
 // bf16, local output only (no scatter / push): CTA pairs, 256-row tiles
 cudaError_t launch_grouped_gemm_pair(const GroupedGemmArgs& args, cudaStream_t stream);
+
+// gemm_sm100_bwd.cu (bf16, tcgen05): backward of the grouped linear ---------
+// dgrad: out[r, :] = grad_out[r, :Kc] @ weight[g] with weight [G][Kc][Nout]
+// (the grouped linear's own [G, N, K] weight, contracted over N).  With
+// gate_up set, the epilogue is the SiLU(gate) * up backward instead: the
+// product is d(h) for h [M, Nout = I], gate_up [M, 2I] holds the saved gate
+// and up values, and d_gate_up [M, 2I] receives their gradients.
+struct GroupedDgradArgs {
+  const void* grad_out;   // [M, Kc]
+  const void* weight;     // [G, Kc, Nout]
+  const int32_t* counts;  // [G]
+  void* out;              // [M, Nout] (plain)
+  const void* gate_up = nullptr;  // [M, 2 * Nout] (SwiGLU backward)
+  void* d_gate_up = nullptr;      // [M, 2 * Nout]
+  int64_t M;
+  int Kc;
+  int Nout;
+  int G;
+  int* err;
+  int sm_limit;
+};
+cudaError_t launch_grouped_dgrad(const GroupedDgradArgs& args, cudaStream_t stream);
+// wgrad: out[g] = grad_out[rows of g]^T @ input[rows of g], out [G, Mw, Nw].
+struct GroupedWgradArgs {
+  const void* grad_out;   // [M, Mw]
+  const void* input;      // [M, Nw]
+  const int32_t* counts;  // [G]
+  void* out;              // [G, Mw, Nw]
+  int64_t M;
+  int Mw;
+  int Nw;
+  int G;
+  int* err;
+  int sm_limit;
+};
+cudaError_t launch_grouped_wgrad(const GroupedWgradArgs& args, cudaStream_t stream);
+
+// train.cu (bf16): the backward's non-GEMM kernels and the aux statistics ----
+// Blocks of the deterministic partial sums below (partials: blocks * E).
+int train_partial_blocks(int64_t T);
+// Per token: d_expert_out rows (at pos), d_logits [T, E]; writes T to
+// *count_out (if set) for the router's single-group GEMMs.
+cudaError_t launch_combine_router_bwd(const void* grad_y, const void* expert_out,
+                                      const int32_t* pos, const int32_t* topk_idx,
+                                      const float* topk_w, const void* logits, int64_t T, int d,
+                                      int k, int E, int norm, const float* aux_grad,
+                                      const float* expert_counts, int64_t n_valid,
+                                      void* d_expert_out, void* d_logits, int32_t* count_out,
+                                      cudaStream_t stream);
+// dx[t] = bf16(dx_router[t] + bf16(sum over the token's rows of d_x_sorted)).
+cudaError_t launch_dx(const void* d_x_sorted, const int32_t* pos, const void* dx_router, int64_t T,
+                      int d, int k, void* dx, cudaStream_t stream);
+// aux loss and expert counts over the first n tokens (partials: nblocks * E each).
+cudaError_t launch_aux_stats(const void* logits, const int32_t* topk_idx, int64_t n, int E, int k,
+                             float* partial_p, int* partial_c, int nblocks, float* aux_out,
+                             float* counts_out, cudaStream_t stream);
+// out[e] = bf16(sum_t m[t, e]) for a bf16 [T, E] matrix.
+cudaError_t launch_colsum_bf16(const void* m, int64_t T, int E, float* partial, int nblocks,
+                               void* out, cudaStream_t stream);
 
 // ep_p2p.cu -------------------------------------------------------------
 size_t ep_symmetric_bytes(const ::hmoe_shape& s, int64_t max_tokens, int world);

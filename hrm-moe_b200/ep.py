@@ -343,9 +343,13 @@ class SparseMoEExpertParallelSwiGLU(torch.nn.Module):
         self._peer = None
 
     def forward(self, x, moe_context=None, total_seqlen=None, **_seq_info):
-        from .layers import _check_no_grad
+        from .layers import _needs_grad
         le = self.experts.local_experts
-        _check_no_grad(x, self.gate.weight, le.gate_up_weight, le.down_weight)
+        if _needs_grad(x, self.gate.weight, le.gate_up_weight, le.down_weight):
+            raise NotImplementedError(
+                "the expert-parallel layer runs the forward pass only (the backward of its "
+                "all-to-all exchange is not built); run it under torch.no_grad() or train with "
+                "SparseMoESwiGLU on each GPU")
         shape = x.shape
         h = x.reshape(-1, self.hidden_size)
         wr, wgu, wd = (self.gate.weight.to(h.dtype), le.gate_up_weight.to(h.dtype),

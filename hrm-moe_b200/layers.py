@@ -9,8 +9,14 @@ Weights copied from the reference's ``origin`` / ``grouped`` /
 ``grouped_triton`` layers (e.g. scripts/test_moe_shard_equivalence.py:23-37)
 load as they are.
 
-The backend is forward-only: calling it where autograd would need a
-backward raises instead of silently dropping gradients.
+Training works as in the reference: with autograd recording and any of x
+or the parameters requiring grad, ``SparseMoESwiGLU`` runs the training
+forward and its native backward (one autograd node for the layer), and with
+a ``moe_context`` it appends the aux load-balancing loss and the expert
+counts under the reference's keys (models/layers.py:619-632).
+``SparseMoEGroupedExperts`` under autograd composes the reference's own
+expert steps (layers.py:311-334) around the differentiable grouped GEMM.
+Training is bf16 only, as the reference's Triton backend.
 """
 from __future__ import annotations
 
@@ -57,11 +63,15 @@ class LinearInit(nn.Module):
         return nn.functional.linear(input, self.weight, self.bias)
 
 
-def _check_no_grad(*tensors: Optional[Tensor]) -> None:
-    if torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in tensors):
-        raise NotImplementedError(
-            "the grouped_b200 MoE backend implements the forward pass only; run it under "
-            "torch.no_grad() / torch.inference_mode() or detach the parameters")
+def _needs_grad(*tensors: Optional[Tensor]) -> bool:
+    return torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in tensors)
+
+
+def _valid_tokens(total_seqlen, tokens: int) -> int:
+    """int(unwrap_tensor(total_seqlen).item()) (models/layers.py:622), at most tokens."""
+    v = getattr(total_seqlen, "value", total_seqlen)  # a WrappedTensor holds .value
+    v = int(v.item()) if hasattr(v, "item") else int(v)
+    return max(0, min(v, tokens))
 
 
 class SparseMoEGroupedExperts(nn.Module):
@@ -88,11 +98,32 @@ class SparseMoEGroupedExperts(nn.Module):
         """Adds the experts' weighted outputs into final_hidden_states (in place)."""
         if hidden_states.shape[0] == 0:
             return final_hidden_states
-        _check_no_grad(hidden_states, routing_weights, self.gate_up_weight, self.down_weight)
         dt = hidden_states.dtype
+        w_gate_up, w_down = self.gate_up_weight.to(dt), self.down_weight.to(dt)
+        if _needs_grad(hidden_states, routing_weights, w_gate_up, w_down, final_hidden_states):
+            return self._forward_autograd(hidden_states, selected_experts, routing_weights,
+                                          final_hidden_states, w_gate_up, w_down)
         return ops.experts_forward(hidden_states, selected_experts, routing_weights,
-                                   final_hidden_states, self.gate_up_weight.to(dt),
-                                   self.down_weight.to(dt))
+                                   final_hidden_states, w_gate_up, w_down)
+
+    def _forward_autograd(self, hidden_states, selected_experts, routing_weights,
+                          final_hidden_states, w_gate_up, w_down):
+        """The reference's expert steps (layers.py:311-334) with the native
+        dispatch (integer work, no gradient) and the differentiable grouped
+        GEMM; the gathers, SiLU * up, weighting and index_add_ are the same
+        torch ops the reference uses, so autograd differentiates them alike."""
+        k = selected_experts.shape[-1]
+        r = ops.dispatch(selected_experts.reshape(-1, k).to(torch.int32), self.num_experts)
+        sort_idx, sorted_token = r["sort_idx"].long(), r["sorted_token"].long()
+        sorted_weights = routing_weights.reshape(-1).index_select(0, sort_idx)
+        sorted_hidden = hidden_states.index_select(0, sorted_token)
+        gate_up = ops.grouped_linear(sorted_hidden, w_gate_up, r["counts"])
+        gate, up = gate_up.chunk(2, dim=-1)
+        activated = nn.functional.silu(gate) * up
+        expert_output = ops.grouped_linear(activated, w_down, r["counts"])
+        expert_output = expert_output * sorted_weights[:, None]
+        final_hidden_states.index_add_(0, sorted_token, expert_output.to(hidden_states.dtype))
+        return final_hidden_states
 
 
 class SparseMoESwiGLU(nn.Module):
@@ -131,17 +162,30 @@ class SparseMoESwiGLU(nn.Module):
                 total_seqlen: Optional[Tensor] = None, **_seq_info) -> Tensor:
         original_shape = x.shape
         hidden_states = x.reshape(-1, self.hidden_size)
-        _check_no_grad(x, self.gate.weight, self.gate.bias, self.experts.gate_up_weight,
-                       self.experts.down_weight)
-        want_counts = moe_context is not None
-        res = ops.ffn_forward(
-            hidden_states, self.gate.weight, self.experts.gate_up_weight,
-            self.experts.down_weight, self.top_k, self.norm_topk_prob,
-            router_bias=self.gate.bias, return_routing=want_counts)
-        y, routing = res if want_counts else (res, None)
-        if routing is not None:
-            # the reference records aux losses only when gradients flow
-            # (layers.py:619); without them it keeps nothing, and the expert
-            # counts are exposed here for monitoring
-            moe_context.setdefault("expert_counts_b200", []).append(routing["counts"].float())
+        dt = hidden_states.dtype
+        w_router, bias = self.gate.weight, self.gate.bias
+        w_gate_up = self.experts.gate_up_weight.to(dt)
+        w_down = self.experts.down_weight.to(dt)
+        # the reference records the aux loss and the expert counts only while
+        # autograd records (layers.py:619)
+        want_aux = moe_context is not None and torch.is_grad_enabled()
+        if want_aux or _needs_grad(x, w_router, bias, w_gate_up, w_down):
+            T = hidden_states.shape[0]
+            aux_tokens = -1
+            if want_aux:
+                aux_tokens = T if total_seqlen is None else _valid_tokens(total_seqlen, T)
+            if T == 0:
+                y = hidden_states * 0
+                aux = torch.zeros((), dtype=torch.float32, device=x.device)
+                counts = torch.zeros(self.num_experts, dtype=torch.float32, device=x.device)
+            else:
+                y, aux, counts = ops.ffn_forward_autograd(
+                    hidden_states, w_router, w_gate_up, w_down, self.top_k, self.norm_topk_prob,
+                    router_bias=bias, aux_tokens=aux_tokens)
+            if want_aux:
+                moe_context.setdefault("aux_losses", []).append(aux)
+                moe_context.setdefault("expert_counts", []).append(counts)
+            return y.reshape(original_shape)
+        y = ops.ffn_forward(hidden_states, w_router, w_gate_up, w_down, self.top_k,
+                            self.norm_topk_prob, router_bias=bias)
         return y.reshape(original_shape)

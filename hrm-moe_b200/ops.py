@@ -164,13 +164,98 @@ def _grouped(input: torch.Tensor, weight: torch.Tensor, tokens_per_expert: torch
     return out
 
 
+def grouped_linear_backward(grad_out: torch.Tensor, input: torch.Tensor, weight: torch.Tensor,
+                            tokens_per_expert: torch.Tensor, need_input: bool = True,
+                            need_weight: bool = True):
+    """_TritonGroupedLinear.backward (models/moe_triton_grouped_gemm.py:427-456).
+
+    grad_out [M, N], input [M, K], weight [G, N, K] -> (grad_input [M, K] or
+    None, grad_weight [G, N, K] or None), bf16 on the tensor cores (the
+    reference's Triton backward raises TypeError for other dtypes).
+    """
+    dev = _require_cuda(grad_out, input, weight, tokens_per_expert)
+    M, K = input.shape
+    G, N, WK = weight.shape
+    if WK != K or tuple(grad_out.shape) != (M, N):
+        raise ValueError(f"grouped GEMM backward shapes: grad_out {tuple(grad_out.shape)}, "
+                         f"input {tuple(input.shape)}, weight {tuple(weight.shape)}")
+    if tokens_per_expert.numel() != G:
+        raise ValueError(f"tokens_per_expert has {tokens_per_expert.numel()} entries, weight has {G} groups")
+    if not (grad_out.dtype == input.dtype == weight.dtype == torch.bfloat16):
+        raise TypeError(f"grouped GEMM backward supports bf16 only, got {grad_out.dtype}, "
+                        f"{input.dtype}, {weight.dtype}")
+    grad_out, input, weight = grad_out.contiguous(), input.contiguous(), weight.contiguous()
+    tpe = tokens_per_expert.to(device=dev, dtype=torch.int32).contiguous()
+    gi = torch.empty((M, K), dtype=input.dtype, device=dev) if need_input else None
+    gw = torch.empty((G, N, K), dtype=weight.dtype, device=dev) if need_weight else None
+    if gi is None and gw is None:
+        return None, None
+    lib = _lib.load()
+    ws = _workspace(lib.hmoe_grouped_linear_workspace_bytes(G), dev)
+    _lib.check(lib.hmoe_grouped_linear_backward(
+        _ptr(grad_out), _ptr(input), _ptr(weight), _ptr(tpe), M, N, K, G, _lib.DTYPE_BF16,
+        _ptr(gi), _ptr(gw), _ptr(ws), ws.numel(), _stream(dev)))
+    return gi, gw
+
+
+def grouped_swiglu_backward(grad_out: torch.Tensor, w_down: torch.Tensor, gate_up: torch.Tensor,
+                            tokens_per_expert: torch.Tensor) -> torch.Tensor:
+    """Backward through the down projection and SiLU(gate) * up
+    (models/layers.py:327-331) in one GEMM: grad_out [M, d] = d(expert
+    output), w_down [G, d, I], gate_up [M, 2I] saved by the forward ->
+    d_gate_up [M, 2I].  bf16 only."""
+    dev = _require_cuda(grad_out, w_down, gate_up, tokens_per_expert)
+    M, d = grad_out.shape
+    G, wd, I = w_down.shape
+    if wd != d or tuple(gate_up.shape) != (M, 2 * I):
+        raise ValueError(f"swiglu backward shapes: grad_out {tuple(grad_out.shape)}, "
+                         f"w_down {tuple(w_down.shape)}, gate_up {tuple(gate_up.shape)}")
+    if not (grad_out.dtype == w_down.dtype == gate_up.dtype == torch.bfloat16):
+        raise TypeError("swiglu backward supports bf16 only")
+    grad_out, w_down, gate_up = grad_out.contiguous(), w_down.contiguous(), gate_up.contiguous()
+    tpe = tokens_per_expert.to(device=dev, dtype=torch.int32).contiguous()
+    out = torch.empty((M, 2 * I), dtype=grad_out.dtype, device=dev)
+    if M == 0:
+        return out
+    lib = _lib.load()
+    ws = _workspace(lib.hmoe_grouped_linear_workspace_bytes(G), dev)
+    _lib.check(lib.hmoe_grouped_swiglu_backward(
+        _ptr(grad_out), _ptr(w_down), _ptr(gate_up), _ptr(tpe), M, d, I, G, _ptr(out), _ptr(ws),
+        ws.numel(), _stream(dev)))
+    return out
+
+
+class _GroupedLinearFn(torch.autograd.Function):
+    """Autograd wrapper of the grouped linear, as _TritonGroupedLinear
+    (models/moe_triton_grouped_gemm.py:420-456): saves input and weight,
+    backward runs the dgrad and wgrad grouped GEMMs."""
+
+    @staticmethod
+    def forward(ctx, input, weight, tokens_per_expert):
+        out = _grouped(input, weight, tokens_per_expert, swiglu=False)
+        ctx.save_for_backward(input, weight, tokens_per_expert)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        input, weight, tpe = ctx.saved_tensors
+        gi, gw = grouped_linear_backward(grad_out.to(input.dtype), input, weight, tpe,
+                                         ctx.needs_input_grad[0], ctx.needs_input_grad[1])
+        return gi, gw, None
+
+
 def grouped_linear(input: torch.Tensor, weight: torch.Tensor,
                    tokens_per_expert: torch.Tensor) -> torch.Tensor:
     """triton_grouped_linear (models/moe_triton_grouped_gemm.py:478-485).
 
     input [M, K], weight [G, N, K], tokens_per_expert [G] (rows per group,
-    contiguous in order) -> [M, N].  Forward only.
+    contiguous in order) -> [M, N].  Differentiable for bf16 (the backward
+    of _TritonGroupedLinear, :420-456): with autograd recording and input or
+    weight requiring grad, the backward runs grouped_linear_backward.
     """
+    if (torch.is_grad_enabled() and input.shape[0] > 0
+            and (input.requires_grad or weight.requires_grad)):
+        return _GroupedLinearFn.apply(input, weight, tokens_per_expert)
     return _grouped(input, weight, tokens_per_expert, swiglu=False)
 
 
@@ -327,6 +412,135 @@ def ffn_forward(x: torch.Tensor, w_router: torch.Tensor, w_gate_up: torch.Tensor
         _ptr(out), 1 if accumulate else 0, _ptr(r.get("topk_idx")), _ptr(r.get("topk_weight")),
         _ptr(r.get("counts")), _ptr(r.get("sort_idx")), _ptr(ws), ws.numel(), _stream(dev)))
     return (out, routing) if return_routing else out
+
+
+# ---------------------------------------------------------------- training --
+def _train_shape(x, w_router, w_gate_up, w_down, top_k, norm_topk_prob):
+    T, d = x.shape
+    E = w_router.shape[0]
+    I = w_gate_up.shape[1] // 2
+    if tuple(w_gate_up.shape) != (E, 2 * I, d) or tuple(w_down.shape) != (E, d, I):
+        raise ValueError(f"expert weights {tuple(w_gate_up.shape)} / {tuple(w_down.shape)} do not "
+                         f"match hidden size {d} and {E} experts")
+    if x.dtype != torch.bfloat16:
+        # the reference's Triton backend has no other training dtype
+        # (models/moe_triton_grouped_gemm.py:350-355)
+        raise TypeError(f"the B200 MoE training path supports bf16 only, got {x.dtype}")
+    return _lib.HmoeShape(T, d, E, I, top_k, _lib.DTYPE_BF16, 1 if norm_topk_prob else 0)
+
+
+def ffn_forward_train(x: torch.Tensor, w_router: torch.Tensor, w_gate_up: torch.Tensor,
+                      w_down: torch.Tensor, top_k: int, norm_topk_prob: bool,
+                      router_bias: Optional[torch.Tensor] = None, aux_tokens: int = -1):
+    """The layer forward keeping what the backward needs (bf16).
+
+    Returns (y [T, d], saved (opaque uint8 buffer), aux_loss (fp32 scalar
+    tensor), expert_counts (fp32 [E])).  With ``aux_tokens`` >= 0 the aux
+    loss and counts are those of models/layers.py:619-632 over the first
+    ``aux_tokens`` tokens; otherwise they are zeros.
+    """
+    dev = _require_cuda(x, w_router, w_gate_up, w_down, router_bias)
+    shape = _train_shape(x, w_router, w_gate_up, w_down, top_k, norm_topk_prob)
+    T, d = x.shape
+    E = w_router.shape[0]
+    lib = _lib.load()
+    saved_bytes = lib.hmoe_ffn_train_saved_bytes(ctypes.byref(shape))
+    ws_bytes = lib.hmoe_ffn_train_workspace_bytes(ctypes.byref(shape))
+    if saved_bytes == 0 or ws_bytes == 0:
+        raise ValueError(_lib.last_error())
+    saved = _workspace(saved_bytes, dev)
+    ws = _workspace(ws_bytes, dev)
+    y = torch.empty((T, d), dtype=x.dtype, device=dev)
+    aux = torch.zeros((), dtype=torch.float32, device=dev)
+    counts = torch.zeros(E, dtype=torch.float32, device=dev)
+    x, w_router = x.contiguous(), w_router.contiguous()
+    w_gate_up, w_down = w_gate_up.contiguous(), w_down.contiguous()
+    bias = None if router_bias is None else router_bias.to(x.dtype).contiguous()
+    _lib.check(lib.hmoe_ffn_forward_train(
+        ctypes.byref(shape), _ptr(x), _ptr(w_router), _ptr(bias), _ptr(w_gate_up), _ptr(w_down),
+        _ptr(y), int(aux_tokens), _ptr(aux), _ptr(counts), _ptr(saved), saved.numel(), _ptr(ws),
+        ws.numel(), _stream(dev)))
+    return y, saved, aux, counts
+
+
+def ffn_backward(grad_y: torch.Tensor, saved: torch.Tensor, x: torch.Tensor,
+                 w_router: torch.Tensor, w_gate_up: torch.Tensor, w_down: torch.Tensor,
+                 top_k: int, norm_topk_prob: bool, router_bias: Optional[torch.Tensor] = None,
+                 aux_grad: Optional[torch.Tensor] = None, aux_tokens: int = -1,
+                 needs=(True, True, True, True, True)):
+    """Gradients of the layer (models/layers.py:596-634, with the aux loss of
+    :619-632 when ``aux_grad`` is given) from a :func:`ffn_forward_train`.
+
+    ``needs`` selects (x, w_router, router_bias, w_gate_up, w_down).  Returns
+    the five gradients (None where not needed or not applicable), bf16.
+    """
+    dev = _require_cuda(grad_y, saved, x, w_router, w_gate_up, w_down, router_bias, aux_grad)
+    shape = _train_shape(x, w_router, w_gate_up, w_down, top_k, norm_topk_prob)
+    T, d = x.shape
+    E, I = w_router.shape[0], w_gate_up.shape[1] // 2
+
+    def make(n, *sz):
+        return torch.empty(sz, dtype=torch.bfloat16, device=dev) if n else None
+
+    gx = make(needs[0], T, d)
+    gwr = make(needs[1], E, d)
+    gb = make(needs[2] and router_bias is not None, E)
+    gwgu = make(needs[3], E, 2 * I, d)
+    gwd = make(needs[4], E, d, I)
+    lib = _lib.load()
+    ws = _workspace(lib.hmoe_ffn_train_workspace_bytes(ctypes.byref(shape)), dev)
+    grad_y = grad_y.to(torch.bfloat16).contiguous()
+    ag = None if aux_grad is None else aux_grad.to(torch.float32).reshape(()).contiguous()
+    bias = None if router_bias is None else router_bias.to(x.dtype).contiguous()
+    _lib.check(lib.hmoe_ffn_backward(
+        ctypes.byref(shape), _ptr(grad_y), _ptr(ag), int(aux_tokens), _ptr(x.contiguous()),
+        _ptr(w_router.contiguous()), _ptr(bias), _ptr(w_gate_up.contiguous()),
+        _ptr(w_down.contiguous()), _ptr(saved), saved.numel(), _ptr(gx), _ptr(gwr), _ptr(gb),
+        _ptr(gwgu), _ptr(gwd), _ptr(ws), ws.numel(), _stream(dev)))
+    return gx, gwr, gb, gwgu, gwd
+
+
+class _FfnFunction(torch.autograd.Function):
+    """SparseMoESwiGLU's forward and backward as one autograd node: the
+    training forward keeps its activations in one buffer, and the backward
+    runs the native backward kernels.  Outputs (y, aux_loss, expert_counts);
+    expert_counts is not differentiable (the reference computes it under
+    no_grad, models/layers.py:630-631)."""
+
+    @staticmethod
+    def forward(ctx, x, w_router, router_bias, w_gate_up, w_down, top_k, norm_topk_prob,
+                aux_tokens):
+        y, saved, aux, counts = ffn_forward_train(x, w_router, w_gate_up, w_down, top_k,
+                                                  norm_topk_prob, router_bias, aux_tokens)
+        ctx.save_for_backward(x, w_router, router_bias, w_gate_up, w_down, saved)
+        ctx.cfg = (top_k, norm_topk_prob, aux_tokens)
+        ctx.mark_non_differentiable(counts)
+        return y, aux, counts
+
+    @staticmethod
+    def backward(ctx, grad_y, grad_aux, _grad_counts):
+        x, w_router, router_bias, w_gate_up, w_down, saved = ctx.saved_tensors
+        top_k, norm, aux_tokens = ctx.cfg
+        n = ctx.needs_input_grad
+        if grad_y is None:
+            grad_y = torch.zeros_like(x)
+        gx, gwr, gb, gwgu, gwd = ffn_backward(
+            grad_y, saved, x, w_router, w_gate_up, w_down, top_k, norm, router_bias,
+            aux_grad=grad_aux if aux_tokens >= 0 else None, aux_tokens=aux_tokens,
+            needs=(n[0], n[1], n[2], n[3], n[4]))
+        return gx, gwr, gb, gwgu, gwd, None, None, None
+
+
+def ffn_forward_autograd(x: torch.Tensor, w_router: torch.Tensor, w_gate_up: torch.Tensor,
+                         w_down: torch.Tensor, top_k: int, norm_topk_prob: bool,
+                         router_bias: Optional[torch.Tensor] = None, aux_tokens: int = -1):
+    """Differentiable layer forward (bf16): (y, aux_loss, expert_counts).
+
+    Gradients flow to x, the router weight (and bias) and both expert
+    weights; aux_loss (when ``aux_tokens`` >= 0) is differentiable too.
+    """
+    return _FfnFunction.apply(x, w_router, router_bias, w_gate_up, w_down, int(top_k),
+                              bool(norm_topk_prob), int(aux_tokens))
 
 
 class CapturedFfn:

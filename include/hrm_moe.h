@@ -174,6 +174,43 @@ int hmoe_grouped_swiglu(const void* input, const void* w_gate_up,
                         void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Backward of hmoe_grouped_linear: _TritonGroupedLinear.backward
+ * (models/moe_triton_grouped_gemm.py:427-456), for output = input @ W[g]^T
+ * with weight [G, N, K] and grad_out [M, N]:
+ *   grad_input  [M, K]    = grad_out[rows of g] @ W[g]
+ *                           (_m_grouped_gemm(trans_b=False), :358-417, kernel :187-260)
+ *   grad_weight [G, N, K] = grad_out[rows of g]^T @ input[rows of g]
+ *                           (_k_grouped_gemm, :350-..., kernel :277-347)
+ * fp32 accumulation on the tcgen05 tensor cores, one rounding to bf16; a
+ * group without rows gets a zero weight gradient.  bf16 only: fp32 is
+ * refused with HMOE_EINVAL, as the reference's Triton path raises TypeError
+ * for it (:350-355).  Either output may be NULL (not computed).  K and N
+ * multiples of 8.  Workspace: hmoe_grouped_linear_workspace_bytes (the
+ * device error word).
+ */
+int hmoe_grouped_linear_backward(const void* grad_out, const void* input, const void* weight,
+                                 const int32_t* tokens_per_expert, int64_t M, int32_t N,
+                                 int32_t K, int32_t groups, int32_t dtype, void* grad_input,
+                                 void* grad_weight, void* workspace, size_t workspace_bytes,
+                                 void* stream);
+
+/*
+ * Backward through the down projection and SiLU(gate) * up
+ * (models/layers.py:327-331) in one GEMM: with h = silu(gate) * up and
+ * expert_out = h @ w_down[g]^T, given grad_out = d(expert_out) [M, d],
+ *   dh     = grad_out @ w_down[g]                    (rounded to bf16)
+ *   d_up   = dh * bf16(silu(gate)),  d_sg = dh * up  (each rounded)
+ *   d_gate = d_sg * s * (1 + gate * (1 - s)),  s = sigmoid(gate)
+ * written as d_gate_up [M, 2I] (gate half, then up half), from the saved
+ * gate_up [M, 2I] of the forward.  w_down [G, d, I].  bf16 only.
+ */
+int hmoe_grouped_swiglu_backward(const void* grad_out, const void* w_down,
+                                 const void* gate_up, const int32_t* tokens_per_expert,
+                                 int64_t M, int32_t d, int32_t I, int32_t groups,
+                                 void* d_gate_up, void* workspace, size_t workspace_bytes,
+                                 void* stream);
+
+/*
  * Grouped GEMM over groups that reuse weights: group g (group_rows[g] rows,
  * contiguous in order) is multiplied by weight[group_weight[g]] (of
  * num_weights).  swiglu = 0: output [M, N] = rows @ W^T with W [N, K];
@@ -269,6 +306,49 @@ int hmoe_ep_forward_marked(const hmoe_shape* shape, int64_t max_tokens, int32_t 
                            const void* w_gate_up_local, const void* w_down_local, void* y,
                            void* workspace, size_t workspace_bytes, void* stream,
                            void* const* phase_events);
+
+/*
+ * Training: the layer forward that keeps what its backward needs, and the
+ * backward of SparseMoESwiGLU.forward (models/layers.py:596-634) with the
+ * aux load-balancing loss (layers.py:163-170, 619-632): the gradients
+ * autograd computes through the reference with the grouped expert backend
+ * (the grouped GEMMs' backward is _TritonGroupedLinear.backward,
+ * models/moe_triton_grouped_gemm.py:420-456).  bf16 only, experts a
+ * multiple of 8.
+ *
+ * hmoe_ffn_forward_train computes y as hmoe_ffn_forward does (same kernels,
+ * same bits) and fills `saved` (hmoe_ffn_train_saved_bytes: router logits,
+ * routing, positions, counts, the gathered rows, the gate_up, SiLU*up and
+ * expert outputs) for hmoe_ffn_backward.  aux_tokens >= 0 also computes, over
+ * the first aux_tokens tokens (the reference's total_seqlen, layers.py:
+ * 620-626), the aux loss (aux_loss, device fp32 scalar, may be NULL) and the
+ * expert selection counts (expert_counts, device fp32 [E], may be NULL):
+ * the values the reference appends to moe_context.  Negative: no aux.
+ *
+ * hmoe_ffn_backward: given grad_y [T, d] and, when the aux loss was part of
+ * the loss, aux_grad (device fp32 scalar, its gradient; NULL = none) with the
+ * same aux_tokens, writes grad_x [T, d], grad_w_router [E, d],
+ * grad_router_bias [E] (only with a router_bias), grad_w_gate_up [E, 2I, d]
+ * and grad_w_down [E, d, I], each in bf16, each optional (NULL = not
+ * computed).  `saved` must come from the matching forward call, with the same
+ * inputs.  Workspace: hmoe_ffn_train_workspace_bytes (also the forward's).
+ * Rounding follows the reference's bf16 tensors: every GEMM accumulates in
+ * fp32 and rounds once; the SiLU and combine products are rounded as the
+ * reference rounds them; a token's d_x sums its rows' gradients in fp32.
+ */
+size_t hmoe_ffn_train_saved_bytes(const hmoe_shape* shape);
+size_t hmoe_ffn_train_workspace_bytes(const hmoe_shape* shape);
+int hmoe_ffn_forward_train(const hmoe_shape* shape, const void* x, const void* w_router,
+                           const void* router_bias, const void* w_gate_up, const void* w_down,
+                           void* y, int64_t aux_tokens, float* aux_loss, float* expert_counts,
+                           void* saved, size_t saved_bytes, void* workspace,
+                           size_t workspace_bytes, void* stream);
+int hmoe_ffn_backward(const hmoe_shape* shape, const void* grad_y, const float* aux_grad,
+                      int64_t aux_tokens, const void* x, const void* w_router,
+                      const void* router_bias, const void* w_gate_up, const void* w_down,
+                      const void* saved, size_t saved_bytes, void* grad_x, void* grad_w_router,
+                      void* grad_router_bias, void* grad_w_gate_up, void* grad_w_down,
+                      void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * Read (and synchronise the stream for) the error word kernels leave at the

@@ -151,8 +151,6 @@ def test_module_mirror_matches_ops():
     assert tuple(y.shape) == (4, 16, 256)
     o = O.moe_forward(inp.x, inp.w_router, inp.w_gate_up, inp.w_down, 4, True, "bf16")
     assert O.max_rel(to_np(y).reshape(64, 256), o["y"]) <= 1e-2
-    with pytest.raises(NotImplementedError):
-        mod(to_dev(inp.x, "bf16"))  # grad enabled and parameters require grad
 
 
 def test_combine_op_matches_reference_rounding():

@@ -40,11 +40,15 @@ def test_no_cpu_path():
         ops.dtype_code(torch.float16)
 
 
-def test_forward_refuses_autograd():
+def test_forward_has_no_cpu_path_for_training():
+    """With autograd recording the module runs the native training path; on
+    CPU tensors that fails loudly (there is no CPU fallback)."""
     layers = package().layers
     m = layers.SparseMoESwiGLU(16, 32, 8, 2, True)
-    with pytest.raises(NotImplementedError):
+    with pytest.raises(RuntimeError, match="CUDA"):
         m(torch.zeros((3, 16)))
+    with pytest.raises(RuntimeError, match="CUDA"):
+        m(torch.zeros((3, 16)), moe_context={})
 
 
 def test_reference_state_dict_loads(tmp_path):
