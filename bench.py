@@ -72,6 +72,10 @@ def parse_args():
                     help="target duration of the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-train", action="store_true",
+                    help="N=1: skip the training-step measurement (forward that keeps its "
+                         "activations + the full backward with the aux loss)")
+    ap.add_argument("--train-steps", type=int, default=50)
     ap.add_argument("--e2e-chunk", type=int, default=4096,
                     help="tokens per host-copy chunk of the end-to-end measurement")
     ap.add_argument("--no-graph", action="store_true",
@@ -419,6 +423,96 @@ def reference_gpu_arm(args, rank, world, local_rank):
     return 0
 
 
+# ------------------------------------------------------- training step --
+TRAIN_PHASES = ["forward_train", "combine_router_bwd", "down_dgrad_swiglu_bwd", "down_wgrad",
+                "gate_up_dgrad", "gate_up_wgrad", "router_dgrad_and_dx", "router_wgrad"]
+
+
+def measure_train_step(torch, lib, _lib, ops, shape, x, w_router, bias, w_gate_up, w_down, flush,
+                       stream, warmup, steps, peaks):
+    """One training step of the layer per iteration: the forward that keeps
+    its activations (with the aux loss over all tokens) and the whole
+    backward (grad of sum(y * g) + aux), each phase between CUDA events."""
+    T, d = x.shape
+    E, I, k = shape.experts, shape.intermediate, shape.top_k
+    dev = x.device
+    cs = ops.make_shape(T, d, E, I, k, torch.bfloat16, shape.norm_topk_prob)
+    saved = torch.empty(lib.hmoe_ffn_train_saved_bytes(ctypes.byref(cs)), dtype=torch.uint8,
+                        device=dev)
+    ws = torch.empty(lib.hmoe_ffn_train_workspace_bytes(ctypes.byref(cs)), dtype=torch.uint8,
+                     device=dev)
+    y = torch.empty_like(x)
+    gy = (torch.randn((T, d), generator=torch.Generator(device=dev).manual_seed(77), device=dev)
+          .to(torch.bfloat16))
+    aux = torch.zeros((), dtype=torch.float32, device=dev)
+    counts = torch.zeros(E, dtype=torch.float32, device=dev)
+    aux_grad = torch.ones((), dtype=torch.float32, device=dev)
+    gx, gwr = torch.empty_like(x), torch.empty_like(w_router)
+    gb = torch.empty_like(bias) if bias is not None else None
+    gwgu, gwd = torch.empty_like(w_gate_up), torch.empty_like(w_down)
+    p = lambda t: None if t is None else ctypes.c_void_p(t.data_ptr())
+    st = ctypes.c_void_p(stream.cuda_stream)
+
+    def events(n):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(n)]
+        for e in ev:
+            e.record(stream)
+        return ev
+
+    def step(ev):
+        ev[0].record(stream)
+        _lib.check(lib.hmoe_ffn_forward_train(
+            ctypes.byref(cs), p(x), p(w_router), p(bias), p(w_gate_up), p(w_down), p(y), T,
+            p(aux), p(counts), p(saved), saved.numel(), p(ws), ws.numel(), st))
+        arr = (ctypes.c_void_p * 8)(*[ctypes.c_void_p(e.cuda_event) for e in ev[1:]])
+        _lib.check(lib.hmoe_ffn_backward_marked(
+            ctypes.byref(cs), p(gy), p(aux_grad), T, p(x), p(w_router), p(bias), p(w_gate_up),
+            p(w_down), p(saved), saved.numel(), p(gx), p(gwr), p(gb), p(gwgu), p(gwd), p(ws),
+            ws.numel(), st, arr))
+
+    warm = events(9)
+    for _ in range(max(3, warmup)):
+        flush.zero_()
+        step(warm)
+    torch.cuda.synchronize()
+    ops.workspace_status(ws)
+    evs = [events(9) for _ in range(steps)]
+    torch.cuda.synchronize()
+    for i in range(steps):
+        flush.zero_()
+        step(evs[i])
+    torch.cuda.synchronize()
+    ops.workspace_status(ws)
+    ms = {n: statistics.mean(e[i].elapsed_time(e[i + 1]) for e in evs)
+          for i, n in enumerate(TRAIN_PHASES)}
+    total = statistics.mean(e[0].elapsed_time(e[8]) for e in evs)
+    A = T * k
+    gflop = {"down_dgrad_swiglu_bwd": 2.0 * A * d * I, "down_wgrad": 2.0 * A * d * I,
+             "gate_up_dgrad": 4.0 * A * d * I, "gate_up_wgrad": 4.0 * A * d * I,
+             "router_wgrad": 2.0 * T * E * d}
+    hbm = {"combine_router_bwd": T * d * 2 + 2 * A * d * 2 + 2 * T * E * 2 + A * 12,
+           "router_dgrad_and_dx": A * d * 2 + 2 * T * d * 2 + A * 4}
+    phases = {}
+    for n in TRAIN_PHASES:
+        sec = ms[n] * 1e-3
+        if n in gflop:
+            ach = gflop[n] / sec / 1e12
+            phases[n] = {"ms": ms[n], "bound": "tensor", "achieved": ach, "unit": "TFLOP/s",
+                         "frac": ach / peaks["bf16_tflops"]}
+        elif n in hbm:
+            ach = hbm[n] / sec / 1e9
+            phases[n] = {"ms": ms[n], "bound": "hbm", "achieved": ach, "unit": "GB/s",
+                         "frac": ach / peaks["hbm_gbs"]}
+        else:
+            phases[n] = {"ms": ms[n]}
+    flops = 3 * sum(shape.gemm_flops())  # forward + dgrad + wgrad of both expert GEMMs
+    return {"tokens_per_s": T / (total * 1e-3), "ms_per_step": total, "steps": steps,
+            "what": "forward that keeps activations (aux loss over all tokens) + backward of "
+                    "sum(y * grad_y) + aux: grads of x, router weight, both expert weights",
+            "expert_gemm_tflops": flops / (total * 1e-3) / 1e12, "phases": phases,
+            "gpu_launches_per_step": 18 if bias is None else 20}
+
+
 # ------------------------------------------------------------- B200 arm --
 def b200_arm(args, rank, world, local_rank):
     import torch
@@ -681,6 +775,10 @@ def b200_arm(args, rank, world, local_rank):
 
     # ------------------------------------------------------------ roofline
     peaks = measured_peaks()
+    train = None
+    if world == 1 and not args.no_train and shape.dtype == "bf16":
+        train = measure_train_step(torch, lib, _lib, ops, shape, x, w_router, bias, w_gate_up,
+                                   w_down, flush, stream, args.warmup, args.train_steps, peaks)
     A = T * k
     gu_flops, dn_flops = shape.gemm_flops()
     if ep is None:
@@ -800,6 +898,8 @@ def b200_arm(args, rank, world, local_rank):
     }
     if ep_parity is not None:
         line["ep_parity"] = ep_parity
+    if train is not None:
+        line["train"] = train
     print(json.dumps(line), flush=True)
     return 0
 

@@ -90,6 +90,10 @@ SIGNATURES = {
                                   c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p,
                                   c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t,
                                   c_void_p]),
+    "hmoe_ffn_backward_marked": (c_int, [ShapeP, c_void_p, c_void_p, c_int64, c_void_p, c_void_p,
+                                         c_void_p, c_void_p, c_void_p, c_void_p, c_size_t,
+                                         c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                         c_void_p, c_size_t, c_void_p, ctypes.POINTER(c_void_p)]),
     "hmoe_grouped_gemm_mapped": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int32,
                                          c_int32, c_int32, c_int32, c_int32, c_int32, c_void_p,
                                          c_void_p, c_size_t, c_void_p]),

@@ -952,6 +952,7 @@ struct TrainWs {
   void* d_eo;            // backward [A, d], later d_x_sorted
   void* d_gu;            // backward [A, 2I]
   void* dx_router;       // backward [T, d]
+  float* wr_partial;     // backward: split-K partials of the router wgrad [<= 64, E, d]
 };
 
 TrainWs carve_train_ws(Carve& c, const hmoe_shape& s) {
@@ -969,6 +970,7 @@ TrainWs carve_train_ws(Carve& c, const hmoe_shape& s) {
   b.d_eo = c.take<void>(2 * A * s.hidden);
   b.d_gu = c.take<void>(2 * A * 2 * s.intermediate);
   b.dx_router = c.take<void>(2 * s.tokens * s.hidden);
+  b.wr_partial = c.take<float>(sizeof(float) * 64 * s.experts * s.hidden);
   return b;
 }
 
@@ -1072,12 +1074,15 @@ int hmoe_ffn_forward_train(const hmoe_shape* shape, const void* x, const void* w
   return HMOE_OK;
 }
 
-int hmoe_ffn_backward(const hmoe_shape* shape, const void* grad_y, const float* aux_grad,
-                      int64_t aux_tokens, const void* x, const void* w_router,
-                      const void* router_bias, const void* w_gate_up, const void* w_down,
-                      const void* saved, size_t saved_bytes, void* grad_x, void* grad_w_router,
-                      void* grad_router_bias, void* grad_w_gate_up, void* grad_w_down,
-                      void* workspace, size_t workspace_bytes, void* stream) {
+int hmoe_ffn_backward_marked(const hmoe_shape* shape, const void* grad_y, const float* aux_grad,
+                             int64_t aux_tokens, const void* x, const void* w_router,
+                             const void* router_bias, const void* w_gate_up, const void* w_down,
+                             const void* saved, size_t saved_bytes, void* grad_x,
+                             void* grad_w_router, void* grad_router_bias, void* grad_w_gate_up,
+                             void* grad_w_down, void* workspace, size_t workspace_bytes,
+                             void* stream, void* const* phase_events) {
+  PhaseMarks pm;
+  pm.ev = phase_events;
   int rc = check_train_shape(shape);
   if (rc) return rc;
   const hmoe_shape& s = *shape;
@@ -1115,12 +1120,14 @@ int hmoe_ffn_backward(const hmoe_shape* shape, const void* grad_y, const float* 
   const int64_t A = s.tokens * s.top_k;
   const int E = s.experts, d = s.hidden, I = s.intermediate;
   HMOE_CUDA(cudaMemsetAsync(w.err, 0, sizeof(int), st), "reset error word");
+  if ((rc = pm.mark(0, st))) return rc;
   // 1. combine and router backward: d_expert_out rows, d_logits
   HMOE_CUDA(launch_combine_router_bwd(grad_y, sv.expert_out, sv.pos, sv.topk_idx, sv.topk_w,
                                       sv.logits, s.tokens, d, s.top_k, E, s.norm_topk_prob,
                                       aux_grad, sv.aux_counts, aux_tokens < 0 ? 0 : aux_tokens,
                                       w.d_eo, w.d_logits, w.count_T, st),
             "combine/router backward");
+  if ((rc = pm.mark(1, st))) return rc;
   // 2. down projection dgrad fused with the SiLU(gate) * up backward -> d_gate_up
   {
     GroupedDgradArgs a;
@@ -1138,6 +1145,7 @@ int hmoe_ffn_backward(const hmoe_shape* shape, const void* grad_y, const float* 
     a.sm_limit = 0;
     HMOE_CUDA(launch_grouped_dgrad(a, st), "down dgrad + SwiGLU backward");
   }
+  if ((rc = pm.mark(2, st))) return rc;
   // 3. down projection wgrad: d_w_down[e] = d_eo[e]^T @ h[e]
   if (grad_w_down) {
     GroupedWgradArgs a;
@@ -1153,6 +1161,7 @@ int hmoe_ffn_backward(const hmoe_shape* shape, const void* grad_y, const float* 
     a.sm_limit = 0;
     HMOE_CUDA(launch_grouped_wgrad(a, st), "down wgrad");
   }
+  if ((rc = pm.mark(3, st))) return rc;
   // 4. gate_up dgrad: d_x_sorted = d_gate_up @ w_gate_up[e] (into d_eo's buffer)
   void* d_xs = w.d_eo;
   if (grad_x) {
@@ -1169,6 +1178,7 @@ int hmoe_ffn_backward(const hmoe_shape* shape, const void* grad_y, const float* 
     a.sm_limit = 0;
     HMOE_CUDA(launch_grouped_dgrad(a, st), "gate_up dgrad");
   }
+  if ((rc = pm.mark(4, st))) return rc;
   // 5. gate_up wgrad: d_w_gate_up[e] = d_gate_up[e]^T @ x_sorted[e]
   if (grad_w_gate_up) {
     GroupedWgradArgs a;
@@ -1184,6 +1194,7 @@ int hmoe_ffn_backward(const hmoe_shape* shape, const void* grad_y, const float* 
     a.sm_limit = 0;
     HMOE_CUDA(launch_grouped_wgrad(a, st), "gate_up wgrad");
   }
+  if ((rc = pm.mark(5, st))) return rc;
   // 6. router: dx_router = d_logits @ w_router, d_w_router = d_logits^T @ x, d_bias
   if (grad_x) {
     GroupedDgradArgs a;
@@ -1200,6 +1211,7 @@ int hmoe_ffn_backward(const hmoe_shape* shape, const void* grad_y, const float* 
     HMOE_CUDA(launch_grouped_dgrad(a, st), "router dgrad");
     HMOE_CUDA(launch_dx(d_xs, sv.pos, w.dx_router, s.tokens, d, s.top_k, grad_x, st), "dx");
   }
+  if ((rc = pm.mark(6, st))) return rc;
   if (grad_w_router) {
     GroupedWgradArgs a;
     a.grad_out = w.d_logits;
@@ -1212,13 +1224,29 @@ int hmoe_ffn_backward(const hmoe_shape* shape, const void* grad_y, const float* 
     a.G = 1;
     a.err = w.err;
     a.sm_limit = 0;
+    // E x d is only a few output tiles: split the tokens (fp32 partials,
+    // summed in order, one rounding)
+    a.ksplit = wgrad_ksplit(s.tokens, E, d, 1);
+    a.partial = w.wr_partial;
     HMOE_CUDA(launch_grouped_wgrad(a, st), "router wgrad");
   }
   if (grad_router_bias)
     HMOE_CUDA(launch_colsum_bf16(w.d_logits, s.tokens, E, w.part_p,
                                  train_partial_blocks(s.tokens), grad_router_bias, st),
               "router bias grad");
-  return HMOE_OK;
+  return pm.mark(7, st);
+}
+
+int hmoe_ffn_backward(const hmoe_shape* shape, const void* grad_y, const float* aux_grad,
+                      int64_t aux_tokens, const void* x, const void* w_router,
+                      const void* router_bias, const void* w_gate_up, const void* w_down,
+                      const void* saved, size_t saved_bytes, void* grad_x, void* grad_w_router,
+                      void* grad_router_bias, void* grad_w_gate_up, void* grad_w_down,
+                      void* workspace, size_t workspace_bytes, void* stream) {
+  return hmoe_ffn_backward_marked(shape, grad_y, aux_grad, aux_tokens, x, w_router, router_bias,
+                                  w_gate_up, w_down, saved, saved_bytes, grad_x, grad_w_router,
+                                  grad_router_bias, grad_w_gate_up, grad_w_down, workspace,
+                                  workspace_bytes, stream, nullptr);
 }
 
 int hmoe_workspace_status(const void* workspace, void* stream) {

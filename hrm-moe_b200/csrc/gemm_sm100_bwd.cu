@@ -57,7 +57,9 @@ constexpr int kQAcc = 2;
 constexpr int kQTmemCols = QN * kQAcc;          // all 512 columns
 constexpr int kQMaxGroups = 1024;
 constexpr int kQEpiChunk = 32 * 32 * 2;
-constexpr int kQEpiBytes = 4 * 2 * kQEpiChunk;  // plain epilogue: 2 boxes per warp
+// plain epilogue: 2 staging boxes for each of 4 warps; SwiGLU backward: one
+// 2 KiB transpose buffer for each of 8 warps
+constexpr int kQEpiBytes = 4 * 2 * kQEpiChunk;
 
 enum BwdMode : int { kModeDgrad = 0, kModeDgradSwiglu = 1, kModeWgrad = 2 };
 
@@ -93,7 +95,9 @@ struct BwdParams {
   int Mw;                 // wgrad: output rows per group
   int n_tiles;            // column blocks of QN
   int m_tiles;            // wgrad: row blocks of QM per group
+  int ksplit;             // wgrad: slices of each group's rows (1 = none)
   uint16_t* out;          // plain dgrad [M, Nout]; wgrad [G * Mw, Nout]
+  float* out_f32;         // wgrad with ksplit > 1: fp32 partials [ksplit, G * Mw, Nout]
   // swiglu dgrad: saved gate_up rows [M, 2I] in, their gradient [M, 2I] out (I = Nout)
   const uint16_t* gate_up;
   uint16_t* d_gate_up;
@@ -130,6 +134,15 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
+__device__ __forceinline__ uint4 ld_shared_v4q(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
 __device__ __forceinline__ void st_shared_v4q(uint32_t addr, uint4 v) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z),
                "r"(v.w)
@@ -137,11 +150,14 @@ __device__ __forceinline__ void st_shared_v4q(uint32_t addr, uint4 v) {
 }
 
 // Tile t of the schedule.  dgrad: (128-row block over all groups, column
-// block), column blocks innermost; wgrad: (group, row block, column block).
+// block), column blocks innermost; wgrad: (group, row slice, row block,
+// column block), where a group's rows are cut into ksplit slices of whole
+// 64-row blocks (split-K: each slice's product is an fp32 partial).
 struct QTile {
   int g;
-  int row0;     // dgrad: first output row; wgrad: first row of the group
-  int row_end;  // dgrad: the group's end row; wgrad: the group's end row
+  int split;    // wgrad: row slice
+  int row0;     // dgrad: first output row; wgrad: first row of the slice
+  int row_end;  // dgrad: the group's end row; wgrad: the slice's end row
   int m0;       // wgrad: first output row inside the group's block
   int n0;       // first output column
   int nkb;      // k-blocks of 64
@@ -151,14 +167,19 @@ template <int MODE>
 __device__ __forceinline__ QTile decode_q(const BwdCtl& ctl, const BwdParams& p, int tile) {
   QTile t;
   if (MODE == kModeWgrad) {
-    const int per_g = p.m_tiles * p.n_tiles;
+    const int per_s = p.m_tiles * p.n_tiles;
+    const int per_g = per_s * p.ksplit;
     t.g = tile / per_g;
-    const int r = tile - t.g * per_g;
+    int r = tile - t.g * per_g;
+    t.split = r / per_s;
+    r -= t.split * per_s;
     const int mt = r / p.n_tiles;
     t.n0 = (r - mt * p.n_tiles) * QN;
     t.m0 = mt * QM;
-    t.row0 = ctl.group_rows[t.g];
-    t.row_end = ctl.group_rows[t.g + 1];
+    const int g0 = ctl.group_rows[t.g], g1 = ctl.group_rows[t.g + 1];
+    const int slice = cdiv(cdiv(g1 - g0, p.ksplit), QK) * QK;
+    t.row0 = min(g1, g0 + t.split * slice);
+    t.row_end = min(g1, t.row0 + slice);
     t.nkb = cdiv(t.row_end - t.row0, QK);
   } else {
     const int mt = tile / p.n_tiles;
@@ -172,6 +193,7 @@ __device__ __forceinline__ QTile decode_q(const BwdCtl& ctl, const BwdParams& p,
     t.row0 = ctl.group_rows[lo] + (mt - ctl.tile_prefix[lo]) * QM;
     t.row_end = ctl.group_rows[lo + 1];
     t.m0 = 0;
+    t.split = 0;
     t.nkb = cdiv(p.Kc, QK);
   }
   return t;
@@ -273,7 +295,8 @@ grouped_gemm_bwd_kernel(const __grid_constant__ CUtensorMap tmA,
   tc_fence_after();
 
   const uint32_t tmem_base = ctl.tmem_base;
-  const int num_tiles = kWgrad ? G * p.m_tiles * p.n_tiles : ctl.num_m_tiles * p.n_tiles;
+  const int num_tiles =
+      kWgrad ? G * p.ksplit * p.m_tiles * p.n_tiles : ctl.num_m_tiles * p.n_tiles;
   volatile int* abort = &ctl.abort;
   int never = 0;
   const unsigned long long lim = p.wait_limit_ns;
@@ -411,18 +434,118 @@ grouped_gemm_bwd_kernel(const __grid_constant__ CUtensorMap tmA,
       const bool row_ok = r_in_tile < nrows && (kWgrad || orow0 + r_in_tile < p.M);
       const bool quad_full = (quad + 1) * 32 <= nrows && (kWgrad || orow0 + (quad + 1) * 32 <= p.M);
       const int64_t grow = orow0 + r_in_tile;
+      float* prow = nullptr;  // wgrad split-K: this row's fp32 partial
+      if (kWgrad && p.out_f32)
+        prow = p.out_f32 + (static_cast<int64_t>(t.split) * G * p.Mw + grow) * p.Nout;
       if (kWgrad && t.nkb == 0) {
-        // a group with no rows: its weight gradient is zero
+        // a group (or slice) with no rows: its contribution is zero
         if (row_ok) {
           for (int c = first; c < QN / 32; c += kStride) {
             const int col0 = t.n0 + c * 32;
 #pragma unroll
-            for (int c4 = 0; c4 < 4; ++c4)
-              if (col0 + c4 * 8 + 8 <= p.Nout)
+            for (int c4 = 0; c4 < 4; ++c4) {
+              if (col0 + c4 * 8 + 8 > p.Nout) continue;
+              if (prow) {
+                *reinterpret_cast<uint4*>(prow + col0 + c4 * 8) = make_uint4(0u, 0u, 0u, 0u);
+                *reinterpret_cast<uint4*>(prow + col0 + c4 * 8 + 4) = make_uint4(0u, 0u, 0u, 0u);
+              } else {
                 *reinterpret_cast<uint4*>(p.out + grow * p.Nout + col0 + c4 * 8) =
                     make_uint4(0u, 0u, 0u, 0u);
+              }
+            }
           }
         }
+        continue;
+      }
+      if (MODE == kModeDgradSwiglu) {
+        // SiLU(gate) * up backward.  Nout = I; the saved gate_up row holds
+        // gate at [0, I) and up at [I, 2I).  A lane owns one accumulator row,
+        // so reading and writing 64 B per lane and row would touch 32 lines
+        // per instruction; instead the warp moves each 32-row x 32-column
+        // block through a 2 KiB swizzled buffer: global loads and stores are
+        // coalesced (8 rows x 64 B per instruction) and the buffer turns them
+        // into one row per lane.  The gate/up values of a chunk are loaded
+        // one chunk ahead (the first while the accumulator is being
+        // computed).  A chunk may end past I (a multiple of 8, not of 32):
+        // only its 8-column groups inside [0, I) are read and written.
+        const int64_t I = p.Nout;
+        const uint32_t tbuf = sbase + kQStages * kQStageBytes + ew * 2048;
+        const int cr = lane >> 2, cc = lane & 3;  // coalesced: row 8 i + cr, 16 B column cc
+        // rows of this quadrant that are inside the tile's group and inside M
+        const int64_t qrow0 = orow0 + quad * 32;
+        const int qrows = static_cast<int>(
+            max(int64_t(0), min(min(int64_t(32), int64_t(nrows) - quad * 32), p.M - qrow0)));
+        auto load_gu = [&](int c, uint4 (&g)[4], uint4 (&u)[4]) {
+          const int col = t.n0 + c * 32 + cc * 8;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int r = 8 * i + cr;
+            const bool in = r < qrows && col + 8 <= p.Nout;
+            const uint16_t* src = p.gate_up + (qrow0 + (in ? r : 0)) * 2 * I + col;
+            g[i] = in ? *reinterpret_cast<const uint4*>(src) : make_uint4(0u, 0u, 0u, 0u);
+            u[i] = in ? *reinterpret_cast<const uint4*>(src + I) : make_uint4(0u, 0u, 0u, 0u);
+          }
+        };
+        // coalesced layout <-> one row per lane, through the warp's buffer
+        auto to_rows = [&](const uint4 (&q)[4], uint4 (&row)[4]) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int r = 8 * i + cr;
+            st_shared_v4q(tbuf + r * 64 + ((cc ^ ((r >> 1) & 3)) << 4), q[i]);
+          }
+          __syncwarp();
+#pragma unroll
+          for (int c4 = 0; c4 < 4; ++c4)
+            row[c4] = ld_shared_v4q(tbuf + lane * 64 + ((c4 ^ ((lane >> 1) & 3)) << 4));
+          __syncwarp();
+        };
+        auto store_rows = [&](const uint4 (&row)[4], uint16_t* base_col) {
+#pragma unroll
+          for (int c4 = 0; c4 < 4; ++c4)
+            st_shared_v4q(tbuf + lane * 64 + ((c4 ^ ((lane >> 1) & 3)) << 4), row[c4]);
+          __syncwarp();
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int r = 8 * i + cr;
+            const uint4 v = ld_shared_v4q(tbuf + r * 64 + ((cc ^ ((r >> 1) & 3)) << 4));
+            if (r < qrows && base_col) *reinterpret_cast<uint4*>(base_col + (qrow0 + r) * 2 * I) = v;
+          }
+          __syncwarp();
+        };
+        uint4 gq[4], uq[4];
+        load_gu(first, gq, uq);
+        if (!mbar_wait_bounded(smem_u32(&ctl.acc_full[acc]), acc_phase, abort, p.err, lim)) break;
+        tc_fence_after();
+        const uint32_t trow = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
+                              static_cast<uint32_t>(acc * QN);
+#pragma unroll 1
+        for (int c = first; c < QN / 32; c += kStride) {
+          uint4 gn[4], un[4];
+          if (c + kStride < QN / 32) load_gu(c + kStride, gn, un);
+          uint32_t ra[32];
+          tmem_ld_32cols(trow + c * 32, ra);
+          tc_wait_ld();
+          const int col0 = t.n0 + c * 32;
+          if (qrows > 0 && col0 < p.Nout) {
+            uint4 gw[4], uw[4], dg[4], du[4];
+            to_rows(gq, gw);
+            to_rows(uq, uw);
+            swiglu_bwd_pack(ra, gw, uw, dg, du);
+            const int col = col0 + cc * 8;
+            const bool col_in = col + 8 <= p.Nout;
+            store_rows(dg, col_in ? p.d_gate_up + col : nullptr);
+            store_rows(du, col_in ? p.d_gate_up + I + col : nullptr);
+          }
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            gq[i] = gn[i];
+            uq[i] = un[i];
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&ctl.acc_empty[acc]));
+        if (++acc == kQAcc) { acc = 0; acc_phase ^= 1u; }
         continue;
       }
       if (!mbar_wait_bounded(smem_u32(&ctl.acc_full[acc]), acc_phase, abort, p.err, lim)) break;
@@ -436,29 +559,17 @@ grouped_gemm_bwd_kernel(const __grid_constant__ CUtensorMap tmA,
         tc_wait_ld();
         const int col0 = t.n0 + c * 32;
         if (col0 >= p.Nout) continue;
-        if (MODE == kModeDgradSwiglu) {
-          // Nout = I; the saved gate_up row holds gate at [0, I) and up at [I, 2I)
-          if (!row_ok) continue;
-          const int64_t I = p.Nout;
-          const uint16_t* grow_p = p.gate_up + grow * 2 * I;
-          uint16_t* drow_p = p.d_gate_up + grow * 2 * I;
-          // a chunk may end past I (I is a multiple of 8, not of 32): only
-          // its 8-column groups inside [0, I) are read and written
-          uint4 gw[4], uw[4], dg[4], du[4];
+        if (kWgrad && prow) {
+          // split-K partial: the fp32 sums, unrounded
+          if (row_ok) {
 #pragma unroll
-          for (int c4 = 0; c4 < 4; ++c4) {
-            const bool in = col0 + c4 * 8 + 8 <= p.Nout;
-            gw[c4] = in ? *reinterpret_cast<const uint4*>(grow_p + col0 + c4 * 8)
-                        : make_uint4(0u, 0u, 0u, 0u);
-            uw[c4] = in ? *reinterpret_cast<const uint4*>(grow_p + I + col0 + c4 * 8)
-                        : make_uint4(0u, 0u, 0u, 0u);
-          }
-          swiglu_bwd_pack(ra, gw, uw, dg, du);
-#pragma unroll
-          for (int c4 = 0; c4 < 4; ++c4) {
-            if (col0 + c4 * 8 + 8 > p.Nout) continue;
-            *reinterpret_cast<uint4*>(drow_p + col0 + c4 * 8) = dg[c4];
-            *reinterpret_cast<uint4*>(drow_p + I + col0 + c4 * 8) = du[c4];
+            for (int c4 = 0; c4 < 4; ++c4) {
+              if (col0 + c4 * 8 + 8 > p.Nout) continue;
+              *reinterpret_cast<uint4*>(prow + col0 + c4 * 8) =
+                  make_uint4(ra[8 * c4], ra[8 * c4 + 1], ra[8 * c4 + 2], ra[8 * c4 + 3]);
+              *reinterpret_cast<uint4*>(prow + col0 + c4 * 8 + 4) =
+                  make_uint4(ra[8 * c4 + 4], ra[8 * c4 + 5], ra[8 * c4 + 6], ra[8 * c4 + 7]);
+            }
           }
           continue;
         }
@@ -506,6 +617,21 @@ grouped_gemm_bwd_kernel(const __grid_constant__ CUtensorMap tmA,
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, kQTmemCols);
+  }
+}
+
+// Split-K wgrad: out[i] = bf16(sum over slices, in order, of partial[s][i]).
+__global__ void __launch_bounds__(256)
+splitk_reduce_kernel(const float4* __restrict__ partial, int64_t n4, int ksplit,
+                     uint2* __restrict__ out) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float4 a = partial[i];
+    for (int s2 = 1; s2 < ksplit; ++s2) {
+      const float4 b = partial[static_cast<int64_t>(s2) * n4 + i];
+      a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
+    }
+    out[i] = make_uint2(cvt_bf16x2(a.x, a.y), cvt_bf16x2(a.z, a.w));
   }
 }
 
@@ -606,6 +732,7 @@ cudaError_t launch_grouped_dgrad(const GroupedDgradArgs& a, cudaStream_t stream)
     return cudaErrorInvalidValue;
   }
   BwdParams p = {};
+  p.ksplit = 1;
   p.counts = a.counts;
   p.G = a.G;
   p.M = a.M;
@@ -643,11 +770,31 @@ cudaError_t launch_grouped_wgrad(const GroupedWgradArgs& a, cudaStream_t stream)
   p.Nout = a.Nw;
   p.m_tiles = cdiv(a.Mw, QM);
   p.n_tiles = cdiv(a.Nw, QN);
+  p.ksplit = a.partial && a.ksplit > 1 ? a.ksplit : 1;
   p.out = static_cast<uint16_t*>(a.out);
+  p.out_f32 = p.ksplit > 1 ? a.partial : nullptr;
   p.err = a.err;
   p.wait_limit_ns = kWaitLimitNs;
-  const int64_t max_tiles = static_cast<int64_t>(a.G) * p.m_tiles * p.n_tiles;
-  return launch_bwd<kModeWgrad>(ma, mb, mc, p, max_tiles, a.sm_limit, stream);
+  const int64_t max_tiles = static_cast<int64_t>(a.G) * p.ksplit * p.m_tiles * p.n_tiles;
+  cudaError_t e = launch_bwd<kModeWgrad>(ma, mb, mc, p, max_tiles, a.sm_limit, stream);
+  if (e != cudaSuccess || p.ksplit == 1) return e;
+  const int64_t n4 = static_cast<int64_t>(a.G) * a.Mw * a.Nw / 4;
+  const int blocks = static_cast<int>(cdiv64(n4, 256) < 4 * 148 ? cdiv64(n4, 256) : 4 * 148);
+  splitk_reduce_kernel<<<blocks, 256, 0, stream>>>(reinterpret_cast<const float4*>(a.partial), n4,
+                                                    p.ksplit, reinterpret_cast<uint2*>(a.out));
+  return cudaGetLastError();
 }
 
+}  // namespace hmoe
+
+namespace hmoe {
+int wgrad_ksplit(int64_t M, int Mw, int Nw, int G) {
+  const int64_t tiles = static_cast<int64_t>(G) * cdiv(Mw, QM) * cdiv(Nw, QN);
+  const int64_t sms = num_sms_for_current_device();
+  if (tiles >= sms) return 1;
+  int64_t ks = cdiv64(sms, tiles);
+  const int64_t max_by_rows = cdiv64(M, 4 * QK);  // at least four 64-row blocks per slice
+  if (ks > max_by_rows) ks = max_by_rows;
+  return ks < 1 ? 1 : static_cast<int>(ks > 64 ? 64 : ks);
+}
 }  // namespace hmoe

@@ -137,6 +137,9 @@ struct GroupedDgradArgs {
 };
 cudaError_t launch_grouped_dgrad(const GroupedDgradArgs& args, cudaStream_t stream);
 // wgrad: out[g] = grad_out[rows of g]^T @ input[rows of g], out [G, Mw, Nw].
+// With ksplit > 1 and `partial` set (fp32, ksplit * G * Mw * Nw floats) each
+// group's rows are cut into ksplit slices whose fp32 products are summed in
+// slice order and rounded once (split-K, for few output tiles over many rows).
 struct GroupedWgradArgs {
   const void* grad_out;   // [M, Mw]
   const void* input;      // [M, Nw]
@@ -148,7 +151,11 @@ struct GroupedWgradArgs {
   int G;
   int* err;
   int sm_limit;
+  int ksplit = 1;
+  float* partial = nullptr;
 };
+// Slices for a split-K wgrad of G groups over M rows (fills the SMs).
+int wgrad_ksplit(int64_t M, int Mw, int Nw, int G);
 cudaError_t launch_grouped_wgrad(const GroupedWgradArgs& args, cudaStream_t stream);
 
 // train.cu (bf16): the backward's non-GEMM kernels and the aux statistics ----

@@ -351,6 +351,22 @@ int hmoe_ffn_backward(const hmoe_shape* shape, const void* grad_y, const float* 
                       void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * hmoe_ffn_backward that also records 8 caller-owned cudaEvent_t (NULL
+ * entries skipped) on the stream: at the start, after the combine/router
+ * backward, after the down projection's dgrad (with the SiLU backward), after
+ * its wgrad, after the gate_up dgrad, after its wgrad, after the router dgrad
+ * and the d_x gather, and at the end (router wgrad and bias).  Same kernels,
+ * same results.
+ */
+int hmoe_ffn_backward_marked(const hmoe_shape* shape, const void* grad_y, const float* aux_grad,
+                             int64_t aux_tokens, const void* x, const void* w_router,
+                             const void* router_bias, const void* w_gate_up, const void* w_down,
+                             const void* saved, size_t saved_bytes, void* grad_x,
+                             void* grad_w_router, void* grad_router_bias, void* grad_w_gate_up,
+                             void* grad_w_down, void* workspace, size_t workspace_bytes,
+                             void* stream, void* const* phase_events);
+
+/*
  * Read (and synchronise the stream for) the error word kernels leave at the
  * start of a workspace used by hmoe_ffn_forward, hmoe_experts_forward,
  * hmoe_dispatch, hmoe_grouped_* or hmoe_ep_forward: HMOE_OK, HMOE_EINVAL (an
