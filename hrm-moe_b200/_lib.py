@@ -64,6 +64,8 @@ SIGNATURES = {
     "hmoe_router_workspace_bytes": (c_size_t, [ShapeP]),
     "hmoe_router_topk": (c_int, [ShapeP, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                  c_void_p, c_void_p, c_size_t, c_void_p]),
+    "hmoe_router_topk_sums": (c_int, [ShapeP, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                      c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
     "hmoe_dispatch_workspace_bytes": (c_size_t, [ShapeP]),
     "hmoe_dispatch": (c_int, [ShapeP, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                               c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),

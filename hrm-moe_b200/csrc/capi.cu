@@ -661,6 +661,33 @@ int hmoe_router_topk(const hmoe_shape* shape, const void* x, const void* w_route
   return HMOE_OK;
 }
 
+int hmoe_router_topk_sums(const hmoe_shape* shape, const void* x, const void* w_router,
+                          const void* router_bias, int32_t* topk_idx, void* topk_weight,
+                          void* logits, float* sums, void* workspace, size_t workspace_bytes,
+                          void* stream) {
+  int rc = validate_shape(shape);
+  if (rc) return rc;
+  const hmoe_shape& s = *shape;
+  if (s.dtype != HMOE_DTYPE_BF16)
+    return fail(HMOE_EINVAL, "tensor-core sums exist for bf16 layers only");
+  if (s.tokens == 0) return HMOE_OK;
+  if (!x || !w_router || !topk_idx || !sums)
+    return fail(HMOE_EINVAL, "x, w_router, topk_idx and sums are required");
+  if (!aligned16(x) || !aligned16(w_router)) return fail(HMOE_EINVAL, "x and w_router must be 16-byte aligned");
+  if ((rc = select_device(x))) return rc;
+  if ((rc = check_ws(workspace, workspace_bytes, hmoe_router_workspace_bytes(shape)))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Carve c{static_cast<char*>(workspace)};
+  int* err = c.take<int>(sizeof(int));
+  void* scratch = c.take<void>(router_tc_scratch_bytes(s.tokens));
+  HMOE_CUDA(cudaMemsetAsync(err, 0, sizeof(int), st), "reset error word");
+  HMOE_CUDA(launch_router_topk_tc(x, w_router, router_bias, s.tokens, s.hidden, s.experts,
+                                  s.top_k, s.norm_topk_prob, topk_idx, nullptr, topk_weight,
+                                  logits, scratch, err, st, sums),
+            "router_topk");
+  return HMOE_OK;
+}
+
 size_t hmoe_dispatch_workspace_bytes(const hmoe_shape* shape) {
   return plan_bytes(shape, [](Carve& c, const hmoe_shape& s) {
     carve_dispatch(c, s);

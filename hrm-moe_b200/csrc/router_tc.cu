@@ -74,6 +74,7 @@ struct RtParams {
   float* topk_w_f32;
   void* topk_w_dtype;
   uint16_t* logits_out;
+  float* sums_out;        // diagnostic: the fp32 tensor-core sums (before the bias)
   int* fix_count;
   int32_t* fix_list;
   unsigned* group_done;   // split fix-up: finished expert groups per token group
@@ -128,6 +129,8 @@ template <int KMAX>
 __device__ __forceinline__ void route_row_certified(float* vrow, uint32_t* krow, uint32_t* xrow,
                                                     const RtParams& p, int64_t t) {
   const int E = p.E, k = p.k;
+  if (p.sums_out)
+    for (int e = 0; e < E; ++e) p.sums_out[t * E + e] = vrow[e];
   float mag = 0.0f;
   for (int e = 0; e < E; ++e) {
     float v = vrow[e];
@@ -759,6 +762,351 @@ bool map_rows(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, ui
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// ----------------------------------------------------------------------------
+// router_rows_kernel: the tensor-core pass with 64 tokens per CTA.
+//
+// x [T, d] is read as the row-major matrix [2T, d/2] (the same bytes): row
+// 2t is the first half of token t's hidden state, row 2t+1 the second.  One
+// 128-row MMA tile is then 64 tokens, and its B operand stacks the two
+// halves of the router weight, [W[:, :d/2]; W[:, d/2:]] (2E rows), so that
+// accumulator row 2t, columns [0, E) hold the first half's sums and row
+// 2t+1, columns [E, 2E) the second half's; logit = first + second.  (The
+// other two quarters of the product are not used: the tensor cores have
+// time to spare, HBM does not.)  Twice as many CTAs as 128-token tiles, two
+// per SM for E <= 64, so one CTA's epilogue overlaps another's stream.
+//
+// A configuration serves every E up to its EMAX (64 or 128): weight rows
+// E..EMAX-1 of each half are past the end of W, so TMA fills them with zeros
+// and those experts are never picked.
+//
+// Epilogue: 8 warps.  The four warps that own the accumulator's TMEM lane
+// quadrants park each row's useful half in shared memory and meet the other
+// four at a hardware named barrier (no spinning).  Then every token is routed
+// by 4 lanes, each holding E/4 logits (experts s, s+4, ...): the same
+// certified selection as route_row_certified (order-preserving keys, the
+// set of bf16 values an exact-order sum could round to, each pick against
+// the next, the last against every unpicked expert) with group shuffles,
+// the softmax over the rounded logits, and the same outputs; uncertified
+// tokens go to the fix list.
+constexpr int RRT = 64;          // tokens per CTA
+constexpr int kRrEpiWarps = 8;   // warps 2..9; 4 lanes per token
+constexpr int kRrThreads = 64 + 32 * kRrEpiWarps;
+
+template <int E>  // the largest expert count of the configuration (64 or 128)
+struct RrCfg {
+  static constexpr int kN = 2 * E;                    // MMA N (and TMEM columns)
+  static constexpr int kABytes = 128 * RBK * 2;        // 16 KiB: 64 tokens x 2 halves
+  static constexpr int kBBytes = kN * RBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStages = E <= 64 ? 3 : 4;       // E <= 64: two CTAs per SM
+  static constexpr int kRingBytes = kStages * kStageBytes;
+  static constexpr int kLgStride = E + 1;
+  static constexpr int kLgBytes = 2 * RRT * kLgStride * 4;  // the two halves' sums
+  static constexpr int kMainBytes = kRingBytes > kLgBytes ? kRingBytes : kLgBytes;
+  static constexpr size_t kSmem = 1024 + kMainBytes + 256;
+  static_assert(kStageBytes % 1024 == 0, "stages keep the 1 KiB swizzle alignment");
+  static_assert(kStages <= 8, "RtCtl holds eight stage barriers of each kind");
+  static_assert(kSmem <= 232448, "shared memory budget");
+};
+
+// Reductions over the 4 lanes of one token.  `gm` names exactly those four
+// lanes: a warp's other tokens may be past T and not take part.
+__device__ __forceinline__ uint32_t shfl4_max(uint32_t v, unsigned gm) {
+  v = max(v, __shfl_xor_sync(gm, v, 1));
+  return max(v, __shfl_xor_sync(gm, v, 2));
+}
+__device__ __forceinline__ float shfl4_maxf(float v, unsigned gm) {
+  v = fmaxf(v, __shfl_xor_sync(gm, v, 1));
+  return fmaxf(v, __shfl_xor_sync(gm, v, 2));
+}
+__device__ __forceinline__ float shfl4_sum(float v, unsigned gm) {
+  v += __shfl_xor_sync(gm, v, 1);
+  return v + __shfl_xor_sync(gm, v, 2);
+}
+// bf16 value (as fp32) of an order-preserving key
+__device__ __forceinline__ float key_value(uint32_t key) {
+  const uint32_t ob = key >> 16;
+  const uint32_t b = (ob & 0x8000u) ? (ob & 0x7FFFu) : (~ob & 0xFFFFu);
+  return bf16_bits_to_f32(b);
+}
+
+__device__ __forceinline__ void named_barrier_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+template <int E, int KMAX>  // E: the configuration's expert maximum (p.E <= E)
+__global__ void __launch_bounds__(kRrThreads, E <= 64 ? 2 : 1)
+router_rows_kernel(const __grid_constant__ CUtensorMap tmX2, const __grid_constant__ CUtensorMap tmW,
+                   const RtParams p) {
+  using C = RrCfg<E>;
+  constexpr int NE = E / 4;  // logits per lane
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  RtCtl& ctl = *reinterpret_cast<RtCtl*>(smem + C::kMainBytes);
+  float* lg0 = reinterpret_cast<float*>(smem);          // [64][E+1] first halves
+  float* lg1 = lg0 + RRT * C::kLgStride;                // [64][E+1] second halves
+  const uint32_t sbase = smem_u32(smem);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t t0 = static_cast<int64_t>(blockIdx.x) * RRT;
+  const int half = p.d / 2;
+  const int nkb = cdiv(half, RBK);
+  const unsigned long long lim = p.wait_limit_ns;
+
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(smem_u32(&ctl.full[s]), 1);
+      mbar_init(smem_u32(&ctl.empty[s]), 1);
+    }
+    mbar_init(smem_u32(&ctl.acc_full), 1);
+    mbar_init(smem_u32(&ctl.drain), 1);
+    ctl.abort = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmX2);
+    tma_prefetch_desc(&tmW);
+  } else if (warp == 1) {
+    tmem_alloc(smem_u32(&ctl.tmem_base), C::kN);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = ctl.tmem_base;
+  volatile int* abort = &ctl.abort;
+  int never = 0;
+  grid_launch_dependents();
+  // this CTA's 64 tokens own 16 counters of the split fix-up
+  if (p.group_done && threadIdx.x < RRT / 4) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * (RRT / 4) + threadIdx.x;
+    if (i < ((cdiv64(p.T, 4) + 3) & ~static_cast<int64_t>(3))) p.group_done[i] = 0u;
+  }
+
+  if (warp == 0) {
+    if (lane == 0) {
+      uint32_t phase = 0, pending = 0, pend_phase = 0;
+      int stage = 0;
+      for (int kb = 0; kb < nkb; ++kb) {
+        if (!mbar_wait_bounded(smem_u32(&ctl.empty[stage]), phase ^ 1u, abort, p.err, lim)) break;
+        const uint32_t fb = smem_u32(&ctl.full[stage]);
+        const uint32_t sa = sbase + stage * C::kStageBytes;
+        mbar_arrive_expect_tx(fb, C::kStageBytes);
+        tma_load_2d(sa, &tmX2, kb * RBK, static_cast<int>(2 * t0), fb);
+        tma_load_2d(sa + C::kABytes, &tmW, kb * RBK, 0, fb);
+        tma_load_2d(sa + C::kABytes + E * 128, &tmW, half + kb * RBK, 0, fb);
+        pending |= 1u << stage;
+        pend_phase = (pend_phase & ~(1u << stage)) | (phase << stage);
+        if (++stage == C::kStages) { stage = 0; phase ^= 1u; }
+      }
+      for (int s = 0; s < C::kStages; ++s)
+        if ((pending >> s) & 1u)
+          mbar_wait_bounded(smem_u32(&ctl.full[s]), (pend_phase >> s) & 1u, &never, p.err, lim);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(128, C::kN);
+      uint32_t phase = 0;
+      int stage = 0;
+      bool ok = true;
+      for (int kb = 0; kb < nkb; ++kb) {
+        if (!mbar_wait_bounded(smem_u32(&ctl.full[stage]), phase, abort, p.err, lim)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sa = sbase + stage * C::kStageBytes;
+#pragma unroll
+        for (int kk = 0; kk < RBK / 16; ++kk)
+          tc_mma_bf16(tmem, smem_desc_sw128(sa + kk * 32), smem_desc_sw128(sa + C::kABytes + kk * 32),
+                      idesc, (kb | kk) != 0 ? 1u : 0u);
+        tc_commit(smem_u32(&ctl.empty[stage]));
+        if (++stage == C::kStages) { stage = 0; phase ^= 1u; }
+      }
+      if (ok) tc_commit(smem_u32(&ctl.acc_full));
+      tc_commit(smem_u32(&ctl.drain));
+      mbar_wait_bounded(smem_u32(&ctl.drain), 0, &never, p.err, lim);
+    }
+  } else {
+    const int ew = warp - 2;
+    if (ew < 4) {
+      // ---- TMEM readers: row r = 32 quad + lane is token r / 2, half r & 1
+      const int quad = warp & 3;
+      const bool ok = mbar_wait_bounded(smem_u32(&ctl.acc_full), 0, abort, p.err, lim);
+      tc_fence_after();
+      if (ok) {
+        const int r = quad * 32 + lane;
+        float* dst = ((r & 1) ? lg1 : lg0) + (r >> 1) * C::kLgStride;
+        const uint32_t col0 = (r & 1) ? E : 0;  // this half's useful columns
+#pragma unroll 1
+        for (int c = 0; c < E / 32; ++c) {
+          uint32_t ra[32], rb[32];
+          tmem_ld_32cols(tmem + (static_cast<uint32_t>(quad * 32) << 16) + c * 32, ra);
+          tmem_ld_32cols(tmem + (static_cast<uint32_t>(quad * 32) << 16) + E + c * 32, rb);
+          tc_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) dst[c * 32 + i] = __uint_as_float(col0 ? rb[i] : ra[i]);
+        }
+      }
+      tc_fence_before();
+    }
+    named_barrier_sync(1, 32 * kRrEpiWarps);
+    // ---- routing: token j on lanes 4 (j % 8) .. +3 of warp j / 8
+    const int j = ew * 8 + (lane >> 2), s = lane & 3;
+    const unsigned gm = 0xFu << (lane & 28);  // this token's four lanes
+    const int64_t t = t0 + j;
+    if (!*abort && t < p.T) {  // uniform over the 4 lanes of a token
+      const float* a0 = lg0 + j * C::kLgStride;
+      const float* a1 = lg1 + j * C::kLgStride;
+      const int En = p.E;
+      float v[NE];
+      float mag = 0.0f;
+#pragma unroll
+      for (int i = 0; i < NE; ++i) {
+        const int e = s + 4 * i;
+        float x = -INFINITY;  // experts past E: never picked (key 0 below)
+        if (e < En) {
+          x = a0[e] + a1[e];
+          if (p.sums_out) p.sums_out[t * En + e] = x;
+          if (p.bias) x = x + bf16_bits_to_f32(p.bias[e]);
+          if (isfinite(x)) mag = fmaxf(mag, fabsf(x));
+          if (p.logits_out)
+            p.logits_out[t * En + e] = static_cast<uint16_t>(f32_to_bf16_bits(x));
+        }
+        v[i] = x;
+      }
+      mag = shfl4_maxf(mag, gm);
+      const float delta = p.cert_rel * mag;
+      // softmax over the rounded logits
+      float mx = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < NE; ++i) mx = fmaxf(mx, round_bf16(v[i]));
+      mx = shfl4_maxf(mx, gm);
+      float ssum = 0.0f;
+#pragma unroll
+      for (int i = 0; i < NE; ++i) ssum += expf(round_bf16(v[i]) - mx);
+      ssum = shfl4_sum(ssum, gm);
+      uint32_t key[NE], kmn[NE], kmx[NE];
+#pragma unroll
+      for (int i = 0; i < NE; ++i) {
+        key_range(v[i], delta, static_cast<uint32_t>(s + 4 * i), kmn[i], kmx[i], key[i]);
+        if (s + 4 * i >= En) key[i] = kmn[i] = kmx[i] = 0u;
+      }
+      uint32_t pk[KMAX];
+      bool bad = false;
+      uint32_t prev_min = 0;
+#pragma unroll
+      for (int r = 0; r < KMAX; ++r) {
+        pk[r] = 0;
+        if (r < p.k) {
+          uint32_t best = 0;
+#pragma unroll
+          for (int i = 0; i < NE; ++i) best = max(best, key[i]);
+          best = shfl4_max(best, gm);
+          uint32_t bmin = 0, bmax = 0;
+#pragma unroll
+          for (int i = 0; i < NE; ++i)
+            if (key[i] == best) { bmin = kmn[i]; bmax = kmx[i]; key[i] = 0; }
+          // only the owner lane found it: the others hold zeros
+          bmin = shfl4_max(bmin, gm);
+          bmax = shfl4_max(bmax, gm);
+          if (r > 0 && !(prev_min > bmax)) bad = true;
+          prev_min = bmin;
+          pk[r] = best;
+        }
+      }
+      uint32_t rest = 0;  // largest key an unpicked expert could take
+#pragma unroll
+      for (int i = 0; i < NE; ++i)
+        if (key[i] != 0) rest = max(rest, kmx[i]);
+      rest = shfl4_max(rest, gm);
+      if (!(prev_min > rest)) bad = true;
+      float pw[KMAX], ps = 0.0f;
+#pragma unroll
+      for (int r = 0; r < KMAX; ++r) {
+        pw[r] = 0.0f;
+        if (r < p.k) {
+          pw[r] = expf(key_value(pk[r]) - mx) / ssum;
+          ps += pw[r];
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < KMAX; ++r) {
+        if (r < p.k && (r & 3) == s) {
+          float w = p.norm ? pw[r] / fmaxf(ps, 1e-12f) : pw[r];
+          w = round_bf16(w);
+          const int64_t o = t * p.k + r;
+          p.topk_idx[o] = 0xFFFF - static_cast<int>(pk[r] & 0xFFFFu);
+          if (p.topk_w_f32) p.topk_w_f32[o] = w;
+          if (p.topk_w_dtype)
+            static_cast<uint16_t*>(p.topk_w_dtype)[o] = static_cast<uint16_t>(f32_to_bf16_bits(w));
+        }
+      }
+      if (bad && s == 0) {
+        const int slot = atomicAdd(p.fix_count, 1);
+        p.fix_list[slot] = static_cast<int32_t>(t);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::kN);
+  }
+}
+
+// x [T, d] as [2T, d/2] rows with [128 x 64] boxes (the row-split operand).
+bool map_half_rows(CUtensorMap* m, const void* base, uint64_t T, uint64_t d) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  const cuuint64_t dims[2] = {d / 2, 2 * T};
+  const cuuint64_t strides[1] = {d};  // (d / 2) bf16
+  const cuuint32_t box[2] = {RBK, 128};
+  const cuuint32_t estr[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// HMOE_ROUTER_WHOLE_ROWS=1 (read once per process) keeps the 128-token
+// whole-row kernel for every d, so tests can compare the two passes.
+bool router_whole_rows_forced() {
+  static const bool forced = [] {
+    const char* v = getenv("HMOE_ROUTER_WHOLE_ROWS");
+    return v && atoi(v) != 0;
+  }();
+  return forced;
+}
+
+template <int E, int KMAX>
+cudaError_t launch_rows_tc(const void* x, const void* w, const RtParams& p, cudaStream_t st) {
+  using C = RrCfg<E>;
+  static int done[64] = {0};
+  static std::mutex mu;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!done[dev]) {
+      e = cudaFuncSetAttribute(router_rows_kernel<E, KMAX>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(C::kSmem));
+      if (e != cudaSuccess) return e;
+      e = cudaFuncSetAttribute(router_rows_kernel<E, KMAX>,
+                               cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+      if (e != cudaSuccess) return e;
+      done[dev] = 1;
+    }
+  }
+  CUtensorMap mx, mw;
+  if (!map_half_rows(&mx, x, static_cast<uint64_t>(p.T), static_cast<uint64_t>(p.d)) ||
+      !map_rows(&mw, w, static_cast<uint64_t>(p.E), static_cast<uint64_t>(p.d), E))
+    return cudaErrorInvalidValue;
+  router_rows_kernel<E, KMAX><<<static_cast<unsigned>(cdiv64(p.T, RRT)), kRrThreads, C::kSmem, st>>>(
+      mx, mw, p);
+  return cudaGetLastError();
+}
+
 template <int EPAD, int KMAX>
 cudaError_t launch_tc(const void* x, const void* w, const RtParams& p, cudaStream_t st) {
   using C = RCfg<EPAD>;
@@ -798,9 +1146,15 @@ cudaError_t launch_tc(const void* x, const void* w, const RtParams& p, cudaStrea
   if (!map_rows(&mx, x, static_cast<uint64_t>(p.T), static_cast<uint64_t>(p.d), RBM) ||
       !map_rows(&mw, w, static_cast<uint64_t>(p.E), static_cast<uint64_t>(p.d), EPAD))
     return cudaErrorInvalidValue;
-  router_tc_kernel<EPAD, KMAX><<<static_cast<unsigned>(cdiv64(p.T, RBM)), kRtThreads, C::kSmem, st>>>(
-      mx, mw, p);
-  e = cudaGetLastError();
+  // the tensor-core pass: 64-token CTAs over the two halves of each row when
+  // d splits into 16-byte aligned halves (router_rows_kernel), else 128-token
+  // CTAs over whole rows
+  if (p.d % 16 == 0 && !router_whole_rows_forced())
+    e = launch_rows_tc<EPAD, KMAX>(x, w, p, st);
+  else
+    router_tc_kernel<EPAD, KMAX><<<static_cast<unsigned>(cdiv64(p.T, RBM)), kRtThreads, C::kSmem,
+                                   st>>>(mx, mw, p);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   const int nb = cdiv(p.d, kLogitBlock);
   // The split fix-up's grid: a multiple of the expert groups, one token group
@@ -879,7 +1233,7 @@ size_t router_tc_scratch_bytes(int64_t T) {
 cudaError_t launch_router_topk_tc(const void* x, const void* w_router, const void* bias,
                                   int64_t T, int d, int E, int k, int norm, int32_t* topk_idx,
                                   float* topk_w_f32, void* topk_w_dtype, void* logits_out,
-                                  void* scratch, int* err, cudaStream_t stream) {
+                                  void* scratch, int* err, cudaStream_t stream, float* sums_out) {
   if (T == 0) return cudaSuccess;
   int* fix_count = static_cast<int*>(scratch);
   cudaError_t e = cudaMemsetAsync(fix_count, 0, sizeof(int), stream);
@@ -895,6 +1249,7 @@ cudaError_t launch_router_topk_tc(const void* x, const void* w_router, const voi
   p.topk_w_f32 = topk_w_f32;
   p.topk_w_dtype = topk_w_dtype;
   p.logits_out = static_cast<uint16_t*>(logits_out);
+  p.sums_out = sums_out;
   p.fix_count = fix_count;
   p.group_done = reinterpret_cast<unsigned*>(fix_count + 64);
   p.fix_list = fix_count + 64 + fix_groups(T);

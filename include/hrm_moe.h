@@ -123,6 +123,19 @@ int hmoe_router_topk(const hmoe_shape* shape, const void* x, const void* w_route
                      void* logits, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * hmoe_router_topk (bf16 layers) that also writes `sums` [T, E] fp32: the
+ * tensor-core sums of x . w_router^T (before the bias) from which the router
+ * certifies its top-k against the fixed-order definition.  No counterpart in
+ * the reference: a diagnostic that lets a test measure how far those sums
+ * are from the fixed-order sums, next to the certification margin.  Same
+ * routing and workspace as hmoe_router_topk.
+ */
+int hmoe_router_topk_sums(const hmoe_shape* shape, const void* x, const void* w_router,
+                          const void* router_bias, int32_t* topk_idx, void* topk_weight,
+                          void* logits, float* sums, void* workspace, size_t workspace_bytes,
+                          void* stream);
+
+/*
  * Dispatch: flatten, stable sort by expert, gather rows, count
  * (models/layers.py:311-322).  Writes sort_idx [T*k], counts [E] and, when
  * non-NULL, sorted_token [T*k] (int32), sorted_weight [T*k] (layer dtype)

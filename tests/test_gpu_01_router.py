@@ -147,3 +147,40 @@ def test_router_fixup_pass_is_exact_order(tmp_path):
         assert np.array_equal(logits, ol), name
         assert np.array_equal(idx.astype(np.int64), oidx), name
         np.testing.assert_allclose(wt, ow, rtol=2 ** -7, atol=0, err_msg=name)
+
+
+def test_router_whole_row_pass_is_exact(tmp_path):
+    """The 128-token whole-row tensor-core pass (the one that runs when d is
+    not a multiple of 16), forced for every d with HMOE_ROUTER_WHOLE_ROWS=1 in
+    a child process: its certified routing must equal the exact-order routing
+    too, on the same cases as the fix-up test."""
+    import os
+    import subprocess
+    import sys
+
+    import torch
+
+    import router_fixup_worker_gpu as W
+
+    path = tmp_path / "whole_rows.pt"
+    env = dict(os.environ, HMOE_ROUTER_WHOLE_ROWS="1")
+    env.pop("HMOE_ROUTER_CERT_REL", None)
+    subprocess.run([sys.executable, W.__file__, str(path)], env=env, check=True, timeout=600)
+    res = torch.load(path)
+    for name, x, w, bias, k, norm in W.cases():
+        idx, wt, _ = (t.numpy() for t in res[name])
+        ol = O.router_logits(x, w, bias, "bf16")
+        oidx, ow, _ = O.route(ol, k, norm, "bf16")
+        assert np.array_equal(idx.astype(np.int64), oidx), name
+        np.testing.assert_allclose(wt, ow, rtol=2 ** -6, atol=0, err_msg=name)
+
+
+@pytest.mark.parametrize("T,d,E,k,seed", [(1000, 24, 16, 4, 11), (333, 1000, 64, 8, 12),
+                                          (4097, 1536, 128, 8, 13), (129, 40, 8, 8, 14)])
+def test_router_odd_shapes_exact(T, d, E, k, seed):
+    """d not a multiple of 16 (whole-row pass) or of 128 (a partial k-block in
+    each half), E below the kernel's 64 / 128 expert maximum, k = E."""
+    rng = np.random.default_rng(seed)
+    x = O.round_to_bf16(rng.standard_normal((T, d), dtype=np.float32))
+    w = O.round_to_bf16(rng.standard_normal((E, d), dtype=np.float32) * np.float32(0.02))
+    _check_against_oracle(x, w, None, k, True, "bf16")
