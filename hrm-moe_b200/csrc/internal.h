@@ -19,7 +19,11 @@ cudaError_t launch_router_topk(const void* x, const void* w_router, const void* 
 // router_tc.cu (bf16 only) -----------------------------------------------
 // Relative margin (of the token's largest |logit|) inside which a tensor-core
 // sum is treated as possibly rounding differently from the exact-order sum.
-constexpr float kRouterCertRel = 1.0f / 16384.0f;
+// Measured on B200 over nine shapes and value scales, the largest
+// |tensor-core sum - exact-order sum| was 0.13 of this margin (0.033 of a
+// four times wider one); tests/test_gpu_10_certification.py keeps it below
+// a quarter.
+constexpr float kRouterCertRel = 1.0f / 65536.0f;
 size_t router_tc_scratch_bytes(int64_t T);
 // sums_out (optional, diagnostic): the fp32 tensor-core sums [T, E] before
 // the bias, as the certification sees them.

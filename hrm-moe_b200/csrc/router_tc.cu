@@ -800,10 +800,13 @@ struct RrCfg {
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kStages = E <= 64 ? 3 : 4;       // E <= 64: two CTAs per SM
   static constexpr int kRingBytes = kStages * kStageBytes;
-  static constexpr int kLgStride = E + 1;
+  // floats per token row: E + 4 puts the 32 lanes of a routing warp (8
+  // tokens x 4 lanes, lane s reading expert s + 4i) in 32 different banks
+  static constexpr int kLgStride = E + 4;
   static constexpr int kLgBytes = 2 * RRT * kLgStride * 4;  // the two halves' sums
   static constexpr int kMainBytes = kRingBytes > kLgBytes ? kRingBytes : kLgBytes;
-  static constexpr size_t kSmem = 1024 + kMainBytes + 256;
+  static constexpr int kCtlBytes = 256;
+  static constexpr size_t kSmem = 1024 + kMainBytes + kCtlBytes;
   static_assert(kStageBytes % 1024 == 0, "stages keep the 1 KiB swizzle alignment");
   static_assert(kStages <= 8, "RtCtl holds eight stage barriers of each kind");
   static_assert(kSmem <= 232448, "shared memory budget");
@@ -832,6 +835,105 @@ __device__ __forceinline__ float key_value(uint32_t key) {
 
 __device__ __forceinline__ void named_barrier_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// Route token t on the 4 lanes (s = 0..3, mask gm) of its group.  The
+// logits are a0[e] (+ a1[e] when a1 is set: the two halves' sums), plus the
+// bias.  Lane s holds experts s, s+4, ...  delta_rel > 0: certified selection
+// against the bf16 values each logit could round to within delta_rel *
+// max|logit|, returning true when some order decision is not certain
+// (the caller lists the token for the fix-up); delta_rel = 0: the logits are
+// exact and every decision holds.  Writes topk_idx, the weights and (when
+// asked) the rounded logits; with `sums` also the unbiased sums.
+template <int E, int KMAX>
+__device__ __forceinline__ bool route4(const float* a0, const float* a1, const RtParams& p,
+                                       float delta_rel, int64_t t, int s, unsigned gm,
+                                       bool sums) {
+  constexpr int NE = E / 4;
+  const int En = p.E;
+  float v[NE];
+  float mag = 0.0f;
+#pragma unroll
+  for (int i = 0; i < NE; ++i) {
+    const int e = s + 4 * i;
+    float x = -INFINITY;  // experts past E: never picked (key 0 below)
+    if (e < En) {
+      x = a1 ? a0[e] + a1[e] : a0[e];
+      if (sums && p.sums_out) p.sums_out[t * En + e] = x;
+      if (p.bias) x = x + bf16_bits_to_f32(p.bias[e]);
+      if (isfinite(x)) mag = fmaxf(mag, fabsf(x));
+      if (p.logits_out) p.logits_out[t * En + e] = static_cast<uint16_t>(f32_to_bf16_bits(x));
+    }
+    v[i] = x;
+  }
+  mag = shfl4_maxf(mag, gm);
+  const float delta = delta_rel * mag;
+  // softmax over the rounded logits
+  float mx = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < NE; ++i) mx = fmaxf(mx, round_bf16(v[i]));
+  mx = shfl4_maxf(mx, gm);
+  float ssum = 0.0f;
+#pragma unroll
+  for (int i = 0; i < NE; ++i) ssum += expf(round_bf16(v[i]) - mx);
+  ssum = shfl4_sum(ssum, gm);
+  uint32_t key[NE], kmn[NE], kmx[NE];
+#pragma unroll
+  for (int i = 0; i < NE; ++i) {
+    key_range(v[i], delta, static_cast<uint32_t>(s + 4 * i), kmn[i], kmx[i], key[i]);
+    if (s + 4 * i >= En) key[i] = kmn[i] = kmx[i] = 0u;
+  }
+  uint32_t pk[KMAX];
+  bool bad = false;
+  uint32_t prev_min = 0;
+#pragma unroll
+  for (int r = 0; r < KMAX; ++r) {
+    pk[r] = 0;
+    if (r < p.k) {
+      uint32_t best = 0;
+#pragma unroll
+      for (int i = 0; i < NE; ++i) best = max(best, key[i]);
+      best = shfl4_max(best, gm);
+      uint32_t bmin = 0, bmax = 0;
+#pragma unroll
+      for (int i = 0; i < NE; ++i)
+        if (key[i] == best) { bmin = kmn[i]; bmax = kmx[i]; key[i] = 0; }
+      // only the owner lane found it: the others hold zeros
+      bmin = shfl4_max(bmin, gm);
+      bmax = shfl4_max(bmax, gm);
+      if (r > 0 && !(prev_min > bmax)) bad = true;
+      prev_min = bmin;
+      pk[r] = best;
+    }
+  }
+  uint32_t rest = 0;  // largest key an unpicked expert could take
+#pragma unroll
+  for (int i = 0; i < NE; ++i)
+    if (key[i] != 0) rest = max(rest, kmx[i]);
+  rest = shfl4_max(rest, gm);
+  if (!(prev_min > rest)) bad = true;
+  float pw[KMAX], ps = 0.0f;
+#pragma unroll
+  for (int r = 0; r < KMAX; ++r) {
+    pw[r] = 0.0f;
+    if (r < p.k) {
+      pw[r] = expf(key_value(pk[r]) - mx) / ssum;
+      ps += pw[r];
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < KMAX; ++r) {
+    if (r < p.k && (r & 3) == s) {
+      float w = p.norm ? pw[r] / fmaxf(ps, 1e-12f) : pw[r];
+      w = round_bf16(w);
+      const int64_t o = t * p.k + r;
+      p.topk_idx[o] = 0xFFFF - static_cast<int>(pk[r] & 0xFFFFu);
+      if (p.topk_w_f32) p.topk_w_f32[o] = w;
+      if (p.topk_w_dtype)
+        static_cast<uint16_t*>(p.topk_w_dtype)[o] = static_cast<uint16_t>(f32_to_bf16_bits(w));
+    }
+  }
+  return bad;
 }
 
 template <int E, int KMAX>  // E: the configuration's expert maximum (p.E <= E)
@@ -926,122 +1028,44 @@ router_rows_kernel(const __grid_constant__ CUtensorMap tmX2, const __grid_consta
     }
   } else {
     const int ew = warp - 2;
-    if (ew < 4) {
+    constexpr int kEpi = 32 * kRrEpiWarps;
+    // One warp waits (bounded) for the accumulator; the other seven block at
+    // a hardware named barrier meanwhile instead of spinning next to the
+    // producer and MMA warps.
+    if (ew == 0) {
+      const bool ok = mbar_wait_bounded(smem_u32(&ctl.acc_full), 0, abort, p.err, lim);
+      if (!ok && lane == 0) *abort = 1;
+    }
+    named_barrier_sync(1, kEpi);
+    tc_fence_after();
+    if (ew < 4 && !*abort) {
       // ---- TMEM readers: row r = 32 quad + lane is token r / 2, half r & 1
       const int quad = warp & 3;
-      const bool ok = mbar_wait_bounded(smem_u32(&ctl.acc_full), 0, abort, p.err, lim);
-      tc_fence_after();
-      if (ok) {
-        const int r = quad * 32 + lane;
-        float* dst = ((r & 1) ? lg1 : lg0) + (r >> 1) * C::kLgStride;
-        const uint32_t col0 = (r & 1) ? E : 0;  // this half's useful columns
+      const int r = quad * 32 + lane;
+      float* dst = ((r & 1) ? lg1 : lg0) + (r >> 1) * C::kLgStride;
+      const uint32_t col0 = (r & 1) ? E : 0;  // this half's useful columns
 #pragma unroll 1
-        for (int c = 0; c < E / 32; ++c) {
-          uint32_t ra[32], rb[32];
-          tmem_ld_32cols(tmem + (static_cast<uint32_t>(quad * 32) << 16) + c * 32, ra);
-          tmem_ld_32cols(tmem + (static_cast<uint32_t>(quad * 32) << 16) + E + c * 32, rb);
-          tc_wait_ld();
+      for (int c = 0; c < E / 32; ++c) {
+        uint32_t ra[32], rb[32];
+        tmem_ld_32cols(tmem + (static_cast<uint32_t>(quad * 32) << 16) + c * 32, ra);
+        tmem_ld_32cols(tmem + (static_cast<uint32_t>(quad * 32) << 16) + E + c * 32, rb);
+        tc_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) dst[c * 32 + i] = __uint_as_float(col0 ? rb[i] : ra[i]);
-        }
+        for (int i = 0; i < 32; ++i) dst[c * 32 + i] = __uint_as_float(col0 ? rb[i] : ra[i]);
       }
-      tc_fence_before();
     }
-    named_barrier_sync(1, 32 * kRrEpiWarps);
+    tc_fence_before();
+    named_barrier_sync(1, kEpi);
     // ---- routing: token j on lanes 4 (j % 8) .. +3 of warp j / 8
-    const int j = ew * 8 + (lane >> 2), s = lane & 3;
-    const unsigned gm = 0xFu << (lane & 28);  // this token's four lanes
-    const int64_t t = t0 + j;
-    if (!*abort && t < p.T) {  // uniform over the 4 lanes of a token
-      const float* a0 = lg0 + j * C::kLgStride;
-      const float* a1 = lg1 + j * C::kLgStride;
-      const int En = p.E;
-      float v[NE];
-      float mag = 0.0f;
-#pragma unroll
-      for (int i = 0; i < NE; ++i) {
-        const int e = s + 4 * i;
-        float x = -INFINITY;  // experts past E: never picked (key 0 below)
-        if (e < En) {
-          x = a0[e] + a1[e];
-          if (p.sums_out) p.sums_out[t * En + e] = x;
-          if (p.bias) x = x + bf16_bits_to_f32(p.bias[e]);
-          if (isfinite(x)) mag = fmaxf(mag, fabsf(x));
-          if (p.logits_out)
-            p.logits_out[t * En + e] = static_cast<uint16_t>(f32_to_bf16_bits(x));
-        }
-        v[i] = x;
-      }
-      mag = shfl4_maxf(mag, gm);
-      const float delta = p.cert_rel * mag;
-      // softmax over the rounded logits
-      float mx = -INFINITY;
-#pragma unroll
-      for (int i = 0; i < NE; ++i) mx = fmaxf(mx, round_bf16(v[i]));
-      mx = shfl4_maxf(mx, gm);
-      float ssum = 0.0f;
-#pragma unroll
-      for (int i = 0; i < NE; ++i) ssum += expf(round_bf16(v[i]) - mx);
-      ssum = shfl4_sum(ssum, gm);
-      uint32_t key[NE], kmn[NE], kmx[NE];
-#pragma unroll
-      for (int i = 0; i < NE; ++i) {
-        key_range(v[i], delta, static_cast<uint32_t>(s + 4 * i), kmn[i], kmx[i], key[i]);
-        if (s + 4 * i >= En) key[i] = kmn[i] = kmx[i] = 0u;
-      }
-      uint32_t pk[KMAX];
-      bool bad = false;
-      uint32_t prev_min = 0;
-#pragma unroll
-      for (int r = 0; r < KMAX; ++r) {
-        pk[r] = 0;
-        if (r < p.k) {
-          uint32_t best = 0;
-#pragma unroll
-          for (int i = 0; i < NE; ++i) best = max(best, key[i]);
-          best = shfl4_max(best, gm);
-          uint32_t bmin = 0, bmax = 0;
-#pragma unroll
-          for (int i = 0; i < NE; ++i)
-            if (key[i] == best) { bmin = kmn[i]; bmax = kmx[i]; key[i] = 0; }
-          // only the owner lane found it: the others hold zeros
-          bmin = shfl4_max(bmin, gm);
-          bmax = shfl4_max(bmax, gm);
-          if (r > 0 && !(prev_min > bmax)) bad = true;
-          prev_min = bmin;
-          pk[r] = best;
-        }
-      }
-      uint32_t rest = 0;  // largest key an unpicked expert could take
-#pragma unroll
-      for (int i = 0; i < NE; ++i)
-        if (key[i] != 0) rest = max(rest, kmx[i]);
-      rest = shfl4_max(rest, gm);
-      if (!(prev_min > rest)) bad = true;
-      float pw[KMAX], ps = 0.0f;
-#pragma unroll
-      for (int r = 0; r < KMAX; ++r) {
-        pw[r] = 0.0f;
-        if (r < p.k) {
-          pw[r] = expf(key_value(pk[r]) - mx) / ssum;
-          ps += pw[r];
-        }
-      }
-#pragma unroll
-      for (int r = 0; r < KMAX; ++r) {
-        if (r < p.k && (r & 3) == s) {
-          float w = p.norm ? pw[r] / fmaxf(ps, 1e-12f) : pw[r];
-          w = round_bf16(w);
-          const int64_t o = t * p.k + r;
-          p.topk_idx[o] = 0xFFFF - static_cast<int>(pk[r] & 0xFFFFu);
-          if (p.topk_w_f32) p.topk_w_f32[o] = w;
-          if (p.topk_w_dtype)
-            static_cast<uint16_t*>(p.topk_w_dtype)[o] = static_cast<uint16_t>(f32_to_bf16_bits(w));
-        }
-      }
-      if (bad && s == 0) {
-        const int slot = atomicAdd(p.fix_count, 1);
-        p.fix_list[slot] = static_cast<int32_t>(t);
+    const bool live = !*abort;
+    {
+      const int j = ew * 8 + (lane >> 2), s = lane & 3;
+      const unsigned gm = 0xFu << (lane & 28);  // this token's four lanes
+      const int64_t t = t0 + j;
+      if (live && t < p.T) {  // uniform over the 4 lanes of a token
+        const bool bad = route4<E, KMAX>(lg0 + j * C::kLgStride, lg1 + j * C::kLgStride, p,
+                                         p.cert_rel, t, s, gm, true);
+        if (bad && s == 0) p.fix_list[atomicAdd(p.fix_count, 1)] = static_cast<int32_t>(t);
       }
     }
   }
@@ -1065,6 +1089,9 @@ bool map_half_rows(CUtensorMap* m, const void* base, uint64_t T, uint64_t d) {
              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
+
+// The row-split pass needs 16-byte aligned halves of each row.
+inline bool rows_pass_fits(int d) { return d % 16 == 0; }
 
 // HMOE_ROUTER_WHOLE_ROWS=1 (read once per process) keeps the 128-token
 // whole-row kernel for every d, so tests can compare the two passes.
@@ -1149,7 +1176,7 @@ cudaError_t launch_tc(const void* x, const void* w, const RtParams& p, cudaStrea
   // the tensor-core pass: 64-token CTAs over the two halves of each row when
   // d splits into 16-byte aligned halves (router_rows_kernel), else 128-token
   // CTAs over whole rows
-  if (p.d % 16 == 0 && !router_whole_rows_forced())
+  if (rows_pass_fits(p.d) && !router_whole_rows_forced())
     e = launch_rows_tc<EPAD, KMAX>(x, w, p, st);
   else
     router_tc_kernel<EPAD, KMAX><<<static_cast<unsigned>(cdiv64(p.T, RBM)), kRtThreads, C::kSmem,
@@ -1164,7 +1191,8 @@ cudaError_t launch_tc(const void* x, const void* w, const RtParams& p, cudaStrea
   // whole weight in shared memory is faster.
   const int n_eg = cdiv(p.E, kSplitE);
   const int sms = num_sms_for_current_device();
-  const int64_t want = cdiv64(p.T, 128);
+  // expected fix list: under 1% of the tokens at the margin in use, four per group
+  const int64_t want = cdiv64(p.T, 512);
   const int cap = (4 * sms) / n_eg > 1 ? (4 * sms) / n_eg : 1;
   const size_t wsm_smem = 1024 + static_cast<size_t>(nb) * 8192 +
                           sizeof(float) * (static_cast<size_t>(kFixSmG) * p.d + kFixSmG * 64);

@@ -4,14 +4,15 @@ The bf16 router takes each logit from the tensor cores, whose fp32
 accumulation order differs from the fixed order that defines the routing
 (one fma per k within 64-wide blocks, blocks added in order).  A logit is
 trusted to round like the fixed-order sum unless it lies within
-margin = cert_rel * max|logit of the token| (cert_rel = 2^-14) of a bf16
+margin = cert_rel * max|logit of the token| (cert_rel = 2^-16) of a bf16
 rounding midpoint; tokens with any untrusted order decision are recomputed
 in the fixed order.  The margin is not a worst-case bound, so this test
 measures what it protects against: over many seeds, token counts, shapes
 and value scales it compares the tensor-core sums (hmoe_router_topk_sums)
 with the fixed-order fp32 sums of the oracle and records, for every logit,
-|tc - exact| / margin.  The largest ratio seen must stay below 1/8, and the
-routing must be the fixed-order routing on every token.
+|tc - exact| / margin.  The largest ratio seen must stay below 1/4 (the
+margin covers four times the worst error measured), and the routing must be
+the fixed-order routing on every token.
 """
 import ctypes
 import importlib
@@ -25,8 +26,8 @@ from oracle import moe_oracle as O
 
 pytestmark = pytest.mark.gpu
 
-CERT_REL = 2.0 ** -14
-RATIO_LIMIT = 1.0 / 8
+CERT_REL = 2.0 ** -16
+RATIO_LIMIT = 1.0 / 4
 
 CASES = [
     # (T, d, E, k, x scale, w scale, seed, quantised weights)
