@@ -4,7 +4,9 @@
 //   expert_output = expert_output * sorted_weights[:, None]      # layer dtype
 //   final_hidden_states.index_add_(0, sorted_token_idx, expert_output)
 // as a gather instead of a scatter: one warp per token reads the k rows
-// pos(t, 0..k-1) of the expert-sorted output.  The arithmetic follows the
+// pos(t, 0..k-1) of the expert-sorted output (SPLIT: small T, where one warp
+// per token leaves too few loads in flight, one warp per (token, block of 32
+// 16-byte columns)).  The arithmetic follows the
 // reference step by step: each product w * y is rounded to the layer dtype,
 // and the products are added into the accumulator one at a time, each sum
 // rounded, in ascending sorted position -- the order index_add_ visits a
@@ -19,13 +21,17 @@ namespace {
 constexpr int kCombThreads = 256;
 constexpr int kMaxK = 32;
 
-template <bool BF16>
+template <bool BF16, bool SPLIT>
 __global__ void __launch_bounds__(kCombThreads)
 combine_kernel(const void* __restrict__ expert_out, const int32_t* __restrict__ pos,
                const void* __restrict__ topk_w, int topk_w_is_f32, int64_t T, int row_chunks,
                int k, const void* __restrict__ final_in, void* __restrict__ out) {
   const int lane = threadIdx.x & 31;
-  const int64_t t = static_cast<int64_t>(blockIdx.x) * (kCombThreads / 32) + (threadIdx.x >> 5);
+  const int64_t wid = static_cast<int64_t>(blockIdx.x) * (kCombThreads / 32) + (threadIdx.x >> 5);
+  const int ncb = SPLIT ? (row_chunks + 31) / 32 : 1;  // warps per token
+  const int64_t t = SPLIT ? wid / ncb : wid;
+  const int cfirst = SPLIT ? static_cast<int>(wid - t * ncb) * 32 : 0;
+  const int cend = SPLIT ? cfirst + 32 : row_chunks;
   if (t >= T) return;
   int p = -1;
   float w = 0.0f;
@@ -62,7 +68,7 @@ combine_kernel(const void* __restrict__ expert_out, const int32_t* __restrict__ 
   constexpr int EPC = BF16 ? 8 : 4;  // elements per 16-byte chunk
   constexpr int kBatch = 4;          // rows loaded before they are summed
   // every lane runs the same trip count so the shuffles below see all 32 lanes
-  for (int c0 = 0; c0 < row_chunks; c0 += 32) {
+  for (int c0 = cfirst; c0 < cend; c0 += 32) {
     const int c = c0 + lane;
     const bool live = c < row_chunks;
     float acc[EPC];
@@ -140,15 +146,22 @@ cudaError_t launch_combine(const void* expert_out, const int32_t* pos, const voi
   if (k > kMaxK) return cudaErrorInvalidValue;
   const bool bf16 = dtype == kDtypeBF16;
   const int row_chunks = d * (bf16 ? 2 : 4) / 16;
-  const unsigned blocks = static_cast<unsigned>(cdiv64(T, kCombThreads / 32));
-  if (bf16)
-    combine_kernel<true><<<blocks, kCombThreads, 0, stream>>>(expert_out, pos, topk_w,
-                                                              topk_w_is_f32, T, row_chunks, k,
-                                                              final_in, out);
+  // small T: a row over several warps, so that enough loads are in flight
+  const bool split = T < 4096;
+  const unsigned blocks = static_cast<unsigned>(
+      cdiv64(T * (split ? cdiv(row_chunks, 32) : 1), kCombThreads / 32));
+  if (bf16 && split)
+    combine_kernel<true, true><<<blocks, kCombThreads, 0, stream>>>(
+        expert_out, pos, topk_w, topk_w_is_f32, T, row_chunks, k, final_in, out);
+  else if (bf16)
+    combine_kernel<true, false><<<blocks, kCombThreads, 0, stream>>>(
+        expert_out, pos, topk_w, topk_w_is_f32, T, row_chunks, k, final_in, out);
+  else if (split)
+    combine_kernel<false, true><<<blocks, kCombThreads, 0, stream>>>(
+        expert_out, pos, topk_w, topk_w_is_f32, T, row_chunks, k, final_in, out);
   else
-    combine_kernel<false><<<blocks, kCombThreads, 0, stream>>>(expert_out, pos, topk_w,
-                                                               topk_w_is_f32, T, row_chunks, k,
-                                                               final_in, out);
+    combine_kernel<false, false><<<blocks, kCombThreads, 0, stream>>>(
+        expert_out, pos, topk_w, topk_w_is_f32, T, row_chunks, k, final_in, out);
   return cudaGetLastError();
 }
 

@@ -29,7 +29,7 @@ constexpr int kMaxExperts = 128;
 __global__ void __launch_bounds__(kHistThreads)
 hist_rank_kernel(const int32_t* __restrict__ topk_idx, int64_t T, int k, int E, int tblk,
                  int32_t* __restrict__ local_rank, int32_t* __restrict__ block_counts,
-                 int* __restrict__ err) {
+                 int* __restrict__ err, int32_t* __restrict__ single_counts) {
   __shared__ int32_t cnt[kHistChunks][kMaxExperts];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t f0 = static_cast<int64_t>(blockIdx.x) * tblk * k;  // first flat index
@@ -69,7 +69,13 @@ hist_rank_kernel(const int32_t* __restrict__ topk_idx, int64_t T, int k, int E, 
       cnt[c][tid] = run;
       run += v;
     }
-    block_counts[static_cast<int64_t>(blockIdx.x) * E + tid] = run;
+    if (single_counts) {
+      // the only block: what the scan would produce (offset 0, total)
+      block_counts[tid] = 0;
+      single_counts[tid] = run;
+    } else {
+      block_counts[static_cast<int64_t>(blockIdx.x) * E + tid] = run;
+    }
   }
   __syncthreads();
 #pragma unroll
@@ -237,7 +243,7 @@ cudaError_t launch_hist_rank(const int32_t* topk_idx, int64_t T, int k, int E,
   const int tblk = dispatch_block_tokens(k);
   const int64_t nblk = dispatch_num_blocks(T, k);
   hist_rank_kernel<<<static_cast<unsigned>(nblk), kHistThreads, 0, stream>>>(
-      topk_idx, T, k, E, tblk, local_rank, block_counts, err);
+      topk_idx, T, k, E, tblk, local_rank, block_counts, err, nullptr);
   return cudaGetLastError();
 }
 
@@ -245,6 +251,20 @@ cudaError_t launch_scan(int32_t* block_counts, int64_t nblk, int E, int32_t* cou
                         int32_t* /*expert_offsets*/, cudaStream_t stream) {
   scan_kernel<<<E, kScanThreads, 0, stream>>>(block_counts, nblk, E, counts);
   return cudaGetLastError();
+}
+
+cudaError_t launch_hist_scan(const int32_t* topk_idx, int64_t T, int k, int E,
+                             int32_t* local_rank, int32_t* block_counts, int32_t* counts, int* err,
+                             cudaStream_t stream) {
+  if (T == 0) return cudaSuccess;
+  const int tblk = dispatch_block_tokens(k);
+  const int64_t nblk = dispatch_num_blocks(T, k);
+  // one histogram block (small T): it writes the counts itself, no scan launch
+  hist_rank_kernel<<<static_cast<unsigned>(nblk), kHistThreads, 0, stream>>>(
+      topk_idx, T, k, E, tblk, local_rank, block_counts, err, nblk == 1 ? counts : nullptr);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess || nblk == 1) return e;
+  return launch_scan(block_counts, nblk, E, counts, nullptr, stream);
 }
 
 cudaError_t launch_permute_gather(const int32_t* topk_idx, const int32_t* local_rank,

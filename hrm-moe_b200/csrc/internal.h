@@ -46,6 +46,11 @@ cudaError_t launch_hist_rank(const int32_t* topk_idx, int64_t T, int k, int E,
 // (expert_offsets is unused and may be null.)
 cudaError_t launch_scan(int32_t* block_counts, int64_t nblk, int E, int32_t* counts,
                         int32_t* expert_offsets, cudaStream_t stream);
+// hist_rank then scan (the scan is folded into hist_rank when T fits one
+// histogram block): local_rank, block offsets and counts[E].
+cudaError_t launch_hist_scan(const int32_t* topk_idx, int64_t T, int k, int E,
+                             int32_t* local_rank, int32_t* block_counts, int32_t* counts, int* err,
+                             cudaStream_t stream);
 // pos[T*k] and (optionally) sort_idx, sorted_token, sorted weights, x_sorted.
 cudaError_t launch_permute_gather(const int32_t* topk_idx, const int32_t* local_rank,
                                   const int32_t* block_offsets, const int32_t* counts,
