@@ -40,6 +40,17 @@ constexpr int RBM = 128;       // tokens per CTA (MMA M)
 constexpr int RBK = 64;        // bf16 per 128-byte swizzled row
 constexpr int kRtThreads = 192;
 
+// Position of expert e in a token's logits row: 4 floats of padding after
+// every 32, so that the lanes routing a warp's tokens (4 or 8 per token,
+// each reading its own run of experts as 16-byte vectors) meet 32 different
+// banks.  Rows are LgRow<E>::kStride floats apart (E + E/8).
+__host__ __device__ constexpr int lg_idx(int e) { return e + 4 * (e >> 5); }
+template <int E>
+struct LgRow {
+  static constexpr int kStride = E + E / 8;
+};
+
+
 template <int EPAD>
 struct RCfg {
   static constexpr int kStages = EPAD == 64 ? 6 : 4;
@@ -800,9 +811,7 @@ struct RrCfg {
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kStages = E <= 64 ? 3 : 4;       // E <= 64: two CTAs per SM
   static constexpr int kRingBytes = kStages * kStageBytes;
-  // floats per token row: E + 4 puts the 32 lanes of a routing warp (8
-  // tokens x 4 lanes, lane s reading expert s + 4i) in 32 different banks
-  static constexpr int kLgStride = E + 4;
+  static constexpr int kLgStride = LgRow<E>::kStride;  // floats per token row (lg_idx)
   static constexpr int kLgBytes = 2 * RRT * kLgStride * 4;  // the two halves' sums
   static constexpr int kMainBytes = kRingBytes > kLgBytes ? kRingBytes : kLgBytes;
   static constexpr int kCtlBytes = 256;
@@ -812,128 +821,321 @@ struct RrCfg {
   static_assert(kSmem <= 232448, "shared memory budget");
 };
 
-// Reductions over the 4 lanes of one token.  `gm` names exactly those four
-// lanes: a warp's other tokens may be past T and not take part.
-__device__ __forceinline__ uint32_t shfl4_max(uint32_t v, unsigned gm) {
-  v = max(v, __shfl_xor_sync(gm, v, 1));
-  return max(v, __shfl_xor_sync(gm, v, 2));
+// Reductions over the L lanes of one token (xor 1, 2, ...).  Every lane of
+// the warp executes them together.
+template <int L>
+__device__ __forceinline__ uint32_t grp_max(uint32_t v) {
+#pragma unroll
+  for (int o = 1; o < L; o <<= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
 }
-__device__ __forceinline__ float shfl4_maxf(float v, unsigned gm) {
-  v = fmaxf(v, __shfl_xor_sync(gm, v, 1));
-  return fmaxf(v, __shfl_xor_sync(gm, v, 2));
+template <int L>
+__device__ __forceinline__ float grp_maxf(float v) {
+#pragma unroll
+  for (int o = 1; o < L; o <<= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
 }
-__device__ __forceinline__ float shfl4_sum(float v, unsigned gm) {
-  v += __shfl_xor_sync(gm, v, 1);
-  return v + __shfl_xor_sync(gm, v, 2);
+template <int L>
+__device__ __forceinline__ float grp_sum(float v) {
+#pragma unroll
+  for (int o = 1; o < L; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Routing keys.  A logit's key orders experts by rounded value, then by
+// ascending index, and carries the rounding range of the exact-order sum:
+// bits [16, 32) the order-preserving image (ob16) of the rounded value,
+// [3, 10) 127 - e, bit 2 "wide" (the exact sum may round more than one step
+// away), bit 1 "may round one step up", bit 0 "one step down".  Any lane can
+// then tell a pick's range from its key alone.
+constexpr uint32_t kKeyDn = 1u, kKeyUp = 2u, kKeyWide = 4u;
+
+__device__ __forceinline__ float ob_value(uint32_t ob) {
+  return bf16_bits_to_f32((ob & 0x8000u) ? (ob & 0x7FFFu) : (~ob & 0xFFFFu));
 }
 // bf16 value (as fp32) of an order-preserving key
-__device__ __forceinline__ float key_value(uint32_t key) {
-  const uint32_t ob = key >> 16;
-  const uint32_t b = (ob & 0x8000u) ? (ob & 0x7FFFu) : (~ob & 0xFFFFu);
-  return bf16_bits_to_f32(b);
+__device__ __forceinline__ float key_value(uint32_t key) { return ob_value(key >> 16); }
+__device__ __forceinline__ int key_expert(uint32_t key) { return 127 - static_cast<int>((key >> 3) & 127u); }
+
+// Key of logit v (tensor-core sum, bias included) of expert e, with margin
+// delta: the exact-order sum lies in [v - delta, v + delta] (ends rounded
+// outward), so its bf16 rounding lies between the roundings of the two ends.
+// Where |v| >= 1024 delta, the gap to either bf16 neighbour is at least
+// 2 delta, so that rounding is the value itself or one neighbour; smaller
+// logits whose rounding is not certain are marked wide.  Branch-free: the
+// routing runs it for every logit.
+__device__ __forceinline__ uint32_t logit_key(float v, float delta, float wide_below, uint32_t e) {
+  const uint32_t b = f32_to_bf16_bits(v);
+  const uint32_t lh = cvt_bf16x2(__fsub_rd(v, delta), __fadd_ru(v, delta));
+  const uint32_t dn = (lh & 0xFFFFu) != b ? 1u : 0u;
+  const uint32_t up = (lh >> 16) != b ? 1u : 0u;
+  const uint32_t fl = (dn | up) && fabsf(v) < wide_below ? kKeyWide : (dn | (up << 1));
+  return (ob16(b) << 16) | ((127u - e) << 3) | fl;
+}
+// Smallest / largest key the exact-order sum of this logit could take.  A
+// wide logit rounded to r came from a sum between r's neighbours, so its
+// exact sum lies within delta of that interval.  WIDE = false: the caller
+// knows that no key of the token is wide.
+template <bool WIDE = true>
+__device__ __forceinline__ uint32_t key_min(uint32_t key, float delta) {
+  if (WIDE && (key & kKeyWide)) {
+    const uint32_t ob = key >> 16;
+    const float lo = __fsub_rd(ob_value(ob > 0u ? ob - 1u : ob), delta);
+    return (ob16(f32_to_bf16_bits(lo)) << 16) | (key & 0xFFFFu);
+  }
+  return key - ((key & kKeyDn) << 16);
+}
+template <bool WIDE = true>
+__device__ __forceinline__ uint32_t key_max(uint32_t key, float delta) {
+  if (WIDE && (key & kKeyWide)) {
+    const uint32_t ob = key >> 16;
+    const float hi = __fadd_ru(ob_value(ob < 0xFFFFu ? ob + 1u : ob), delta);
+    return (ob16(f32_to_bf16_bits(hi)) << 16) | (key & 0xFFFFu);
+  }
+  return key + ((key & kKeyUp) << 15);
+}
+
+// Certification of a selection: each pick's smallest key beats the next
+// pick's largest, and the last pick's beats every unpicked expert's largest
+// (rest: the lane's unpicked keys, 0 for picked or absent ones).  Returns
+// true when some decision is not certain; lmin = the smallest pick key.
+template <bool WIDE, int L, int KMAX, int NE>
+__device__ __forceinline__ bool certify(const uint32_t (&pk)[KMAX], const uint32_t (&rest)[NE],
+                                        int k, float delta, uint32_t& lmin) {
+  bool bad = false;
+  uint32_t last_min = 0;
+  lmin = 0xFFFFFFFFu;
+#pragma unroll
+  for (int r = 0; r < KMAX; ++r) {
+    if (r < k) {
+      const uint32_t mn = key_min<WIDE>(pk[r], delta);
+      lmin = min(lmin, mn);
+      last_min = mn;
+      if (r + 1 < k) bad |= !(mn > key_max<WIDE>(pk[r + 1], delta));
+    }
+  }
+  uint32_t rmax = 0;
+#pragma unroll
+  for (int i = 0; i < NE; ++i) rmax = max(rmax, key_max<WIDE>(rest[i], delta));
+  rmax = grp_max<L>(rmax);
+  return bad || !(last_min > rmax);
 }
 
 __device__ __forceinline__ void named_barrier_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
-// Route token t on the 4 lanes (s = 0..3, mask gm) of its group.  The
-// logits are a0[e] (+ a1[e] when a1 is set: the two halves' sums), plus the
-// bias.  Lane s holds experts s, s+4, ...  delta_rel > 0: certified selection
-// against the bf16 values each logit could round to within delta_rel *
-// max|logit|, returning true when some order decision is not certain
-// (the caller lists the token for the fix-up); delta_rel = 0: the logits are
-// exact and every decision holds.  Writes topk_idx, the weights and (when
-// asked) the rounded logits; with `sums` also the unbiased sums.
-template <int E, int KMAX>
-__device__ __forceinline__ bool route4(const float* a0, const float* a1, const RtParams& p,
-                                       float delta_rel, int64_t t, int s, unsigned gm,
-                                       bool sums) {
-  constexpr int NE = E / 4;
+// What route_tok found out about a token whose order decisions were not all
+// certain: the margin in use and the smallest key any pick could take.
+struct RouteCert {
+  float delta;
+  uint32_t lmin;
+};
+
+// Bitonic sort of N keys into descending order (registers, unrolled).
+template <int N>
+__device__ __forceinline__ void sort_desc(uint32_t (&a)[N]) {
+#pragma unroll
+  for (int size = 2; size <= N; size <<= 1) {
+#pragma unroll
+    for (int stride = size / 2; stride > 0; stride >>= 1) {
+#pragma unroll
+      for (int i = 0; i < N; ++i) {
+        const int j = i ^ stride;
+        if (j > i) {
+          const uint32_t x = a[i], y = a[j];
+          const bool desc = (i & size) == 0 || size == N;
+          a[i] = desc ? max(x, y) : min(x, y);
+          a[j] = desc ? min(x, y) : max(x, y);
+        }
+      }
+    }
+  }
+}
+// a: this lane's N largest keys, descending.  After the call every lane of
+// the L-lane group holds the group's N largest keys, descending: at each
+// level a lane and its partner keep the larger half of their two lists
+// (max of a[i] and the partner's a[N-1-i] is a bitonic sequence holding
+// them), then sort it with a bitonic merge.
+template <int N, int L>
+__device__ __forceinline__ void group_top(uint32_t (&a)[N]) {
+#pragma unroll
+  for (int o = 1; o < L; o <<= 1) {
+    uint32_t b[N];
+#pragma unroll
+    for (int i = 0; i < N; ++i) b[i] = __shfl_xor_sync(0xffffffffu, a[i], o);
+#pragma unroll
+    for (int i = 0; i < N; ++i) a[i] = max(a[i], b[N - 1 - i]);
+#pragma unroll
+    for (int stride = N / 2; stride > 0; stride >>= 1) {
+#pragma unroll
+      for (int i = 0; i < N; ++i) {
+        const int j = i ^ stride;
+        if (j > i) {
+          const uint32_t x = a[i], y = a[j];
+          a[i] = max(x, y);
+          a[j] = min(x, y);
+        }
+      }
+    }
+  }
+}
+
+// Route token t on the L lanes (s = 0..L-1) of its group; lane s holds
+// experts [s E/L, (s+1) E/L).  The logits are a0[lg_idx(e)] (+ a1[...] when
+// a1 is set: the two halves' sums), plus the bias.  Every lane of the warp
+// calls it together (the group reductions are full-warp shuffles); lanes
+// whose token is past the end pass live = false and write nothing.
+// delta_rel > 0: certified selection against the bf16 values each logit
+// could round to within delta_rel * max|logit|, returning true when some
+// order decision is not certain (each pick against the next, the last pick
+// against every unpicked expert); delta_rel = 0: the logits are exact and
+// every decision holds.  The k picks are found on plain keys (one group
+// maximum each); the ranges ride in the keys, so the certification needs no
+// further exchange.  Writes topk_idx, the weights and (when asked) the
+// rounded logits; with `sums` also the unbiased sums; with `cert` the margin
+// and the smallest pick key.
+template <int E, int KMAX, int L, bool KFIX = false>
+__device__ __forceinline__ bool route_tok(const float* a0, const float* a1, const RtParams& p,
+                                          float delta_rel, int64_t t, int s, bool live, bool sums,
+                                          RouteCert* cert = nullptr) {
+  constexpr int NE = E / L;
+  static_assert(NE % 4 == 0 && KMAX % L == 0, "lane shares");
   const int En = p.E;
+  const int k = KFIX ? KMAX : p.k;  // KFIX: the caller knows k == KMAX
+  const int e0 = NE * s;
+  const bool full = e0 + NE <= En;  // every expert of this lane exists
   float v[NE];
+#pragma unroll
+  for (int q = 0; q < NE / 4; ++q) {
+    float4 u = *reinterpret_cast<const float4*>(a0 + lg_idx(e0 + 4 * q));
+    if (a1) {
+      const float4 u1 = *reinterpret_cast<const float4*>(a1 + lg_idx(e0 + 4 * q));
+      u.x = u.x + u1.x;
+      u.y = u.y + u1.y;
+      u.z = u.z + u1.z;
+      u.w = u.w + u1.w;
+    }
+    v[4 * q] = u.x;
+    v[4 * q + 1] = u.y;
+    v[4 * q + 2] = u.z;
+    v[4 * q + 3] = u.w;
+  }
+  if (sums && p.sums_out && live) {
+#pragma unroll
+    for (int i = 0; i < NE; ++i)
+      if (e0 + i < En) p.sums_out[t * En + e0 + i] = v[i];
+  }
+  if (p.bias) {
+#pragma unroll
+    for (int i = 0; i < NE; ++i) v[i] = v[i] + bf16_bits_to_f32(p.bias[e0 + i < En ? e0 + i : 0]);
+  }
+  if (!full) {  // experts past E: never picked (key 0 below)
+#pragma unroll
+    for (int i = 0; i < NE; ++i) v[i] = e0 + i < En ? v[i] : -INFINITY;
+  }
+  if (p.logits_out && live) {
+#pragma unroll
+    for (int i = 0; i < NE; ++i)
+      if (e0 + i < En) p.logits_out[t * En + e0 + i] = static_cast<uint16_t>(f32_to_bf16_bits(v[i]));
+  }
   float mag = 0.0f;
 #pragma unroll
-  for (int i = 0; i < NE; ++i) {
-    const int e = s + 4 * i;
-    float x = -INFINITY;  // experts past E: never picked (key 0 below)
-    if (e < En) {
-      x = a1 ? a0[e] + a1[e] : a0[e];
-      if (sums && p.sums_out) p.sums_out[t * En + e] = x;
-      if (p.bias) x = x + bf16_bits_to_f32(p.bias[e]);
-      if (isfinite(x)) mag = fmaxf(mag, fabsf(x));
-      if (p.logits_out) p.logits_out[t * En + e] = static_cast<uint16_t>(f32_to_bf16_bits(x));
-    }
-    v[i] = x;
-  }
-  mag = shfl4_maxf(mag, gm);
+  for (int i = 0; i < NE; ++i) mag = fmaxf(mag, isfinite(v[i]) ? fabsf(v[i]) : 0.0f);
+  mag = grp_maxf<L>(mag);
   const float delta = delta_rel * mag;
-  // softmax over the rounded logits
-  float mx = -INFINITY;
+  const float wide_below = 1024.0f * delta;
+  uint32_t key[NE], wide = 0;
 #pragma unroll
-  for (int i = 0; i < NE; ++i) mx = fmaxf(mx, round_bf16(v[i]));
-  mx = shfl4_maxf(mx, gm);
+  for (int i = 0; i < NE; ++i) {
+    key[i] = logit_key(v[i], delta, wide_below, static_cast<uint32_t>(e0 + i));
+    if (!full) key[i] = e0 + i < En ? key[i] : 0u;
+    wide |= key[i];
+  }
+  // the KMAX largest keys of the token on every lane of its group: each
+  // lane sorts its own (zeros pad a short list), then the group merges
+  constexpr int NS = NE > KMAX ? NE : KMAX;
+  uint32_t srt[NS];
+#pragma unroll
+  for (int i = 0; i < NS; ++i) srt[i] = i < NE ? key[i] : 0u;
+  sort_desc<NS>(srt);
+  uint32_t pk[KMAX];
+#pragma unroll
+  for (int r = 0; r < KMAX; ++r) pk[r] = srt[r];
+  group_top<KMAX, L>(pk);
+  // unpicked keys: the lane's keys below the k-th pick (keys are distinct)
+  uint32_t kth = pk[0];
+#pragma unroll
+  for (int r = 1; r < KMAX; ++r) kth = r < k ? pk[r] : kth;
+#pragma unroll
+  for (int i = 0; i < NE; ++i) key[i] = key[i] < kth ? key[i] : 0u;
+  // softmax over the rounded logits; the largest is the first pick's value
+  const float mx = key_value(pk[0]);
   float ssum = 0.0f;
 #pragma unroll
-  for (int i = 0; i < NE; ++i) ssum += expf(round_bf16(v[i]) - mx);
-  ssum = shfl4_sum(ssum, gm);
-  uint32_t key[NE], kmn[NE], kmx[NE];
-#pragma unroll
-  for (int i = 0; i < NE; ++i) {
-    key_range(v[i], delta, static_cast<uint32_t>(s + 4 * i), kmn[i], kmx[i], key[i]);
-    if (s + 4 * i >= En) key[i] = kmn[i] = kmx[i] = 0u;
+  for (int i = 0; i < NE; ++i) ssum += __expf(round_bf16(v[i]) - mx);
+  ssum = grp_sum<L>(ssum);
+  // certification; the exact form for wide ranges only where the warp has one
+  uint32_t lmin;
+  const bool bad = __any_sync(0xffffffffu, (wide & kKeyWide) != 0u)
+                       ? certify<true, L>(pk, key, k, delta, lmin)
+                       : certify<false, L>(pk, key, k, delta, lmin);
+  if (cert) {
+    cert->delta = delta;
+    cert->lmin = lmin;
   }
-  uint32_t pk[KMAX];
-  bool bad = false;
-  uint32_t prev_min = 0;
+  // weights: lane s takes picks s, s+L, ...; every lane then adds the k
+  // probabilities in pick order
+  uint32_t mk[KMAX / L];
+  float pw[KMAX / L];
 #pragma unroll
-  for (int r = 0; r < KMAX; ++r) {
-    pk[r] = 0;
-    if (r < p.k) {
-      uint32_t best = 0;
+  for (int j = 0; j < KMAX / L; ++j) {
+    mk[j] = pk[L * j];
 #pragma unroll
-      for (int i = 0; i < NE; ++i) best = max(best, key[i]);
-      best = shfl4_max(best, gm);
-      uint32_t bmin = 0, bmax = 0;
-#pragma unroll
-      for (int i = 0; i < NE; ++i)
-        if (key[i] == best) { bmin = kmn[i]; bmax = kmx[i]; key[i] = 0; }
-      // only the owner lane found it: the others hold zeros
-      bmin = shfl4_max(bmin, gm);
-      bmax = shfl4_max(bmax, gm);
-      if (r > 0 && !(prev_min > bmax)) bad = true;
-      prev_min = bmin;
-      pk[r] = best;
-    }
+    for (int i = 1; i < L; ++i) mk[j] = s == i ? pk[L * j + i] : mk[j];
+    pw[j] = L * j + s < k ? expf(key_value(mk[j]) - mx) / ssum : 0.0f;
   }
-  uint32_t rest = 0;  // largest key an unpicked expert could take
+  float ps = 0.0f;
 #pragma unroll
-  for (int i = 0; i < NE; ++i)
-    if (key[i] != 0) rest = max(rest, kmx[i]);
-  rest = shfl4_max(rest, gm);
-  if (!(prev_min > rest)) bad = true;
-  float pw[KMAX], ps = 0.0f;
+  for (int r = 0; r < KMAX; ++r)
+    if (r < k) ps += __shfl_sync(0xffffffffu, pw[r / L], (threadIdx.x & (32 - L)) | (r % L));
 #pragma unroll
-  for (int r = 0; r < KMAX; ++r) {
-    pw[r] = 0.0f;
-    if (r < p.k) {
-      pw[r] = expf(key_value(pk[r]) - mx) / ssum;
-      ps += pw[r];
-    }
-  }
-#pragma unroll
-  for (int r = 0; r < KMAX; ++r) {
-    if (r < p.k && (r & 3) == s) {
-      float w = p.norm ? pw[r] / fmaxf(ps, 1e-12f) : pw[r];
-      w = round_bf16(w);
-      const int64_t o = t * p.k + r;
-      p.topk_idx[o] = 0xFFFF - static_cast<int>(pk[r] & 0xFFFFu);
+  for (int j = 0; j < KMAX / L; ++j) {
+    const int r = L * j + s;
+    float w = p.norm ? pw[j] / fmaxf(ps, 1e-12f) : pw[j];
+    w = round_bf16(w);
+    if (live && r < k) {
+      const int64_t o = t * k + r;
+      p.topk_idx[o] = key_expert(mk[j]);
       if (p.topk_w_f32) p.topk_w_f32[o] = w;
       if (p.topk_w_dtype)
         static_cast<uint16_t*>(p.topk_w_dtype)[o] = static_cast<uint16_t>(f32_to_bf16_bits(w));
     }
   }
   return bad;
+}
+
+// Lane s's experts (bit i: expert s E/L + i) of a token that route_tok could
+// not certify whose rounding is not certain and whose largest key reaches
+// the smallest key any pick could take.  An expert below that bound stays
+// below every pick, in exact values and in its own rounding alike, so exact
+// values for these experts alone make the routing exact.
+template <int E, int L>
+__device__ __forceinline__ uint32_t fix_mask_tok(const float* row, const RtParams& p,
+                                                 const RouteCert& c, int s) {
+  constexpr int NE = E / L;
+  uint32_t m = 0;
+#pragma unroll
+  for (int i = 0; i < NE; ++i) {
+    const int e = NE * s + i;
+    if (e < p.E) {
+      float x = row[lg_idx(e)];
+      if (p.bias) x = x + bf16_bits_to_f32(p.bias[e]);
+      const uint32_t key = logit_key(x, c.delta, 1024.0f * c.delta, static_cast<uint32_t>(e));
+      if ((key & 7u) != 0u && key_max(key, c.delta) >= c.lmin) m |= 1u << i;
+    }
+  }
+  return m;
 }
 
 template <int E, int KMAX>  // E: the configuration's expert maximum (p.E <= E)
@@ -946,8 +1148,8 @@ router_rows_kernel(const __grid_constant__ CUtensorMap tmX2, const __grid_consta
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   RtCtl& ctl = *reinterpret_cast<RtCtl*>(smem + C::kMainBytes);
-  float* lg0 = reinterpret_cast<float*>(smem);          // [64][E+1] first halves
-  float* lg1 = lg0 + RRT * C::kLgStride;                // [64][E+1] second halves
+  float* lg0 = reinterpret_cast<float*>(smem);          // [64][kLgStride] first halves
+  float* lg1 = lg0 + RRT * C::kLgStride;                // [64][kLgStride] second halves
   const uint32_t sbase = smem_u32(smem);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t t0 = static_cast<int64_t>(blockIdx.x) * RRT;
@@ -1051,22 +1253,19 @@ router_rows_kernel(const __grid_constant__ CUtensorMap tmX2, const __grid_consta
         tmem_ld_32cols(tmem + (static_cast<uint32_t>(quad * 32) << 16) + E + c * 32, rb);
         tc_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) dst[c * 32 + i] = __uint_as_float(col0 ? rb[i] : ra[i]);
+        for (int i = 0; i < 32; ++i) dst[lg_idx(c * 32 + i)] = __uint_as_float(col0 ? rb[i] : ra[i]);
       }
     }
     tc_fence_before();
     named_barrier_sync(1, kEpi);
     // ---- routing: token j on lanes 4 (j % 8) .. +3 of warp j / 8
     const bool live = !*abort;
-    {
+    if (live) {  // uniform over the CTA
       const int j = ew * 8 + (lane >> 2), s = lane & 3;
-      const unsigned gm = 0xFu << (lane & 28);  // this token's four lanes
       const int64_t t = t0 + j;
-      if (live && t < p.T) {  // uniform over the 4 lanes of a token
-        const bool bad = route4<E, KMAX>(lg0 + j * C::kLgStride, lg1 + j * C::kLgStride, p,
-                                         p.cert_rel, t, s, gm, true);
-        if (bad && s == 0) p.fix_list[atomicAdd(p.fix_count, 1)] = static_cast<int32_t>(t);
-      }
+      const bool bad = route_tok<E, KMAX, 4>(lg0 + j * C::kLgStride, lg1 + j * C::kLgStride, p,
+                                             p.cert_rel, t, s, t < p.T, true);
+      if (bad && s == 0 && t < p.T) p.fix_list[atomicAdd(p.fix_count, 1)] = static_cast<int32_t>(t);
     }
   }
   tc_fence_before();
@@ -1131,6 +1330,505 @@ cudaError_t launch_rows_tc(const void* x, const void* w, const RtParams& p, cuda
     return cudaErrorInvalidValue;
   router_rows_kernel<E, KMAX><<<static_cast<unsigned>(cdiv64(p.T, RRT)), kRrThreads, C::kSmem, st>>>(
       mx, mw, p);
+  return cudaGetLastError();
+}
+
+// ----------------------------------------------------------------------------
+// router_pair_kernel: the tensor-core pass for E <= 64 on CTA pairs, with the
+// router weight resident in shared memory, persistent over 128-token tiles,
+// and the fix-up done in the kernel itself.
+//
+// The operands are router_rows_kernel's (x read as [2T, d/2]: rows 2t and
+// 2t+1 are the two halves of token t), but the two CTAs of a cluster share
+// one 256-row MMA (tcgen05.mma.cta_group::2, M=256, N=128).  Each CTA stages
+// its own 64 tokens (128 rows) per tile and holds one half of the stacked
+// weight for the whole kernel: the even CTA W[:, :d/2], the odd CTA
+// W[:, d/2:], 64 rows each (zeros past E).  The weight therefore crosses L2
+// once per CTA instead of once per k-step and tile, and the TMA ring holds
+// token rows only (up to 8 stages of 16 KiB).  Accumulator row 2j of a CTA
+// holds token j's first-half sums in columns [0, 64), row 2j+1 its
+// second-half sums in columns [64, 128).  The weight's k-blocks are loaded
+// with the first tile's token blocks, on the same stage barriers.
+//
+// Roles: warp 0 TMA, warp 1 MMA (the even CTA issues for both), warps 2-5
+// read the accumulator (one TMEM lane quadrant each), add each token's two
+// halves (lanes 2j and 2j+1 each take 8 of every 16 experts and trade the
+// other half of their sums with shuffles) and park the logits in shared
+// memory, which frees the accumulator; warps 6-21 route each token on 8
+// lanes (route_tok).  Two accumulators and the logits buffer let one tile's
+// routing run under the next tile's stream.
+//
+// Uncertified tokens are fixed where they are found.  Their decision-
+// relevant uncertain logits (fix_mask_tok) go to the tile's fix list, and the
+// routing warps share the list out: a warp computes one exact-order logit at
+// a time from x and W in global memory (lane = 64-k block, block sums folded
+// in order).  A token with more than kRpFixPerToken such logits is
+// recomputed whole by its own warp (lane = expert, blocks in order).  A token
+// whose exact logits all round as its tensor-core sums did keeps the first
+// pass's results; the others are routed once more from exact values, with no
+// margin.  The result equals the exact-order routing, as the fix-up kernels'
+// does, without a second launch.
+constexpr int kRpTok = 64;                 // tokens per CTA and tile (128 per pair)
+constexpr int kRpReaders = 4;              // warps 2..5
+constexpr int kRpRouters = 16;             // warps 6..21
+constexpr int kRpLanes = 8;                // routing lanes per token
+constexpr int kRpThreads = 32 * (2 + kRpReaders + kRpRouters);
+constexpr int kRpMaxStages = 8;
+constexpr int kRpABytes = 128 * RBK * 2;   // 16 KiB: 64 tokens x 2 halves
+constexpr int kRpBBlock = 64 * RBK * 2;    // 8 KiB: one k-block of a weight half
+constexpr int kRpN = 128;                  // MMA N: 64 experts x 2 halves
+constexpr int kRpTmemCols = 2 * kRpN;      // two accumulators
+constexpr int kRpLgStride = LgRow<64>::kStride;  // floats per token row (lg_idx)
+constexpr int kRpLgBytes = kRpTok * kRpLgStride * 4;
+constexpr int kRpFixPerToken = 4;         // listed exact logits per token; more: the whole token
+constexpr int kRpFixCap = kRpTok * kRpFixPerToken;  // (token, expert) fixes per tile
+constexpr int kRpCtlBytes = 768;
+constexpr long kRpSmemMax = 232448;
+
+struct RpCtl {
+  uint64_t full[kRpMaxStages];   // even CTA: both CTAs' blocks of a stage landed
+  uint64_t empty[kRpMaxStages];  // each CTA: the pair's MMAs released the stage
+  uint64_t acc_full[2];          // each CTA: its accumulator rows are complete
+  uint64_t acc_empty[2];         // even CTA: both CTAs' readers drained it
+  uint64_t lg_full;              // the readers parked a tile's logits
+  uint64_t lg_empty;             // the routing warps are done with them
+  uint64_t drain;                // even CTA: every MMA issued has completed
+  uint64_t reroute[2];           // tokens of a tile (bit jt) to route again, by tile parity
+  uint32_t tmem_base;
+  int abort;
+  int fix_n;                     // entries in fix_list for the current tile
+  uint16_t fix_list[kRpFixCap];  // (token jt << 8) | expert: exact logits to compute
+};
+static_assert(sizeof(RpCtl) <= kRpCtlBytes, "control block");
+
+// Ring stages that fit next to a weight half of nkb k-blocks.
+inline int rp_stages(int nkb) {
+  const long s = (kRpSmemMax - 1024 - kRpCtlBytes - kRpLgBytes - static_cast<long>(nkb) * kRpBBlock) /
+                 kRpABytes;
+  return s > kRpMaxStages ? kRpMaxStages : static_cast<int>(s);
+}
+inline size_t rp_smem(int nkb, int stages) {
+  return 1024 + static_cast<size_t>(nkb) * kRpBBlock + static_cast<size_t>(stages) * kRpABytes +
+         kRpLgBytes + kRpCtlBytes;
+}
+
+// One exact-order logit (without the bias) of token t, expert e, on a whole
+// warp: lane b runs 64-k block b (one fma per k, ascending, from +0), and
+// the block sums are added in ascending block order from +0 on every lane.
+__device__ __forceinline__ float warp_exact_logit(const uint16_t* __restrict__ x,
+                                                  const uint16_t* __restrict__ w, int64_t t, int e,
+                                                  int d, int lane) {
+  const int nb = cdiv(d, kLogitBlock);
+  const uint16_t* xr = x + t * d;
+  const uint16_t* wr = w + static_cast<int64_t>(e) * d;
+  float tot = 0.0f;
+  for (int b0 = 0; b0 < nb; b0 += 32) {
+    const int b = b0 + lane;
+    float part = 0.0f;
+    if (b < nb) {
+      const int k0 = b * kLogitBlock;
+      const int nv = min(kLogitBlock, d - k0) / 8;
+      // half a block's loads at a time, issued before its fmas
+#pragma unroll
+      for (int c0 = 0; c0 < kLogitBlock / 8; c0 += 4) {
+        uint4 xv[4], wv[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const bool in = c0 + c < nv;
+          xv[c] = in ? __ldg(reinterpret_cast<const uint4*>(xr + k0) + c0 + c) : make_uint4(0, 0, 0, 0);
+          wv[c] = in ? __ldg(reinterpret_cast<const uint4*>(wr + k0) + c0 + c) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          if (c0 + c < nv) {
+            part = fmaf(bf16_lo(xv[c].x), bf16_lo(wv[c].x), part);
+            part = fmaf(bf16_hi(xv[c].x), bf16_hi(wv[c].x), part);
+            part = fmaf(bf16_lo(xv[c].y), bf16_lo(wv[c].y), part);
+            part = fmaf(bf16_hi(xv[c].y), bf16_hi(wv[c].y), part);
+            part = fmaf(bf16_lo(xv[c].z), bf16_lo(wv[c].z), part);
+            part = fmaf(bf16_hi(xv[c].z), bf16_hi(wv[c].z), part);
+            part = fmaf(bf16_lo(xv[c].w), bf16_lo(wv[c].w), part);
+            part = fmaf(bf16_hi(xv[c].w), bf16_hi(wv[c].w), part);
+          }
+        }
+      }
+    }
+    // ascending block order: eight blocks' sums are fetched, then added
+    const int nq = min(32, nb - b0);
+    for (int q0 = 0; q0 < nq; q0 += 8) {
+      float bs[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) bs[q] = __shfl_sync(0xffffffffu, part, (q0 + q) & 31);
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        if (q0 + q < nq) tot = tot + bs[q];
+    }
+  }
+  return tot;
+}
+
+// Every exact-order logit (without the bias) of token t on a whole warp:
+// lane l computes experts l and l + 32, block after block in ascending
+// order, and stores them in row[lg_idx(e)].
+__device__ __forceinline__ void warp_exact_token(const uint16_t* __restrict__ x,
+                                                 const uint16_t* __restrict__ w, int64_t t, int d,
+                                                 int E, int lane, float* row) {
+  const int nb = cdiv(d, kLogitBlock);
+  const uint16_t* xr = x + t * d;
+  const int e0 = lane, e1 = lane + 32;
+  const uint16_t* w0 = w + static_cast<int64_t>(min(e0, E - 1)) * d;
+  const uint16_t* w1 = w + static_cast<int64_t>(min(e1, E - 1)) * d;
+  float acc0 = 0.0f, acc1 = 0.0f;
+  for (int b = 0; b < nb; ++b) {
+    const int k0 = b * kLogitBlock;
+    const int nv = min(kLogitBlock, d - k0) / 8;
+    float p0 = 0.0f, p1 = 0.0f;
+    // a half block's loads are issued before its fmas
+#pragma unroll
+    for (int c0 = 0; c0 < kLogitBlock / 8; c0 += 4) {
+      uint4 xv[4], u0[4], u1[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const bool in = c0 + c < nv;
+        xv[c] = in ? __ldg(reinterpret_cast<const uint4*>(xr + k0) + c0 + c) : make_uint4(0, 0, 0, 0);
+        u0[c] = in ? __ldg(reinterpret_cast<const uint4*>(w0 + k0) + c0 + c) : make_uint4(0, 0, 0, 0);
+        u1[c] = in ? __ldg(reinterpret_cast<const uint4*>(w1 + k0) + c0 + c) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        if (c0 + c < nv) {
+          const float xs[8] = {bf16_lo(xv[c].x), bf16_hi(xv[c].x), bf16_lo(xv[c].y), bf16_hi(xv[c].y),
+                               bf16_lo(xv[c].z), bf16_hi(xv[c].z), bf16_lo(xv[c].w), bf16_hi(xv[c].w)};
+          const float ws0[8] = {bf16_lo(u0[c].x), bf16_hi(u0[c].x), bf16_lo(u0[c].y), bf16_hi(u0[c].y),
+                                bf16_lo(u0[c].z), bf16_hi(u0[c].z), bf16_lo(u0[c].w), bf16_hi(u0[c].w)};
+          const float ws1[8] = {bf16_lo(u1[c].x), bf16_hi(u1[c].x), bf16_lo(u1[c].y), bf16_hi(u1[c].y),
+                                bf16_lo(u1[c].z), bf16_hi(u1[c].z), bf16_lo(u1[c].w), bf16_hi(u1[c].w)};
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            p0 = fmaf(xs[j], ws0[j], p0);
+            p1 = fmaf(xs[j], ws1[j], p1);
+          }
+        }
+      }
+    }
+    acc0 = acc0 + p0;
+    acc1 = acc1 + p1;
+  }
+  if (e0 < E) row[lg_idx(e0)] = acc0;
+  if (e1 < E) row[lg_idx(e1)] = acc1;
+}
+
+template <int KMAX, bool KFIX>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kRpThreads, 1)
+router_pair_kernel(const __grid_constant__ CUtensorMap tmX2, const __grid_constant__ CUtensorMap tmW,
+                   const RtParams p, const uint16_t* __restrict__ xg,
+                   const uint16_t* __restrict__ wg, int stages) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  const int half = p.d / 2;
+  const int nkb = cdiv(half, RBK);
+  const uint32_t sB = smem_u32(smem);                       // weight half: nkb x 8 KiB
+  const uint32_t sRing = sB + nkb * kRpBBlock;              // stages x 16 KiB
+  float* lg = reinterpret_cast<float*>(smem + nkb * kRpBBlock + stages * kRpABytes);
+  RpCtl& ctl = *reinterpret_cast<RpCtl*>(reinterpret_cast<uint8_t*>(lg) + kRpLgBytes);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const int64_t pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int64_t ntiles = cdiv64(p.T, 2 * kRpTok);
+  const unsigned long long lim = p.wait_limit_ns;
+
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(smem_u32(&ctl.full[s]), 1);   // the even CTA's arm
+      mbar_init(smem_u32(&ctl.empty[s]), 1);  // one commit per stage use
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_u32(&ctl.acc_full[a]), 1);
+      mbar_init(smem_u32(&ctl.acc_empty[a]), 2 * kRpReaders);  // both CTAs' readers
+    }
+    mbar_init(smem_u32(&ctl.lg_full), kRpReaders);
+    mbar_init(smem_u32(&ctl.lg_empty), kRpRouters);
+    mbar_init(smem_u32(&ctl.drain), 1);
+    ctl.abort = 0;
+    ctl.fix_n = 0;
+    ctl.reroute[0] = ctl.reroute[1] = 0ull;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmX2);
+    tma_prefetch_desc(&tmW);
+  } else if (warp == 1) {
+    tmem_alloc_pair(smem_u32(&ctl.tmem_base), kRpTmemCols);
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // barrier inits visible to the peer CTA before any remote signal
+  tc_fence_after();
+  const uint32_t tmem = ctl.tmem_base;
+  volatile int* abort = &ctl.abort;
+  int never = 0;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true, first = true;
+      for (int64_t tile = pair; ok && tile < ntiles; tile += npairs) {
+        const int row0 = static_cast<int>(2 * (tile * 2 * kRpTok + rank * kRpTok));
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!mbar_wait_bounded(smem_u32(&ctl.empty[stage]), phase ^ 1u, abort, p.err, lim)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = smem_u32(&ctl.full[stage]);
+          const uint32_t fb_leader = map_to_rank(fb, 0);
+          if (leader) mbar_arrive_expect_tx(fb, 2 * (kRpABytes + (first ? kRpBBlock : 0)));
+          tma_load_2d_pair(sRing + stage * kRpABytes, &tmX2, kb * RBK, row0, fb_leader);
+          if (first)
+            tma_load_2d_pair(sB + kb * kRpBBlock, &tmW, (rank ? half : 0) + kb * RBK, 0, fb_leader);
+          if (++stage == stages) { stage = 0; phase ^= 1u; }
+        }
+        first = false;
+      }
+      // every stage this CTA filled is released by the pair's MMAs before
+      // the CTA leaves (no copy still landing, no commit on its way)
+      for (int i = 0; i < stages; ++i) {
+        if (!mbar_wait_bounded(smem_u32(&ctl.empty[stage]), phase ^ 1u, &never, p.err, lim)) break;
+        if (++stage == stages) { stage = 0; phase ^= 1u; }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- MMA issuer
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(256, kRpN);
+      int stage = 0, acc = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      bool ok = true;
+      for (int64_t tile = pair; ok && tile < ntiles; tile += npairs) {
+        if (!mbar_wait_bounded(smem_u32(&ctl.acc_empty[acc]), acc_phase ^ 1u, abort, p.err, lim))
+          break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + static_cast<uint32_t>(acc * kRpN);
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!mbar_wait_bounded(smem_u32(&ctl.full[stage]), phase, abort, p.err, lim)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = sRing + stage * kRpABytes;
+          const uint32_t sb = sB + kb * kRpBBlock;
+#pragma unroll
+          for (int kk = 0; kk < RBK / 16; ++kk)
+            tc_mma_bf16_pair(d_tmem, smem_desc_sw128(sa + kk * 32), smem_desc_sw128(sb + kk * 32),
+                             idesc, (kb | kk) != 0 ? 1u : 0u);
+          tc_commit_pair_both(smem_u32(&ctl.empty[stage]));
+          if (++stage == stages) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        tc_commit_pair_both(smem_u32(&ctl.acc_full[acc]));
+        if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+      }
+      tc_commit_pair(smem_u32(&ctl.drain));
+      mbar_wait_bounded(smem_u32(&ctl.drain), 0, &never, p.err, lim);
+      for (int i = 0; i < 2; ++i) {
+        if (!mbar_wait_bounded(smem_u32(&ctl.acc_empty[acc]), acc_phase ^ 1u, &never, p.err, lim))
+          break;
+        if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+      }
+    }
+  } else if (warp < 2 + kRpReaders) {
+    // ------------------------------------------------- accumulator readers
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;  // accumulator row: token r / 2, half r & 1
+    const int h = r & 1;
+    float* dst = lg + (r >> 1) * kRpLgStride;
+    int acc = 0;
+    uint32_t acc_phase = 0, lg_phase = 0;
+    for (int64_t tile = pair; tile < ntiles; tile += npairs) {
+      if (!mbar_wait_bounded(smem_u32(&ctl.acc_full[acc]), acc_phase, abort, p.err, lim)) break;
+      if (!mbar_wait_bounded(smem_u32(&ctl.lg_empty), lg_phase ^ 1u, abort, p.err, lim)) break;
+      tc_fence_after();
+      const uint32_t trow = tmem + (static_cast<uint32_t>(quad * 32) << 16) +
+                            static_cast<uint32_t>(acc * kRpN);
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        // experts 16c..16c+15: lane 2j holds their first-half sums, lane
+        // 2j+1 their second-half sums; lane 2j keeps experts 16c..+7, lane
+        // 2j+1 16c+8..+15, each receiving the partner's half of them:
+        // logit = first + second
+        uint32_t ra[16], rb[16];
+        tmem_ld_16cols(trow + c * 16, ra);
+        tmem_ld_16cols(trow + 64 + c * 16, rb);
+        tc_wait_ld();
+        float o[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float send = __uint_as_float(h ? rb[i] : ra[8 + i]);
+          const float recv = __shfl_xor_sync(0xffffffffu, send, 1);
+          o[i] = h ? recv + __uint_as_float(rb[8 + i]) : __uint_as_float(ra[i]) + recv;
+        }
+        float* q = dst + lg_idx(16 * c + 8 * h);
+        reinterpret_cast<float4*>(q)[0] = make_float4(o[0], o[1], o[2], o[3]);
+        reinterpret_cast<float4*>(q)[1] = make_float4(o[4], o[5], o[6], o[7]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive_cluster(map_to_rank(smem_u32(&ctl.acc_empty[acc]), 0));
+        mbar_arrive(smem_u32(&ctl.lg_full));
+      }
+      if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+      lg_phase ^= 1u;
+    }
+  } else {
+    // ------------------------------------------------------------- routing
+    constexpr int L = kRpLanes;
+    constexpr int TPW = 32 / L;  // tokens per routing warp
+    const int rw = warp - 2 - kRpReaders;
+    const int jt = rw * TPW + lane / L, s = lane % L;  // token jt of the tile on L lanes
+    float* row = lg + jt * kRpLgStride;
+    constexpr int kRouteThreads = 32 * kRpRouters;
+    uint32_t lg_phase = 0;
+    // Every routing warp goes through every tile and both named barriers,
+    // also after a wait gave up (it then does no work), so that none waits
+    // at a barrier for a warp that left.
+    for (int64_t tile = pair; tile < ntiles; tile += npairs) {
+      const bool ok = mbar_wait_bounded(smem_u32(&ctl.lg_full), lg_phase, abort, p.err, lim);
+      const int64_t tile0 = tile * 2 * kRpTok + rank * kRpTok;
+      const int64_t t = tile0 + jt;
+      RouteCert cert{0.0f, 0u};
+      bool bad = false;
+      if (ok) bad = route_tok<64, KMAX, L, KFIX>(row, nullptr, p, p.cert_rel, t, s, t < p.T, true, &cert) &&
+                    t < p.T;
+      // Tokens whose order decisions are not certain need exact-order
+      // logits for their relevant uncertain experts.  Those (token, expert)
+      // pairs go to the tile's fix list, which all routing warps then share
+      // out; a token with more of them than fix_logits_max is recomputed
+      // whole by its own warp.  Where every exact logit rounds as its
+      // tensor-core sum did, the keys, the selection and the weights of the
+      // first pass stand; the other tokens are routed once more.
+      unsigned todo = __ballot_sync(0xffffffffu, bad && s == 0);
+      while (todo) {
+        const int src = __ffs(todo) - 1;
+        todo &= todo - 1;
+        const int jsrc = rw * TPW + src / L;
+        float* trow = lg + jsrc * kRpLgStride;
+        uint32_t um = 0;
+        if (lane / L == src / L) um = fix_mask_tok<64, L>(trow, p, cert, s);
+        uint32_t m[L];
+        int nu = 0;
+#pragma unroll
+        for (int q = 0; q < L; ++q) {
+          m[q] = __shfl_sync(0xffffffffu, um, src + q);
+          nu += __popc(m[q]);
+        }
+        if (nu <= kRpFixPerToken) {
+          if (lane == 0) {
+            int slot = atomicAdd(&ctl.fix_n, nu);
+#pragma unroll
+            for (int q = 0; q < L; ++q) {
+              uint32_t mm = m[q];
+              while (mm) {
+                const int i = __ffs(mm) - 1;
+                mm &= mm - 1;
+                ctl.fix_list[slot++] = static_cast<uint16_t>((jsrc << 8) | ((64 / L) * q + i));
+              }
+            }
+          }
+        } else {
+          warp_exact_token(xg, wg, tile0 + jsrc, p.d, p.E, lane, trow);
+          if (lane == 0) atomicOr(reinterpret_cast<unsigned long long*>(&ctl.reroute[lg_phase]),
+                                  1ull << jsrc);
+        }
+      }
+      named_barrier_sync(1, kRouteThreads);  // the tile's fix list is complete
+      const int nfix = ctl.fix_n;
+      for (int i = rw; i < nfix; i += kRpRouters) {
+        const int jf = ctl.fix_list[i] >> 8, e = ctl.fix_list[i] & 0xFF;
+        const float v = warp_exact_logit(xg, wg, tile0 + jf, e, p.d, lane);
+        float* frow = lg + jf * kRpLgStride;
+        const float bias = p.bias ? bf16_bits_to_f32(p.bias[e]) : 0.0f;
+        const bool changed = round_bf16(v + bias) != round_bf16(frow[lg_idx(e)] + bias);
+        __syncwarp();
+        if (lane == 0) {
+          frow[lg_idx(e)] = v;
+          if (changed)
+            atomicOr(reinterpret_cast<unsigned long long*>(&ctl.reroute[lg_phase]), 1ull << jf);
+        }
+      }
+      named_barrier_sync(1, kRouteThreads);  // exact logits written, tokens to re-route marked
+      const uint64_t rr = ctl.reroute[lg_phase];
+      const bool mine = ((rr >> jt) & 1ull) != 0ull;
+      if (__any_sync(0xffffffffu, mine))
+        route_tok<64, KMAX, L, KFIX>(row, nullptr, p, 0.0f, t, s, mine && t < p.T, false);
+      if (rw == 0 && lane == 0) {
+        // the next tile's list starts empty; the other parity's mask was
+        // last read before this tile's logits arrived
+        ctl.fix_n = 0;
+        ctl.reroute[lg_phase ^ 1u] = 0ull;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&ctl.lg_empty));
+      lg_phase ^= 1u;
+    }
+  }
+
+  // --------------------------------------------------------------- teardown
+  __syncwarp();  // single-lane roles rejoin their warps before the CTA barrier
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // neither CTA leaves while the pair's MMAs or the peer use it
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, kRpTmemCols);
+  }
+}
+
+// HMOE_ROUTER_PAIR=0 (read once per process) turns the pair pass off, so
+// tests can run the other passes and fix-up kernels for E <= 64.
+bool router_pair_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("HMOE_ROUTER_PAIR");
+    return !(v && atoi(v) == 0);
+  }();
+  return on;
+}
+
+bool pair_pass_fits(int64_t T, int d, int E) {
+  if (E > 64 || d % 16 != 0 || !router_pair_enabled() || router_whole_rows_forced()) return false;
+  return rp_stages(cdiv(d / 2, RBK)) >= 3 && 2 * T < (static_cast<int64_t>(1) << 31);
+}
+
+template <int KMAX, bool KFIX>
+cudaError_t launch_pair_tc(const void* x, const void* w, const RtParams& p, cudaStream_t st) {
+  static int done[64] = {0};
+  static std::mutex mu;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!done[dev]) {
+      e = cudaFuncSetAttribute(router_pair_kernel<KMAX, KFIX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(kRpSmemMax));
+      if (e != cudaSuccess) return e;
+      done[dev] = 1;
+    }
+  }
+  const int nkb = cdiv(p.d / 2, RBK);
+  const int stages = rp_stages(nkb);
+  CUtensorMap mx, mw;
+  if (!map_half_rows(&mx, x, static_cast<uint64_t>(p.T), static_cast<uint64_t>(p.d)) ||
+      !map_rows(&mw, w, static_cast<uint64_t>(p.E), static_cast<uint64_t>(p.d), 64))
+    return cudaErrorInvalidValue;
+  const int64_t ntiles = cdiv64(p.T, 2 * kRpTok);
+  const int sms = num_sms_for_current_device();
+  const int64_t pairs = ntiles < sms / 2 ? ntiles : sms / 2;
+  router_pair_kernel<KMAX, KFIX><<<static_cast<unsigned>(2 * (pairs < 1 ? 1 : pairs)), kRpThreads,
+                             rp_smem(nkb, stages), st>>>(
+      mx, mw, p, static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(w), stages);
   return cudaGetLastError();
 }
 
@@ -1264,8 +1962,12 @@ cudaError_t launch_router_topk_tc(const void* x, const void* w_router, const voi
                                   void* scratch, int* err, cudaStream_t stream, float* sums_out) {
   if (T == 0) return cudaSuccess;
   int* fix_count = static_cast<int*>(scratch);
-  cudaError_t e = cudaMemsetAsync(fix_count, 0, sizeof(int), stream);
-  if (e != cudaSuccess) return e;
+  // the pair pass fixes its uncertified tokens itself: no fix list
+  const bool pair = pair_pass_fits(T, d, E);
+  if (!pair) {
+    cudaError_t e = cudaMemsetAsync(fix_count, 0, sizeof(int), stream);
+    if (e != cudaSuccess) return e;
+  }
   RtParams p;
   p.bias = static_cast<const uint16_t*>(bias);
   p.T = T;
@@ -1285,6 +1987,10 @@ cudaError_t launch_router_topk_tc(const void* x, const void* w_router, const voi
   p.err = err;
   p.wait_limit_ns = kWaitLimitNs;
   p.cert_rel = router_cert_rel();
+  if (pair)
+    return k == 8   ? launch_pair_tc<8, true>(x, w_router, p, stream)
+           : k < 8  ? launch_pair_tc<8, false>(x, w_router, p, stream)
+                    : launch_pair_tc<32, false>(x, w_router, p, stream);
   if (k <= 8)
     return E <= 64 ? launch_tc<64, 8>(x, w_router, p, stream)
                    : launch_tc<128, 8>(x, w_router, p, stream);

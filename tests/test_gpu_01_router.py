@@ -124,10 +124,17 @@ def test_router_full_size_exact_e128_near_ties():
     _check_against_oracle(x, w, None, k, True, "bf16")
 
 
-def test_router_fixup_pass_is_exact_order(tmp_path):
-    """With HMOE_ROUTER_CERT_REL=1 (child process) no token is certified and
-    the fix-up kernels route every token: their logits must be the
-    exact-order logits bit for bit, and the routing the oracle's."""
+@pytest.mark.parametrize("mode", ["pair_token", "pair_logit", "fixup_kernels"])
+def test_router_fixup_pass_is_exact_order(tmp_path, mode):
+    """With HMOE_ROUTER_CERT_REL=1 (child process) no token is certified, so
+    every token takes a fix-up path: their logits must be the exact-order
+    logits bit for bit, and the routing the oracle's.  Paths: the pair pass's
+    in-kernel recompute of a whole token (every logit is uncertain) and the
+    separate fix-up kernels behind the other passes (HMOE_ROUTER_PAIR=0).
+    pair_logit widens the margin to 2^-12 instead, so that many tokens take
+    the pair pass's shared one-logit-at-a-time fixes; only their decisive
+    logits are recomputed there, so the routing is compared, not every
+    logit."""
     import os
     import subprocess
     import sys
@@ -136,24 +143,34 @@ def test_router_fixup_pass_is_exact_order(tmp_path):
 
     import router_fixup_worker_gpu as W
 
-    path = tmp_path / "fixup.pt"
+    path = tmp_path / f"{mode}.pt"
     env = dict(os.environ, HMOE_ROUTER_CERT_REL="1")
+    if mode == "pair_logit":
+        env["HMOE_ROUTER_CERT_REL"] = str(2.0 ** -12)
+    elif mode == "fixup_kernels":
+        env["HMOE_ROUTER_PAIR"] = "0"
     subprocess.run([sys.executable, W.__file__, str(path)], env=env, check=True, timeout=600)
     res = torch.load(path)
     for name, x, w, bias, k, norm in W.cases():
         idx, wt, logits = (t.numpy() for t in res[name])
         ol = O.router_logits(x, w, bias, "bf16")
         oidx, ow, _ = O.route(ol, k, norm, "bf16")
-        assert np.array_equal(logits, ol), name
+        if mode != "pair_logit":
+            assert np.array_equal(logits, ol), name
         assert np.array_equal(idx.astype(np.int64), oidx), name
-        np.testing.assert_allclose(wt, ow, rtol=2 ** -7, atol=0, err_msg=name)
+        np.testing.assert_allclose(wt, ow, rtol=2 ** -6 if mode == "pair_logit" else 2 ** -7,
+                                   atol=0, err_msg=name)
 
 
-def test_router_whole_row_pass_is_exact(tmp_path):
-    """The 128-token whole-row tensor-core pass (the one that runs when d is
-    not a multiple of 16), forced for every d with HMOE_ROUTER_WHOLE_ROWS=1 in
-    a child process: its certified routing must equal the exact-order routing
-    too, on the same cases as the fix-up test."""
+@pytest.mark.parametrize("mode", ["whole_rows", "rows"])
+def test_router_whole_row_pass_is_exact(tmp_path, mode):
+    """The tensor-core passes other than the default pair pass, each with its
+    separate fix-up kernels, in a child process: the 128-token whole-row pass
+    (the one that runs when d is not a multiple of 16), forced for every d
+    with HMOE_ROUTER_WHOLE_ROWS=1, and the 64-token row-split pass (the one
+    for E > 64), forced for E <= 64 with HMOE_ROUTER_PAIR=0.  Their certified
+    routing must equal the exact-order routing too, on the same cases as the
+    fix-up test."""
     import os
     import subprocess
     import sys
@@ -162,8 +179,12 @@ def test_router_whole_row_pass_is_exact(tmp_path):
 
     import router_fixup_worker_gpu as W
 
-    path = tmp_path / "whole_rows.pt"
-    env = dict(os.environ, HMOE_ROUTER_WHOLE_ROWS="1")
+    path = tmp_path / f"{mode}.pt"
+    env = dict(os.environ)
+    if mode == "whole_rows":
+        env["HMOE_ROUTER_WHOLE_ROWS"] = "1"
+    else:
+        env["HMOE_ROUTER_PAIR"] = "0"
     env.pop("HMOE_ROUTER_CERT_REL", None)
     subprocess.run([sys.executable, W.__file__, str(path)], env=env, check=True, timeout=600)
     res = torch.load(path)
