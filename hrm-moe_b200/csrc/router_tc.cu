@@ -1334,9 +1334,9 @@ cudaError_t launch_rows_tc(const void* x, const void* w, const RtParams& p, cuda
 }
 
 // ----------------------------------------------------------------------------
-// router_pair_kernel: the tensor-core pass for E <= 64 on CTA pairs, with the
-// router weight resident in shared memory, persistent over 128-token tiles,
-// and the fix-up done in the kernel itself.
+// router_pair_kernel: the tensor-core pass for E <= 128 on CTA pairs,
+// persistent over 128-token tiles, with the fix-up done in the kernel itself;
+// for E <= 64 the router weight is resident in shared memory.
 //
 // The operands are router_rows_kernel's (x read as [2T, d/2]: rows 2t and
 // 2t+1 are the two halves of token t), but the two CTAs of a cluster share
@@ -1348,7 +1348,11 @@ cudaError_t launch_rows_tc(const void* x, const void* w, const RtParams& p, cuda
 // token rows only (up to 8 stages of 16 KiB).  Accumulator row 2j of a CTA
 // holds token j's first-half sums in columns [0, 64), row 2j+1 its
 // second-half sums in columns [64, 128).  The weight's k-blocks are loaded
-// with the first tile's token blocks, on the same stage barriers.
+// with the first tile's token blocks, on the same stage barriers.  For
+// 64 < E <= 128 (EMAX = 128: N = 256, 128 weight rows per CTA) a weight half
+// does not fit next to a ring, so each stage carries the k-block of both
+// the tokens and this CTA's weight half: the pair still reads each weight
+// byte once per tile, not twice as the single-CTA row-split pass does.
 //
 // Roles: warp 0 TMA, warp 1 MMA (the even CTA issues for both), warps 2-5
 // read the accumulator (one TMEM lane quadrant each), add each token's two
@@ -1375,15 +1379,32 @@ constexpr int kRpLanes = 8;                // routing lanes per token
 constexpr int kRpThreads = 32 * (2 + kRpReaders + kRpRouters);
 constexpr int kRpMaxStages = 8;
 constexpr int kRpABytes = 128 * RBK * 2;   // 16 KiB: 64 tokens x 2 halves
-constexpr int kRpBBlock = 64 * RBK * 2;    // 8 KiB: one k-block of a weight half
-constexpr int kRpN = 128;                  // MMA N: 64 experts x 2 halves
-constexpr int kRpTmemCols = 2 * kRpN;      // two accumulators
-constexpr int kRpLgStride = LgRow<64>::kStride;  // floats per token row (lg_idx)
-constexpr int kRpLgBytes = kRpTok * kRpLgStride * 4;
 constexpr int kRpFixPerToken = 4;         // listed exact logits per token; more: the whole token
 constexpr int kRpFixCap = kRpTok * kRpFixPerToken;  // (token, expert) fixes per tile
 constexpr int kRpCtlBytes = 768;
 constexpr long kRpSmemMax = 232448;
+
+template <int EMAX>  // the configuration's expert maximum: 64 or 128
+struct RpCfg {
+  static constexpr bool kResident = EMAX == 64;       // the weight half stays in shared memory
+  static constexpr int kBBlock = EMAX * RBK * 2;      // one k-block of a weight half
+  static constexpr int kN = 2 * EMAX;                 // MMA N: EMAX experts x 2 halves
+  static constexpr int kTmemCols = 2 * kN;            // two accumulators
+  static constexpr int kStage = kResident ? kRpABytes : kRpABytes + kBBlock;
+  static constexpr int kLgStride = LgRow<EMAX>::kStride;  // floats per token row (lg_idx)
+  static constexpr int kLgBytes = kRpTok * kLgStride * 4;
+  // ring stages that fit next to the logits, the control block and (when
+  // resident) a weight half of nkb k-blocks
+  static int stages(int nkb) {
+    const long s = (kRpSmemMax - 1024 - kRpCtlBytes - kLgBytes -
+                    (kResident ? static_cast<long>(nkb) * kBBlock : 0)) / kStage;
+    return s > kRpMaxStages ? kRpMaxStages : static_cast<int>(s);
+  }
+  static size_t smem(int nkb, int stages) {
+    return 1024 + (kResident ? static_cast<size_t>(nkb) * kBBlock : 0) +
+           static_cast<size_t>(stages) * kStage + kLgBytes + kRpCtlBytes;
+  }
+};
 
 struct RpCtl {
   uint64_t full[kRpMaxStages];   // even CTA: both CTAs' blocks of a stage landed
@@ -1400,17 +1421,6 @@ struct RpCtl {
   uint16_t fix_list[kRpFixCap];  // (token jt << 8) | expert: exact logits to compute
 };
 static_assert(sizeof(RpCtl) <= kRpCtlBytes, "control block");
-
-// Ring stages that fit next to a weight half of nkb k-blocks.
-inline int rp_stages(int nkb) {
-  const long s = (kRpSmemMax - 1024 - kRpCtlBytes - kRpLgBytes - static_cast<long>(nkb) * kRpBBlock) /
-                 kRpABytes;
-  return s > kRpMaxStages ? kRpMaxStages : static_cast<int>(s);
-}
-inline size_t rp_smem(int nkb, int stages) {
-  return 1024 + static_cast<size_t>(nkb) * kRpBBlock + static_cast<size_t>(stages) * kRpABytes +
-         kRpLgBytes + kRpCtlBytes;
-}
 
 // One exact-order logit (without the bias) of token t, expert e, on a whole
 // warp: lane b runs 64-k block b (one fma per k, ascending, from +0), and
@@ -1467,15 +1477,15 @@ __device__ __forceinline__ float warp_exact_logit(const uint16_t* __restrict__ x
   return tot;
 }
 
-// Every exact-order logit (without the bias) of token t on a whole warp:
-// lane l computes experts l and l + 32, block after block in ascending
-// order, and stores them in row[lg_idx(e)].
+// Exact-order logits (without the bias) of token t on a whole warp, for
+// experts [eb, eb + 64): lane l computes experts eb + l and eb + l + 32,
+// block after block in ascending order, and stores them in row[lg_idx(e)].
 __device__ __forceinline__ void warp_exact_token(const uint16_t* __restrict__ x,
                                                  const uint16_t* __restrict__ w, int64_t t, int d,
-                                                 int E, int lane, float* row) {
+                                                 int E, int lane, float* row, int eb) {
   const int nb = cdiv(d, kLogitBlock);
   const uint16_t* xr = x + t * d;
-  const int e0 = lane, e1 = lane + 32;
+  const int e0 = eb + lane, e1 = eb + lane + 32;
   const uint16_t* w0 = w + static_cast<int64_t>(min(e0, E - 1)) * d;
   const uint16_t* w1 = w + static_cast<int64_t>(min(e1, E - 1)) * d;
   float acc0 = 0.0f, acc1 = 0.0f;
@@ -1518,7 +1528,7 @@ __device__ __forceinline__ void warp_exact_token(const uint16_t* __restrict__ x,
   if (e1 < E) row[lg_idx(e1)] = acc1;
 }
 
-template <int KMAX, bool KFIX>
+template <int EMAX, int KMAX, bool KFIX>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kRpThreads, 1)
 router_pair_kernel(const __grid_constant__ CUtensorMap tmX2, const __grid_constant__ CUtensorMap tmW,
                    const RtParams p, const uint16_t* __restrict__ xg,
@@ -1526,12 +1536,15 @@ router_pair_kernel(const __grid_constant__ CUtensorMap tmX2, const __grid_consta
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
+  using C = RpCfg<EMAX>;
   const int half = p.d / 2;
   const int nkb = cdiv(half, RBK);
-  const uint32_t sB = smem_u32(smem);                       // weight half: nkb x 8 KiB
-  const uint32_t sRing = sB + nkb * kRpBBlock;              // stages x 16 KiB
-  float* lg = reinterpret_cast<float*>(smem + nkb * kRpBBlock + stages * kRpABytes);
-  RpCtl& ctl = *reinterpret_cast<RpCtl*>(reinterpret_cast<uint8_t*>(lg) + kRpLgBytes);
+  const int bres = C::kResident ? nkb * C::kBBlock : 0;
+  const uint32_t sB = smem_u32(smem);                       // resident weight half: nkb blocks
+  const uint32_t sRing = sB + bres;                         // stages: token block (+ weight block)
+  float* lg = reinterpret_cast<float*>(smem + bres + stages * C::kStage);
+  RpCtl& ctl = *reinterpret_cast<RpCtl*>(reinterpret_cast<uint8_t*>(lg) + C::kLgBytes);
+  constexpr int kLgS = C::kLgStride;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_rank();
   const bool leader = rank == 0;
@@ -1558,7 +1571,7 @@ router_pair_kernel(const __grid_constant__ CUtensorMap tmX2, const __grid_consta
     tma_prefetch_desc(&tmX2);
     tma_prefetch_desc(&tmW);
   } else if (warp == 1) {
-    tmem_alloc_pair(smem_u32(&ctl.tmem_base), kRpTmemCols);
+    tmem_alloc_pair(smem_u32(&ctl.tmem_base), C::kTmemCols);
   }
   tc_fence_before();
   __syncthreads();
@@ -1583,10 +1596,13 @@ router_pair_kernel(const __grid_constant__ CUtensorMap tmX2, const __grid_consta
           }
           const uint32_t fb = smem_u32(&ctl.full[stage]);
           const uint32_t fb_leader = map_to_rank(fb, 0);
-          if (leader) mbar_arrive_expect_tx(fb, 2 * (kRpABytes + (first ? kRpBBlock : 0)));
-          tma_load_2d_pair(sRing + stage * kRpABytes, &tmX2, kb * RBK, row0, fb_leader);
-          if (first)
-            tma_load_2d_pair(sB + kb * kRpBBlock, &tmW, (rank ? half : 0) + kb * RBK, 0, fb_leader);
+          const uint32_t sa = sRing + stage * C::kStage;
+          const bool wb = !C::kResident || first;  // this stage carries a weight block
+          if (leader) mbar_arrive_expect_tx(fb, 2 * (kRpABytes + (wb ? C::kBBlock : 0)));
+          tma_load_2d_pair(sa, &tmX2, kb * RBK, row0, fb_leader);
+          if (wb)
+            tma_load_2d_pair(C::kResident ? sB + kb * C::kBBlock : sa + kRpABytes, &tmW,
+                             (rank ? half : 0) + kb * RBK, 0, fb_leader);
           if (++stage == stages) { stage = 0; phase ^= 1u; }
         }
         first = false;
@@ -1601,7 +1617,7 @@ router_pair_kernel(const __grid_constant__ CUtensorMap tmX2, const __grid_consta
   } else if (warp == 1) {
     // ---------------------------------------------------------- MMA issuer
     if (leader && lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16_f32(256, kRpN);
+      constexpr uint32_t idesc = idesc_bf16_f32(256, C::kN);
       int stage = 0, acc = 0;
       uint32_t phase = 0, acc_phase = 0;
       bool ok = true;
@@ -1609,15 +1625,15 @@ router_pair_kernel(const __grid_constant__ CUtensorMap tmX2, const __grid_consta
         if (!mbar_wait_bounded(smem_u32(&ctl.acc_empty[acc]), acc_phase ^ 1u, abort, p.err, lim))
           break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem + static_cast<uint32_t>(acc * kRpN);
+        const uint32_t d_tmem = tmem + static_cast<uint32_t>(acc * C::kN);
         for (int kb = 0; kb < nkb; ++kb) {
           if (!mbar_wait_bounded(smem_u32(&ctl.full[stage]), phase, abort, p.err, lim)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t sa = sRing + stage * kRpABytes;
-          const uint32_t sb = sB + kb * kRpBBlock;
+          const uint32_t sa = sRing + stage * C::kStage;
+          const uint32_t sb = C::kResident ? sB + kb * C::kBBlock : sa + kRpABytes;
 #pragma unroll
           for (int kk = 0; kk < RBK / 16; ++kk)
             tc_mma_bf16_pair(d_tmem, smem_desc_sw128(sa + kk * 32), smem_desc_sw128(sb + kk * 32),
@@ -1642,7 +1658,7 @@ router_pair_kernel(const __grid_constant__ CUtensorMap tmX2, const __grid_consta
     const int quad = warp & 3;
     const int r = quad * 32 + lane;  // accumulator row: token r / 2, half r & 1
     const int h = r & 1;
-    float* dst = lg + (r >> 1) * kRpLgStride;
+    float* dst = lg + (r >> 1) * kLgS;
     int acc = 0;
     uint32_t acc_phase = 0, lg_phase = 0;
     for (int64_t tile = pair; tile < ntiles; tile += npairs) {
@@ -1650,16 +1666,16 @@ router_pair_kernel(const __grid_constant__ CUtensorMap tmX2, const __grid_consta
       if (!mbar_wait_bounded(smem_u32(&ctl.lg_empty), lg_phase ^ 1u, abort, p.err, lim)) break;
       tc_fence_after();
       const uint32_t trow = tmem + (static_cast<uint32_t>(quad * 32) << 16) +
-                            static_cast<uint32_t>(acc * kRpN);
+                            static_cast<uint32_t>(acc * C::kN);
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < EMAX / 16; ++c) {
         // experts 16c..16c+15: lane 2j holds their first-half sums, lane
         // 2j+1 their second-half sums; lane 2j keeps experts 16c..+7, lane
         // 2j+1 16c+8..+15, each receiving the partner's half of them:
         // logit = first + second
         uint32_t ra[16], rb[16];
         tmem_ld_16cols(trow + c * 16, ra);
-        tmem_ld_16cols(trow + 64 + c * 16, rb);
+        tmem_ld_16cols(trow + EMAX + c * 16, rb);
         tc_wait_ld();
         float o[8];
 #pragma unroll
@@ -1687,7 +1703,7 @@ router_pair_kernel(const __grid_constant__ CUtensorMap tmX2, const __grid_consta
     constexpr int TPW = 32 / L;  // tokens per routing warp
     const int rw = warp - 2 - kRpReaders;
     const int jt = rw * TPW + lane / L, s = lane % L;  // token jt of the tile on L lanes
-    float* row = lg + jt * kRpLgStride;
+    float* row = lg + jt * kLgS;
     constexpr int kRouteThreads = 32 * kRpRouters;
     uint32_t lg_phase = 0;
     // Every routing warp goes through every tile and both named barriers,
@@ -1699,7 +1715,8 @@ router_pair_kernel(const __grid_constant__ CUtensorMap tmX2, const __grid_consta
       const int64_t t = tile0 + jt;
       RouteCert cert{0.0f, 0u};
       bool bad = false;
-      if (ok) bad = route_tok<64, KMAX, L, KFIX>(row, nullptr, p, p.cert_rel, t, s, t < p.T, true, &cert) &&
+      if (ok) bad = route_tok<EMAX, KMAX, L, KFIX>(row, nullptr, p, p.cert_rel, t, s, t < p.T, true,
+                                                 &cert) &&
                     t < p.T;
       // Tokens whose order decisions are not certain need exact-order
       // logits for their relevant uncertain experts.  Those (token, expert)
@@ -1713,9 +1730,9 @@ router_pair_kernel(const __grid_constant__ CUtensorMap tmX2, const __grid_consta
         const int src = __ffs(todo) - 1;
         todo &= todo - 1;
         const int jsrc = rw * TPW + src / L;
-        float* trow = lg + jsrc * kRpLgStride;
+        float* trow = lg + jsrc * kLgS;
         uint32_t um = 0;
-        if (lane / L == src / L) um = fix_mask_tok<64, L>(trow, p, cert, s);
+        if (lane / L == src / L) um = fix_mask_tok<EMAX, L>(trow, p, cert, s);
         uint32_t m[L];
         int nu = 0;
 #pragma unroll
@@ -1732,12 +1749,13 @@ router_pair_kernel(const __grid_constant__ CUtensorMap tmX2, const __grid_consta
               while (mm) {
                 const int i = __ffs(mm) - 1;
                 mm &= mm - 1;
-                ctl.fix_list[slot++] = static_cast<uint16_t>((jsrc << 8) | ((64 / L) * q + i));
+                ctl.fix_list[slot++] = static_cast<uint16_t>((jsrc << 8) | ((EMAX / L) * q + i));
               }
             }
           }
         } else {
-          warp_exact_token(xg, wg, tile0 + jsrc, p.d, p.E, lane, trow);
+          for (int eb = 0; eb < EMAX; eb += 64)
+            warp_exact_token(xg, wg, tile0 + jsrc, p.d, p.E, lane, trow, eb);
           if (lane == 0) atomicOr(reinterpret_cast<unsigned long long*>(&ctl.reroute[lg_phase]),
                                   1ull << jsrc);
         }
@@ -1747,7 +1765,7 @@ router_pair_kernel(const __grid_constant__ CUtensorMap tmX2, const __grid_consta
       for (int i = rw; i < nfix; i += kRpRouters) {
         const int jf = ctl.fix_list[i] >> 8, e = ctl.fix_list[i] & 0xFF;
         const float v = warp_exact_logit(xg, wg, tile0 + jf, e, p.d, lane);
-        float* frow = lg + jf * kRpLgStride;
+        float* frow = lg + jf * kLgS;
         const float bias = p.bias ? bf16_bits_to_f32(p.bias[e]) : 0.0f;
         const bool changed = round_bf16(v + bias) != round_bf16(frow[lg_idx(e)] + bias);
         __syncwarp();
@@ -1761,7 +1779,7 @@ router_pair_kernel(const __grid_constant__ CUtensorMap tmX2, const __grid_consta
       const uint64_t rr = ctl.reroute[lg_phase];
       const bool mine = ((rr >> jt) & 1ull) != 0ull;
       if (__any_sync(0xffffffffu, mine))
-        route_tok<64, KMAX, L, KFIX>(row, nullptr, p, 0.0f, t, s, mine && t < p.T, false);
+        route_tok<EMAX, KMAX, L, KFIX>(row, nullptr, p, 0.0f, t, s, mine && t < p.T, false);
       if (rw == 0 && lane == 0) {
         // the next tile's list starts empty; the other parity's mask was
         // last read before this tile's logits arrived
@@ -1781,7 +1799,7 @@ router_pair_kernel(const __grid_constant__ CUtensorMap tmX2, const __grid_consta
   cluster_sync_all();  // neither CTA leaves while the pair's MMAs or the peer use it
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc_pair(tmem, kRpTmemCols);
+    tmem_dealloc_pair(tmem, C::kTmemCols);
   }
 }
 
@@ -1796,11 +1814,13 @@ bool router_pair_enabled() {
 }
 
 bool pair_pass_fits(int64_t T, int d, int E) {
-  if (E > 64 || d % 16 != 0 || !router_pair_enabled() || router_whole_rows_forced()) return false;
-  return rp_stages(cdiv(d / 2, RBK)) >= 3 && 2 * T < (static_cast<int64_t>(1) << 31);
+  if (E > 128 || d % 16 != 0 || !router_pair_enabled() || router_whole_rows_forced()) return false;
+  const int nkb = cdiv(d / 2, RBK);
+  const int st = E <= 64 ? RpCfg<64>::stages(nkb) : RpCfg<128>::stages(nkb);
+  return st >= 3 && 2 * T < (static_cast<int64_t>(1) << 31);
 }
 
-template <int KMAX, bool KFIX>
+template <int EMAX, int KMAX, bool KFIX>
 cudaError_t launch_pair_tc(const void* x, const void* w, const RtParams& p, cudaStream_t st) {
   static int done[64] = {0};
   static std::mutex mu;
@@ -1811,23 +1831,24 @@ cudaError_t launch_pair_tc(const void* x, const void* w, const RtParams& p, cuda
   {
     std::lock_guard<std::mutex> lock(mu);
     if (!done[dev]) {
-      e = cudaFuncSetAttribute(router_pair_kernel<KMAX, KFIX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      e = cudaFuncSetAttribute(router_pair_kernel<EMAX, KMAX, KFIX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                static_cast<int>(kRpSmemMax));
       if (e != cudaSuccess) return e;
       done[dev] = 1;
     }
   }
   const int nkb = cdiv(p.d / 2, RBK);
-  const int stages = rp_stages(nkb);
+  using C = RpCfg<EMAX>;
+  const int stages = C::stages(nkb);
   CUtensorMap mx, mw;
   if (!map_half_rows(&mx, x, static_cast<uint64_t>(p.T), static_cast<uint64_t>(p.d)) ||
-      !map_rows(&mw, w, static_cast<uint64_t>(p.E), static_cast<uint64_t>(p.d), 64))
+      !map_rows(&mw, w, static_cast<uint64_t>(p.E), static_cast<uint64_t>(p.d), EMAX))
     return cudaErrorInvalidValue;
   const int64_t ntiles = cdiv64(p.T, 2 * kRpTok);
   const int sms = num_sms_for_current_device();
   const int64_t pairs = ntiles < sms / 2 ? ntiles : sms / 2;
-  router_pair_kernel<KMAX, KFIX><<<static_cast<unsigned>(2 * (pairs < 1 ? 1 : pairs)), kRpThreads,
-                             rp_smem(nkb, stages), st>>>(
+  router_pair_kernel<EMAX, KMAX, KFIX><<<static_cast<unsigned>(2 * (pairs < 1 ? 1 : pairs)), kRpThreads,
+                             C::smem(nkb, stages), st>>>(
       mx, mw, p, static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(w), stages);
   return cudaGetLastError();
 }
@@ -1988,9 +2009,12 @@ cudaError_t launch_router_topk_tc(const void* x, const void* w_router, const voi
   p.wait_limit_ns = kWaitLimitNs;
   p.cert_rel = router_cert_rel();
   if (pair)
-    return k == 8   ? launch_pair_tc<8, true>(x, w_router, p, stream)
-           : k < 8  ? launch_pair_tc<8, false>(x, w_router, p, stream)
-                    : launch_pair_tc<32, false>(x, w_router, p, stream);
+    return E <= 64 ? (k == 8  ? launch_pair_tc<64, 8, true>(x, w_router, p, stream)
+                      : k < 8 ? launch_pair_tc<64, 8, false>(x, w_router, p, stream)
+                              : launch_pair_tc<64, 32, false>(x, w_router, p, stream))
+                   : (k == 8  ? launch_pair_tc<128, 8, true>(x, w_router, p, stream)
+                      : k < 8 ? launch_pair_tc<128, 8, false>(x, w_router, p, stream)
+                              : launch_pair_tc<128, 32, false>(x, w_router, p, stream));
   if (k <= 8)
     return E <= 64 ? launch_tc<64, 8>(x, w_router, p, stream)
                    : launch_tc<128, 8>(x, w_router, p, stream);
