@@ -38,11 +38,12 @@ L2_FLUSH_BYTES = 256 << 20
 NVLINK_GBS = 770.0
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per forward of
 # each phase's kernels, from one ncu capture of this workload on one B200
-# (profiles/grouped_gemm_pair_xl64_t16384_full.md, profiles/hbm_kernels_xl64_t16384.md).
+# (profiles/grouped_gemm_pair_xl64_t16384_full.md, profiles/hbm_kernels_xl64_t16384.md,
+# profiles/router_pair_xl64_t16384.md).
 # Keyed by (config, tokens per GPU); other workloads report null.
 NCU_TRAFFIC_BYTES = {
     ("cfg2_xl64_bf16", 16384): {
-        "router": 50.594e6 + 0.092e6 + 1.326e6,                # router_tc + fix-up
+        "router": 50.606e6 + 45.568e6,  # router_pair (writes: the L2 flush's dirty lines)
         "dispatch": 0.534e6 + 0.039e6 + 51.425e6 + 344.146e6,  # hist + scan + permute
         "gate_up_gemm": 604.140e6 + 123.425e6,
         "down_gemm": 235.043e6 + 354.587e6,
