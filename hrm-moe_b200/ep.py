@@ -122,6 +122,169 @@ def ep_forward(x: torch.Tensor, w_router: torch.Tensor, w_gate_up_local: torch.T
     return y
 
 
+class _AllToAllRows(torch.autograd.Function):
+    """Row all_to_all with host split sizes whose backward sends the
+    gradient rows back the way they came (models/layers.py:360-380)."""
+
+    @staticmethod
+    def forward(ctx, rows, send_splits, recv_splits, group):
+        out = rows.new_empty((int(sum(recv_splits)), *rows.shape[1:]))
+        dist.all_to_all_single(out, rows.contiguous(), list(recv_splits), list(send_splits),
+                               group=group)
+        ctx.splits = (list(send_splits), list(recv_splits))
+        ctx.group = group
+        return out
+
+    @staticmethod
+    def backward(ctx, grad):
+        send, recv = ctx.splits
+        out = grad.new_empty((int(sum(send)), *grad.shape[1:]))
+        dist.all_to_all_single(out, grad.contiguous(), send, recv, group=ctx.group)
+        return out, None, None, None
+
+
+class _RouterLogits(torch.autograd.Function):
+    """The router's rounded logits (computed by the exact-order router, passed
+    in) with the backward of the reference's F.linear gate
+    (models/layers.py:605): grad_x = g @ W, grad_W = g^T @ x, grad_b = sum g."""
+
+    @staticmethod
+    def forward(ctx, x, w, bias, logits):
+        ctx.save_for_backward(x, w)
+        ctx.has_bias = bias is not None
+        return logits.clone()
+
+    @staticmethod
+    def backward(ctx, g):
+        x, w = ctx.saved_tensors
+        g = g.to(x.dtype)
+        gx = g @ w if ctx.needs_input_grad[0] else None
+        gw = g.t() @ x if ctx.needs_input_grad[1] else None
+        gb = g.float().sum(0).to(x.dtype) if ctx.has_bias and ctx.needs_input_grad[2] else None
+        return gx, gw, gb, None
+
+
+class CudaTrainCompute:
+    """The stages of the expert-parallel training forward on this GPU."""
+
+    def route(self, x, w_router, bias, top_k, norm):
+        """(topk_idx [T, k] int32, rounded logits [T, E] in x.dtype), no grad."""
+        idx, _, logits = ops.router_topk(x.detach(), w_router.detach(), top_k, norm,
+                                         None if bias is None else bias.detach(),
+                                         return_logits=True)
+        return idx, logits
+
+    def sort(self, idx, num_experts):
+        """(sort_idx [T*k], counts [E]): the stable sort of the flat assignments."""
+        out = ops.dispatch(idx, num_experts)
+        return out["sort_idx"].long(), out["counts"]
+
+    def grouped_linear(self, rows, weight, counts):
+        return ops.grouped_linear(rows, weight, counts)
+
+
+def load_balancing_loss(probs: torch.Tensor, selected: torch.Tensor,
+                        num_experts: int) -> torch.Tensor:
+    """Qwen-style aux loss of the reference (models/layers.py:163-170)."""
+    tokens_per_expert = torch.bincount(selected.reshape(-1), minlength=num_experts).to(
+        torch.float32) / selected.shape[0]
+    return torch.sum(tokens_per_expert * probs.mean(dim=0)) * num_experts
+
+
+def ep_forward_train(x: torch.Tensor, w_router: torch.Tensor, w_gate_up_local: torch.Tensor,
+                     w_down_local: torch.Tensor, num_experts: int, top_k: int,
+                     norm_topk_prob: bool, group=None, router_bias: Optional[torch.Tensor] = None,
+                     compute=None, aux_tokens: int = -1):
+    """Expert-parallel MoE-FFN forward that autograd can differentiate.
+
+    The reference's grouped_ep training step (models/layers.py:596-634 with
+    SparseMoEExpertParallel, :427-478): the routing comes from the
+    exact-order router; the logits are differentiable as F.linear; softmax,
+    top-k gather, renormalisation, the dispatch gather, the SiLU*up product,
+    the weighting and the index_add combine are torch operations; the row
+    all_to_all each way is an autograd function whose backward sends the
+    gradient rows back; the expert GEMMs are the differentiable grouped
+    linear (grouped_linear), on the received rows sorted by local expert.
+    Returns (y, aux_loss or None, expert_counts or None); aux over the first
+    aux_tokens tokens when aux_tokens >= 0.  The backward runs one all_to_all
+    each way, so every rank must backpropagate through its y (as with the
+    reference's _AllToAllSingle); a rank with no tokens still does.
+    """
+    compute = compute or CudaTrainCompute()
+    world = dist.get_world_size(group)
+    if num_experts % world:
+        raise ValueError(f"num_experts={num_experts} must be divisible by world_size={world}")
+    el = num_experts // world
+    if w_gate_up_local.shape[0] != el or w_down_local.shape[0] != el:
+        raise ValueError(f"this rank holds {w_gate_up_local.shape[0]} experts, expected {el}")
+    T, d = x.shape
+    inter = w_gate_up_local.shape[1] // 2
+    dev = x.device
+    if T > 0:
+        idx, logits = compute.route(x, w_router, router_bias, top_k, norm_topk_prob)
+        logits = _RouterLogits.apply(x, w_router, router_bias, logits.to(x.dtype))
+        probs = torch.softmax(logits, dim=-1, dtype=torch.float32)
+        idx = idx.long()
+        w = probs.gather(1, idx)
+        if norm_topk_prob:
+            w = w / w.sum(dim=-1, keepdim=True).clamp_min(1e-12)
+        w = w.to(x.dtype)
+        sort_idx, counts = compute.sort(idx, num_experts)
+        sorted_token = torch.div(sort_idx, top_k, rounding_mode="floor")
+        x_sorted = x.index_select(0, sorted_token)
+        w_sorted = w.reshape(-1).index_select(0, sort_idx)
+    else:
+        idx = torch.empty((0, top_k), dtype=torch.long, device=dev)
+        probs = torch.empty((0, num_experts), dtype=torch.float32, device=dev)
+        counts = torch.zeros(num_experts, dtype=torch.int32, device=dev)
+        sorted_token = torch.empty(0, dtype=torch.long, device=dev)
+        x_sorted = x[:0]
+        w_sorted = x.new_empty(0)
+    aux = expert_counts = None
+    if aux_tokens >= 0:
+        n = min(aux_tokens, T)
+        aux = load_balancing_loss(probs[:n], idx[:n], num_experts)
+        with torch.no_grad():
+            expert_counts = torch.bincount(idx[:n].reshape(-1), minlength=num_experts).to(
+                torch.float32)
+    # counts of my experts from every source: recv_counts[s * el + e]
+    counts = counts.to(torch.int32).contiguous()
+    recv_counts = torch.empty_like(counts)
+    dist.all_to_all_single(recv_counts, counts, group=group)
+    splits = torch.cat([counts.view(world, el).sum(1), recv_counts.view(world, el).sum(1)])
+    splits = splits.cpu().tolist()
+    send_splits, recv_splits = splits[:world], splits[world:]
+    recv_rows = _AllToAllRows.apply(x_sorted, send_splits, recv_splits, group)
+    # received rows come as (source, local expert) blocks: order them by
+    # local expert for the grouped GEMMs, and back afterwards
+    rc = recv_counts.view(world, el).to(torch.long)
+    starts = (torch.cumsum(rc.reshape(-1), 0) - rc.reshape(-1)).view(world, el)
+    if recv_rows.shape[0] > 0:
+        pieces = [torch.arange(int(starts[s, e]), int(starts[s, e] + rc[s, e]), device=dev)
+                  for e in range(el) for s in range(world)]
+        perm = torch.cat(pieces)
+        rows_e = recv_rows.index_select(0, perm)
+        counts_e = rc.sum(0).to(torch.int32)
+        gate_up = compute.grouped_linear(rows_e, w_gate_up_local, counts_e)
+        h = torch.nn.functional.silu(gate_up[:, :inter]) * gate_up[:, inter:]
+        y_e = compute.grouped_linear(h, w_down_local, counts_e)
+        inv = torch.empty_like(perm)
+        inv[perm] = torch.arange(perm.numel(), device=dev)
+        y_rows = y_e.index_select(0, inv)
+    else:
+        # no rows here: still a node of the graph (through the rows and the
+        # weights), so that every rank runs the backward all_to_all
+        y_rows = recv_rows * 0 + 0 * (w_gate_up_local.sum() + w_down_local.sum()).to(recv_rows.dtype)
+    back = _AllToAllRows.apply(y_rows, recv_splits, send_splits, group)
+    if T > 0:
+        y = torch.zeros_like(x).index_add(0, sorted_token, (back * w_sorted[:, None]).to(x.dtype))
+    else:
+        # no tokens here: y still depends on the returned rows, so that this
+        # rank's backward runs the all_to_all its peers' backward waits for
+        y = torch.zeros_like(x) + 0 * back.sum()
+    return y, aux, expert_counts
+
+
 class PeerExpertParallel:
     """Expert parallelism over peer memory (hmoe_ep_forward), no host sync per call.
 
@@ -309,7 +472,10 @@ class SparseMoEExpertParallelSwiGLU(torch.nn.Module):
     ``experts.local_experts.down_weight`` [E/R, d, I] for this rank's experts.
 
     ``transport="nccl"`` (default) exchanges rows with NCCL all_to_all, as
-    the reference does.  ``transport="peer"`` runs the fused peer-memory path
+    the reference does.  Under autograd (or with a ``moe_context`` while
+    gradients are enabled) every transport runs :func:`ep_forward_train`,
+    the differentiable NCCL orchestration, and records ``aux_losses`` and
+    ``expert_counts`` where the reference does.  ``transport="peer"`` runs the fused peer-memory path
     (:class:`PeerExpertParallel`): it needs ``max_tokens`` (the most tokens any
     rank passes in one call, the same value on every rank), allocates its
     regions collectively on the first forward, and must be released with
@@ -343,13 +509,25 @@ class SparseMoEExpertParallelSwiGLU(torch.nn.Module):
         self._peer = None
 
     def forward(self, x, moe_context=None, total_seqlen=None, **_seq_info):
-        from .layers import _needs_grad
+        from .layers import _needs_grad, _valid_tokens
         le = self.experts.local_experts
-        if _needs_grad(x, self.gate.weight, le.gate_up_weight, le.down_weight):
-            raise NotImplementedError(
-                "the expert-parallel layer runs the forward pass only (the backward of its "
-                "all-to-all exchange is not built); run it under torch.no_grad() or train with "
-                "SparseMoESwiGLU on each GPU")
+        want_aux = moe_context is not None and torch.is_grad_enabled()
+        if want_aux or _needs_grad(x, self.gate.weight, le.gate_up_weight, le.down_weight):
+            # training: the differentiable NCCL orchestration (either transport)
+            shape = x.shape
+            h = x.reshape(-1, self.hidden_size)
+            aux_tokens = -1
+            if want_aux:
+                aux_tokens = (h.shape[0] if total_seqlen is None
+                              else _valid_tokens(total_seqlen, h.shape[0]))
+            y, aux, counts = ep_forward_train(
+                h, self.gate.weight.to(h.dtype), le.gate_up_weight.to(h.dtype),
+                le.down_weight.to(h.dtype), self.num_experts, self.top_k, self.norm_topk_prob,
+                group=self.group, aux_tokens=aux_tokens)
+            if want_aux:
+                moe_context.setdefault("aux_losses", []).append(aux)
+                moe_context.setdefault("expert_counts", []).append(counts)
+            return y.reshape(shape)
         shape = x.shape
         h = x.reshape(-1, self.hidden_size)
         wr, wgu, wd = (self.gate.weight.to(h.dtype), le.gate_up_weight.to(h.dtype),

@@ -3,7 +3,9 @@
 Every rank routes its own seeded tokens through ep.ep_forward (NCCL) and
 through the single-GPU layer with all experts; the two must agree bit for
 bit, because the rows meet the same kernels and the combine sees them in the
-same order.  Writes one line per rank to the file named by argv[1].
+same order.  Then the module trains one step under autograd
+(ep.ep_forward_train) against the single-GPU trainable layer.  Writes one
+line per rank to the file named by argv[1].
 """
 import datetime
 import importlib
@@ -16,6 +18,58 @@ import torch.distributed as dist
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 sys.path.insert(0, ROOT)
+
+
+def _max_rel(a, b):
+    a, b = a.float(), b.float()
+    return ((a - b).abs().max() / b.abs().max().clamp_min(1e-30)).item()
+
+
+def _train_check(rank, world, dev, syn, ep):
+    """The expert-parallel module under autograd (ep_forward_train, NCCL)
+    against the single-GPU trainable layer with all experts: y, the aux
+    loss and d_x of this rank's tokens, d_W_router of its tokens, and its
+    local experts' d_W against the single-GPU d_W summed over ranks; bf16,
+    max-rel 1e-2 per tensor."""
+    layers = importlib.import_module("hrm-moe_b200.layers")
+    T, d, E, I, k = 512 + 29 * rank, 256, 8 * world, 128, 4
+    inp = syn.make_inputs(syn.MoEShape(T, d, E, I, k, True, "bf16"), seed=31, rank=rank)
+    el = E // world
+    bf = torch.bfloat16
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev).to(bf)
+    one = layers.SparseMoESwiGLU(d, I, E, k, True).to(dev, bf)
+    mod = ep.SparseMoEExpertParallelSwiGLU(d, I, E, k, True).to(dev, bf)
+    with torch.no_grad():
+        one.gate.weight.copy_(t(inp.w_router))
+        one.experts.gate_up_weight.copy_(t(inp.w_gate_up))
+        one.experts.down_weight.copy_(t(inp.w_down))
+        mod.gate.weight.copy_(t(inp.w_router))
+        mod.experts.local_experts.gate_up_weight.copy_(t(inp.w_gate_up[rank * el:(rank + 1) * el]))
+        mod.experts.local_experts.down_weight.copy_(t(inp.w_down[rank * el:(rank + 1) * el]))
+    gy = torch.randn((T, d), generator=torch.Generator(device=dev).manual_seed(rank), device=dev)
+    x1 = t(inp.x).requires_grad_(True)
+    xe = t(inp.x).requires_grad_(True)
+    c1, ce = {}, {}
+    y1 = one(x1.unsqueeze(0), moe_context=c1).squeeze(0)
+    ye = mod(xe.unsqueeze(0), moe_context=ce).squeeze(0)
+    ((y1.float() * gy).sum() + c1["aux_losses"][0]).backward()
+    ((ye.float() * gy).sum() + ce["aux_losses"][0]).backward()
+    g_gu = one.experts.gate_up_weight.grad.float().clone()
+    g_d = one.experts.down_weight.grad.float().clone()
+    dist.all_reduce(g_gu)
+    dist.all_reduce(g_d)
+    errs = {
+        "y": _max_rel(ye, y1),
+        "aux": _max_rel(ce["aux_losses"][0], c1["aux_losses"][0]),
+        "dx": _max_rel(xe.grad, x1.grad),
+        "dw_router": _max_rel(mod.gate.weight.grad, one.gate.weight.grad),
+        "dw_gate_up": _max_rel(mod.experts.local_experts.gate_up_weight.grad, g_gu[rank * el:(rank + 1) * el]),
+        "dw_down": _max_rel(mod.experts.local_experts.down_weight.grad, g_d[rank * el:(rank + 1) * el]),
+    }
+    counts_ok = torch.equal(ce["expert_counts"][0], c1["expert_counts"][0])
+    ok = counts_ok and all(v <= 1e-2 for v in errs.values())
+    return ok, ("train " + ("ok" if ok else "BAD") + f" counts {'equal' if counts_ok else 'DIFFER'} "
+                + " ".join(f"{k2} {v:.1e}" for k2, v in errs.items()))
 
 
 def main(out_path):
@@ -85,6 +139,9 @@ def main(out_path):
             ok &= same and same_p
             msgs.append(f"T={shape.tokens} E={E} {dtype} skew={skew}: nccl {'equal' if same else 'DIFFER'}, "
                         f"p2p {'equal' if same_p else 'DIFFER max %g' % (y_p2p.float() - y_1.float()).abs().max().item()}")
+        ok_t, msg_t = _train_check(rank, world, dev, syn, ep)
+        ok &= ok_t
+        msgs.append(msg_t)
         dist.barrier()
     except Exception as e:  # report, then leave the group cleanly
         ok = False
