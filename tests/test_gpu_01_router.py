@@ -79,6 +79,27 @@ def test_router_seeded(T, d, E, k, dtype, seed):
     _check_against_oracle(x, w, None, k, True, dtype)
 
 
+@pytest.mark.parametrize("T,d,E,k,bias,seed", [
+    (3000, 2048, 64, 8, False, 21),   # resident weight half of 16 k-blocks, 4 ring stages
+    (1000, 2560, 64, 8, False, 22),   # too large to keep resident: the row-split pass
+    (700, 1536, 96, 8, True, 23),     # 64 < E < 128: the streamed-weight pair pass
+    (513, 1536, 64, 16, False, 24),   # k > 8
+    (257, 512, 64, 1, True, 25),      # k = 1
+    (129, 256, 128, 32, False, 26),   # E = 128, k = 32
+    (5000, 1536, 32, 8, False, 27),   # E below the configuration's 64
+    (64, 1536, 64, 8, False, 28),     # one pair tile, the odd CTA without tokens
+    (129, 1536, 64, 8, True, 29),     # a second tile of one token
+])
+def test_router_pair_pass_shapes(T, d, E, k, bias, seed):
+    """Shapes at the pair pass's edges: its routing must equal the
+    exact-order routing bit for bit, as every pass's."""
+    rng = np.random.default_rng(seed)
+    x = O.round_to_bf16(rng.standard_normal((T, d), dtype=np.float32))
+    w = O.round_to_bf16(rng.standard_normal((E, d), dtype=np.float32) * np.float32(0.02))
+    b = O.round_to_bf16(rng.standard_normal(E).astype(np.float32) * np.float32(0.1)) if bias else None
+    _check_against_oracle(x, w, b, k, True, "bf16")
+
+
 def test_router_norm_false_and_bias():
     rng = np.random.default_rng(11)
     x = O.round_to_bf16(rng.standard_normal((500, 256), dtype=np.float32))
