@@ -511,7 +511,7 @@ def measure_train_step(torch, lib, _lib, ops, shape, x, w_router, bias, w_gate_u
             "what": "forward that keeps activations (aux loss over all tokens) + backward of "
                     "sum(y * grad_y) + aux: grads of x, router weight, both expert weights",
             "expert_gemm_tflops": flops / (total * 1e-3) / 1e12, "phases": phases,
-            "gpu_launches_per_step": 18 if bias is None else 20}
+            "gpu_launches_per_step": 17 if bias is None else 19}
 
 
 # ------------------------------------------------------------- B200 arm --
@@ -890,11 +890,11 @@ def b200_arm(args, rank, world, local_rank):
         "ms_per_step_eager": ms_eager,
         "cpu_baseline": cpu,
         "e2e": e2e,
-        # ours per step: router (2), dispatch (3), 2 GEMMs, combine; the peer
-        # path adds the exchange and one wait (the row push runs inside the
-        # gate_up GEMM, the return inside the down GEMM); NCCL's own kernels
-        # are not counted
-        "gpu_launches": (10 if peer is not None else 8) * args.steps,
+        # ours per step: router (1: the pair pass fixes its tokens itself),
+        # dispatch (3), 2 GEMMs, combine; the peer path adds the exchange and
+        # one wait (the row push runs inside the gate_up GEMM, the return
+        # inside the down GEMM); NCCL's own kernels are not counted
+        "gpu_launches": (9 if peer is not None else 7) * args.steps,
         "clocks": clk,
     }
     if ep_parity is not None:
