@@ -12,7 +12,10 @@ copied in from pinned host memory and the output read back every step.
 Timing: W untimed warm-up steps, then K steps, each bracketed by CUDA events
 on the launching stream; a 256 MiB buffer (2x the L2) is rewritten before
 every step, outside the events.  Per-stage times come from events the C ABI
-records between its kernels (hmoe_ffn_forward_marked) in the same steps.
+records between its kernels (hmoe_ffn_forward_marked): at N=1 from the
+marked layer captured as one CUDA graph like the timed steps (the events
+become graph nodes; read after each of up to 50 replays, untimed), with the
+eager steps' per-stage times beside them; at N>1 from the timed steps.
 Multi-GPU runs take the max over ranks.
 """
 from __future__ import annotations
@@ -685,6 +688,7 @@ def b200_arm(args, rank, world, local_rank):
     # the first call), so a serving loop captures the layer once and replays
     # it; the K timed steps are K replays, each after the L2 flush.
     graph_used = False
+    phases_eager_ms = None
     if world == 1 and not args.no_graph:
         cap = torch.cuda.Stream(dev)
         cap.wait_stream(stream)
@@ -713,6 +717,32 @@ def b200_arm(args, rank, world, local_rank):
         ms = statistics.mean(a.elapsed_time(b) for a, b in zip(g_s, g_e))
         graph_used = True
         del graph
+        # Per-stage times of the same graph form: the marked layer captured
+        # once (its events become event-record nodes of the graph) and
+        # replayed after the L2 flush, read after each replay (untimed).
+        gm = make_events(n_marks)
+        mgraph = torch.cuda.CUDAGraph()
+        cap.wait_stream(stream)
+        with torch.cuda.graph(mgraph, stream=cap, capture_error_mode="relaxed"):
+            arr = (ctypes.c_void_p * n_marks)(*[ctypes.c_void_p(m.cuda_event) for m in gm])
+            _lib.check(lib.hmoe_ffn_forward_marked(
+                ctypes.byref(cshape), ctypes.c_void_p(x.data_ptr()),
+                ctypes.c_void_p(w_router.data_ptr()), bias_p, ctypes.c_void_p(w_gate_up.data_ptr()),
+                ctypes.c_void_p(w_down.data_ptr()), ctypes.c_void_p(y.data_ptr()), 0,
+                ctypes.c_void_p(ws.data_ptr()), ws.numel(), ctypes.c_void_p(cap.cuda_stream), arr))
+        stream.wait_stream(cap)
+        graph_phase = {n: [] for n in phase_names}
+        for r in range(max(3, min(args.steps, 50)) + 2):
+            flush.zero_()
+            mgraph.replay()
+            torch.cuda.synchronize()
+            if r >= 2:
+                for i, n in enumerate(phase_names):
+                    graph_phase[n].append(gm[i].elapsed_time(gm[i + 1]))
+        ops.workspace_status(ws)
+        del mgraph
+        phases_eager_ms = phase_ms
+        phase_ms = {n: statistics.mean(v) for n, v in graph_phase.items()}
 
     # ------------------------------------------------- end to end (public API)
     # The C ABI on pinned HOST buffers (hmoe_ffn_forward_host): every step
@@ -887,7 +917,11 @@ def b200_arm(args, rank, world, local_rank):
         "phases": phases,
         "launch": ("one CUDA graph per step (the layer captured once, replayed K times)"
                    if graph_used else "eager launches"),
+        "phases_source": ("the marked layer as one CUDA graph, events recorded by graph nodes, "
+                          "mean over replays after the L2 flush" if graph_used
+                          else "events between the kernels of the timed steps"),
         "ms_per_step_eager": ms_eager,
+        "phases_eager_ms": phases_eager_ms,
         "cpu_baseline": cpu,
         "e2e": e2e,
         # ours per step: router (1: the pair pass fixes its tokens itself),

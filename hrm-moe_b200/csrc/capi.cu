@@ -268,11 +268,19 @@ int run_grouped(const void* a, const void* b, const int32_t* counts, int64_t M, 
 
 // Experts on routed tokens: dispatch, two grouped GEMMs, combine.
 // Optional timing marks between stages (events[i] recorded after stage i).
+// Under stream capture a mark becomes an event-record node of the graph
+// (cudaEventRecordExternal), so each replay records it and the caller can
+// time the stages of a replay.
 struct PhaseMarks {
   void* const* ev = nullptr;
   int mark(int i, cudaStream_t st) const {
     if (ev && ev[i]) {
-      cudaError_t e = cudaEventRecord(static_cast<cudaEvent_t>(ev[i]), st);
+      cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+      cudaError_t e = cudaStreamIsCapturing(st, &cs);
+      if (e == cudaSuccess)
+        e = cs == cudaStreamCaptureStatusActive
+                ? cudaEventRecordWithFlags(static_cast<cudaEvent_t>(ev[i]), st, cudaEventRecordExternal)
+                : cudaEventRecord(static_cast<cudaEvent_t>(ev[i]), st);
       if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
     }
     return HMOE_OK;

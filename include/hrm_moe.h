@@ -99,7 +99,9 @@ int hmoe_ffn_forward_host(const hmoe_shape* shape, const void* x_host, const voi
  * hmoe_ffn_forward with timing marks: phase_events points to 6 cudaEvent_t
  * (NULL entries skipped) recorded on the stream before the router, after
  * the router, after dispatch, after the gate_up GEMM, after the down GEMM
- * and after the combine.  Same kernels, same results.
+ * and after the combine.  Same kernels, same results.  Under stream
+ * capture the marks become event-record nodes of the graph, recorded by
+ * every replay.
  */
 int hmoe_ffn_forward_marked(const hmoe_shape* shape, const void* x, const void* w_router,
                             const void* router_bias, const void* w_gate_up, const void* w_down,
