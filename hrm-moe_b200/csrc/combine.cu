@@ -66,7 +66,7 @@ combine_kernel(const void* __restrict__ expert_out, const int32_t* __restrict__ 
   const uint4* fin = static_cast<const uint4*>(final_in);
   uint4* dst = static_cast<uint4*>(out);
   constexpr int EPC = BF16 ? 8 : 4;  // elements per 16-byte chunk
-  constexpr int kBatch = 4;          // rows loaded before they are summed
+  constexpr int kBatch = 8;          // rows loaded before they are summed
   // every lane runs the same trip count so the shuffles below see all 32 lanes
   for (int c0 = cfirst; c0 < cend; c0 += 32) {
     const int c = c0 + lane;
