@@ -80,8 +80,9 @@ def parse_args():
                     help="N=1: skip the training-step measurement (forward that keeps its "
                          "activations + the full backward with the aux loss)")
     ap.add_argument("--train-steps", type=int, default=50)
-    ap.add_argument("--e2e-chunk", type=int, default=4096,
-                    help="tokens per host-copy chunk of the end-to-end measurement")
+    ap.add_argument("--e2e-chunk", type=int, default=3584,
+                    help="tokens per host-copy chunk of the end-to-end measurement (at N=1 "
+                         "3584 measured best of 2560-4096 for 16K tokens)")
     ap.add_argument("--no-graph", action="store_true",
                     help="N=1: time eager launches instead of one CUDA graph per step")
     ap.add_argument("--ep-impl", default="peer", choices=["peer", "nccl"],
