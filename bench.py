@@ -80,9 +80,10 @@ def parse_args():
                     help="N=1: skip the training-step measurement (forward that keeps its "
                          "activations + the full backward with the aux loss)")
     ap.add_argument("--train-steps", type=int, default=50)
-    ap.add_argument("--e2e-chunk", type=int, default=3584,
-                    help="tokens per host-copy chunk of the end-to-end measurement (at N=1 "
-                         "3584 measured best of 2560-4096 for 16K tokens)")
+    ap.add_argument("--e2e-chunk", type=int, default=0,
+                    help="tokens per host-copy chunk of the end-to-end measurement (default: "
+                         "3584 at N=1, the best of 2560-4096 measured for 16K tokens; 4096 for "
+                         "the expert-parallel layer, whose every call repeats the exchange)")
     ap.add_argument("--no-graph", action="store_true",
                     help="N=1: time eager launches instead of one CUDA graph per step")
     ap.add_argument("--ep-impl", default="peer", choices=["peer", "nccl"],
@@ -753,7 +754,7 @@ def b200_arm(args, rank, world, local_rank):
     if not args.no_e2e and ep is None:
         x_host = x.cpu().pin_memory()
         y_host = torch.empty_like(x_host).pin_memory()
-        chunk = min(T, args.e2e_chunk)
+        chunk = min(T, args.e2e_chunk or 3584)
         cs = ops.make_shape(T, d, E, I, k, dt, shape.norm_topk_prob)
         hws = torch.empty(lib.hmoe_ffn_host_workspace_bytes(ctypes.byref(cs), chunk),
                           dtype=torch.uint8, device=dev)
@@ -782,7 +783,7 @@ def b200_arm(args, rank, world, local_rank):
         # back to pinned host memory, in chunks whose copies overlap the layer
         x_host = x.cpu().pin_memory()
         y_host = torch.empty_like(x_host).pin_memory()
-        chunk = min(T, args.e2e_chunk)
+        chunk = min(T, args.e2e_chunk or 4096)
         e_s, e_e = make_events(args.steps), make_events(args.steps)
         dist.barrier()
         for i in range(args.warmup + args.steps):
