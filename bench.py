@@ -10,9 +10,11 @@ copied in from pinned host memory and the output read back every step.
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 
 Timing: W untimed warm-up steps, then K steps, each bracketed by CUDA events
-on the launching stream; a 256 MiB buffer (2x the L2) is rewritten before
-every step, outside the events.  Per-stage times come from events the C ABI
-records between its kernels (hmoe_ffn_forward_marked): at N=1 from the
+on the launching stream; before every step, outside the events, a 256 MiB
+buffer (2x the L2) is rewritten and a second one read, so that the step
+starts with no input in L2 and no dirty line of the flush left to write
+back.  Per-stage times come from events the C ABI records between its
+kernels (hmoe_ffn_forward_marked): at N=1 from the
 marked layer captured as one CUDA graph like the timed steps (the events
 become graph nodes; read after each of up to 50 replays, untimed), with the
 eager steps' per-stage times beside them; at N>1 from the timed steps.
@@ -37,6 +39,24 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "MoE-FFN fwd tokens/s (XL 64x8 bf16)"
 L2_FLUSH_BYTES = 256 << 20
+
+
+L2_NOTE = ("256 MiB buffer rewritten, then another 256 MiB read, before every step "
+           "(outside the timed events)")
+
+
+class L2Flush:
+    """Evicts the L2 before a step: writes one buffer twice the L2, then
+    reads another, so the lines left in L2 are clean and the step's first
+    kernel does not pay for writing the flush's own lines back to HBM."""
+
+    def __init__(self, torch, dev):
+        self.w = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+        self.r = torch.zeros(L2_FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
+
+    def __call__(self):
+        self.w.zero_()
+        self.r.max()
 # measured peer copy bandwidth per direction per GPU on this pool (NVLink 5)
 NVLINK_GBS = 770.0
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per forward of
@@ -361,19 +381,19 @@ def reference_gpu_arm(args, rank, world, local_rank):
             mod.gate.bias.copy_(bias)
         mod.experts.gate_up_weight.copy_(w_gate_up)
         mod.experts.down_weight.copy_(w_down)
-    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    flush = L2Flush(torch, dev)
     stream = torch.cuda.current_stream(dev)
     prof._MOE_PROFILE_ENABLED = False
     with torch.no_grad():
         for _ in range(max(1, args.warmup)):  # the first call autotunes the Triton kernels
-            flush.zero_()
+            flush()
             mod(x)
         torch.cuda.synchronize()
         starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
         ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
         with ClockSampler(gpu_uuid(torch, local_rank)) as clocks:
             for i in range(args.steps):
-                flush.zero_()
+                flush()
                 starts[i].record(stream)
                 y_ref = mod(x)
                 ends[i].record(stream)
@@ -385,7 +405,7 @@ def reference_gpu_arm(args, rank, world, local_rank):
         prof.reset_moe_profile()
         n_prof = min(20, args.steps)
         for _ in range(n_prof):
-            flush.zero_()
+            flush()
             mod(x)
         phases = {n: 1e3 * v / n_prof for n, v in prof.pop_moe_profile().items()}
         prof._MOE_PROFILE_ENABLED = False
@@ -416,7 +436,7 @@ def reference_gpu_arm(args, rank, world, local_rank):
                    "module": "models.layers.SparseMoESwiGLU(implementation='grouped_triton')",
                    "env": {k_: os.environ[k_] for k_ in ("HRM_MOE_TRITON_AUTOTUNE",
                                                          "HRM_MOE_TRITON_SM_MARGIN")},
-                   "l2": "256 MiB buffer rewritten before every step (outside the timed events)"},
+                   "l2": L2_NOTE},
         "phases_ms": phases,
         "gemms": gemm,
         "vs_b200_same_inputs": {
@@ -478,14 +498,14 @@ def measure_train_step(torch, lib, _lib, ops, shape, x, w_router, bias, w_gate_u
 
     warm = events(9)
     for _ in range(max(3, warmup)):
-        flush.zero_()
+        flush()
         step(warm)
     torch.cuda.synchronize()
     ops.workspace_status(ws)
     evs = [events(9) for _ in range(steps)]
     torch.cuda.synchronize()
     for i in range(steps):
-        flush.zero_()
+        flush()
         step(evs[i])
     torch.cuda.synchronize()
     ops.workspace_status(ws)
@@ -556,7 +576,7 @@ def b200_arm(args, rank, world, local_rank):
         zb = syn.zipf_router_bias(E, 4, dead_experts=args.dead_experts)
         bias = torch.from_numpy(zb).to(dev).to(dt)
     bias_p = ctypes.c_void_p(bias.data_ptr()) if bias is not None else None
-    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    flush = L2Flush(torch, dev)
 
     lib = _lib.load()
     cshape = ops.make_shape(T, d, E, I, k, dt, shape.norm_topk_prob)
@@ -612,7 +632,7 @@ def b200_arm(args, rank, world, local_rank):
 
     warm_marks = make_events(n_marks)
     for _ in range(args.warmup):
-        flush.zero_()
+        flush()
         step(warm_marks)
     torch.cuda.synchronize()
     ops.workspace_status(ws)
@@ -656,7 +676,7 @@ def b200_arm(args, rank, world, local_rank):
             dist.barrier()
         torch.cuda.synchronize()
         for i in range(args.steps):
-            flush.zero_()
+            flush()
             starts[i].record(stream)
             step(marks[i])
             ends[i].record(stream)
@@ -704,13 +724,13 @@ def b200_arm(args, rank, world, local_rank):
                 ctypes.c_void_p(cap.cuda_stream)))
         stream.wait_stream(cap)
         for _ in range(args.warmup):
-            flush.zero_()
+            flush()
             graph.replay()
         g_s, g_e = make_events(args.steps), make_events(args.steps)
         torch.cuda.synchronize()
         with ClockSampler(gpu_uuid(torch, local_rank)) as clocks:
             for i in range(args.steps):
-                flush.zero_()
+                flush()
                 g_s[i].record(stream)
                 graph.replay()
                 g_e[i].record(stream)
@@ -735,7 +755,7 @@ def b200_arm(args, rank, world, local_rank):
         stream.wait_stream(cap)
         graph_phase = {n: [] for n in phase_names}
         for r in range(max(3, min(args.steps, 50)) + 2):
-            flush.zero_()
+            flush()
             mgraph.replay()
             torch.cuda.synchronize()
             if r >= 2:
@@ -760,7 +780,7 @@ def b200_arm(args, rank, world, local_rank):
                           dtype=torch.uint8, device=dev)
         e_s, e_e = make_events(args.steps), make_events(args.steps)
         for i in range(args.warmup + args.steps):
-            flush.zero_()
+            flush()
             if i >= args.warmup:
                 e_s[i - args.warmup].record(stream)
             ops.ffn_forward_host(x_host, w_router, w_gate_up, w_down, k, shape.norm_topk_prob,
@@ -787,7 +807,7 @@ def b200_arm(args, rank, world, local_rank):
         e_s, e_e = make_events(args.steps), make_events(args.steps)
         dist.barrier()
         for i in range(args.warmup + args.steps):
-            flush.zero_()
+            flush()
             if i >= args.warmup:
                 e_s[i - args.warmup].record(stream)
             peer.forward_host(x_host, w_router, w_gate_up, w_down, y_host=y_host,
@@ -914,7 +934,7 @@ def b200_arm(args, rank, world, local_rank):
                                    f"expert parallel x{world} ({E // world} experts per GPU, "
                                    + ("rows over NVLink peer memory, no host sync)"
                                       if peer is not None else "NCCL all_to_all)")),
-                   "l2": "256 MiB buffer rewritten before every step (outside the timed events)"},
+                   "l2": L2_NOTE},
         "roofline": roofline,
         "phases": phases,
         "launch": ("one CUDA graph per step (the layer captured once, replayed K times)"

@@ -103,6 +103,7 @@ SIGNATURES = {
     "hmoe_combine": (c_int, [ShapeP, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                              c_size_t, c_void_p]),
     "hmoe_workspace_status": (c_int, [c_void_p, c_void_p]),
+    "hmoe_set_pdl_mask": (ctypes.c_uint, [ctypes.c_uint]),
     "hmoe_ep_symmetric_bytes": (c_size_t, [ShapeP, c_int64, c_int32]),
     "hmoe_ep_workspace_bytes": (c_size_t, [ShapeP, c_int64, c_int32]),
     "hmoe_ep_symmetric_alloc": (c_int, [c_size_t, ctypes.POINTER(c_void_p), c_void_p]),

@@ -9,6 +9,7 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <atomic>
 #include <mutex>
 #include <cstdlib>
 #include <cstring>
@@ -330,6 +331,17 @@ int report_error(int code, const char* fmt, ...) {
 }
 
 int make_device_current(const void* ptr) { return select_device(ptr); }
+
+std::atomic<unsigned>& pdl_mask() {
+  static std::atomic<unsigned> mask{[] {
+    const char* v = std::getenv("HMOE_PDL");
+    return v ? static_cast<unsigned>(std::strtoul(v, nullptr, 0))
+             : static_cast<unsigned>(kPdlRouter | kPdlDispatch | kPdlGemm);
+  }()};
+  return mask;
+}
+
+bool pdl_enabled(unsigned cls) { return (pdl_mask().load(std::memory_order_relaxed) & cls) != 0; }
 
 int validate_shape_public(const hmoe_shape* shape) { return validate_shape(shape); }
 
@@ -1299,6 +1311,11 @@ int hmoe_workspace_status(const void* workspace, void* stream) {
     return fail(HMOE_EIO, "expert-parallel counts exceeded the symmetric buffers");
   if (word != kDevOk) return fail(HMOE_EIO, "unknown device error word %d", word);
   return HMOE_OK;
+}
+
+unsigned hmoe_set_pdl_mask(unsigned mask) {
+  return hmoe::pdl_mask().exchange(mask & (hmoe::kPdlRouter | hmoe::kPdlDispatch | hmoe::kPdlGemm |
+                                           hmoe::kPdlCombine));
 }
 
 }  // extern "C"

@@ -26,6 +26,8 @@ __global__ void __launch_bounds__(kCombThreads)
 combine_kernel(const void* __restrict__ expert_out, const int32_t* __restrict__ pos,
                const void* __restrict__ topk_w, int topk_w_is_f32, int64_t T, int row_chunks,
                int k, const void* __restrict__ final_in, void* __restrict__ out) {
+  grid_dependency_wait();  // launched early (launch_pdl): the expert rows are written before this
+  grid_launch_dependents();
   const int lane = threadIdx.x & 31;
   const int64_t wid = static_cast<int64_t>(blockIdx.x) * (kCombThreads / 32) + (threadIdx.x >> 5);
   const int ncb = SPLIT ? (row_chunks + 31) / 32 : 1;  // warps per token
@@ -151,18 +153,21 @@ cudaError_t launch_combine(const void* expert_out, const int32_t* pos, const voi
   const unsigned blocks = static_cast<unsigned>(
       cdiv64(T * (split ? cdiv(row_chunks, 32) : 1), kCombThreads / 32));
   if (bf16 && split)
-    combine_kernel<true, true><<<blocks, kCombThreads, 0, stream>>>(
-        expert_out, pos, topk_w, topk_w_is_f32, T, row_chunks, k, final_in, out);
+    return launch_pdl(kPdlCombine, combine_kernel<true, true>, dim3(blocks), dim3(kCombThreads), 0,
+                      stream, expert_out, pos, topk_w, topk_w_is_f32, T, row_chunks, k, final_in,
+                      out);
   else if (bf16)
-    combine_kernel<true, false><<<blocks, kCombThreads, 0, stream>>>(
-        expert_out, pos, topk_w, topk_w_is_f32, T, row_chunks, k, final_in, out);
+    return launch_pdl(kPdlCombine, combine_kernel<true, false>, dim3(blocks), dim3(kCombThreads), 0,
+                      stream, expert_out, pos, topk_w, topk_w_is_f32, T, row_chunks, k, final_in,
+                      out);
   else if (split)
-    combine_kernel<false, true><<<blocks, kCombThreads, 0, stream>>>(
-        expert_out, pos, topk_w, topk_w_is_f32, T, row_chunks, k, final_in, out);
+    return launch_pdl(kPdlCombine, combine_kernel<false, true>, dim3(blocks), dim3(kCombThreads), 0,
+                      stream, expert_out, pos, topk_w, topk_w_is_f32, T, row_chunks, k, final_in,
+                      out);
   else
-    combine_kernel<false, false><<<blocks, kCombThreads, 0, stream>>>(
-        expert_out, pos, topk_w, topk_w_is_f32, T, row_chunks, k, final_in, out);
-  return cudaGetLastError();
+    return launch_pdl(kPdlCombine, combine_kernel<false, false>, dim3(blocks), dim3(kCombThreads),
+                      0, stream, expert_out, pos, topk_w, topk_w_is_f32, T, row_chunks, k,
+                      final_in, out);
 }
 
 }  // namespace hmoe

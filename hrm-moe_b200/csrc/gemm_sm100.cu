@@ -286,6 +286,7 @@ grouped_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
 
   // ---------------------------------------------------------------- setup
   if (warp == 0) {
+    grid_dependency_wait();  // launched early (launch_pdl): the counts are written before this
     const int per = cdiv(G, 32);
     const int g0 = min(G, lane * per), g1 = min(G, g0 + per);
     int rows = 0, tiles = 0;
@@ -352,6 +353,8 @@ grouped_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  grid_dependency_wait();
+  grid_launch_dependents();
 
   const uint32_t tmem_base = ctl.tmem_base;
   const int num_tiles = ctl.num_m_tiles * p.n_tiles;
@@ -742,21 +745,20 @@ cudaError_t launch_grouped_gemm_sm100(const GroupedGemmArgs& a, cudaStream_t str
     e = cudaLaunchCooperativeKernel(
         reinterpret_cast<const void*>(&grouped_gemm_sm100_kernel<true, false, true>), dim3(grid),
         dim3(num_threads<true, false, true>()), args, kSmemBytes, stream);
-    if (e != cudaSuccess) return e;
   } else if (a.swiglu) {
     if ((e = ensure_smem_attr<true, false, false>()) != cudaSuccess) return e;
-    grouped_gemm_sm100_kernel<true, false, false>
-        <<<grid, num_threads<true, false, false>(), kSmemBytes, stream>>>(ma, mb, mc, p);
+    e = launch_pdl(kPdlGemm, grouped_gemm_sm100_kernel<true, false, false>, dim3(grid),
+                   dim3(num_threads<true, false, false>()), kSmemBytes, stream, ma, mb, mc, p);
   } else if (scatter) {
     if ((e = ensure_smem_attr<false, true, false>()) != cudaSuccess) return e;
-    grouped_gemm_sm100_kernel<false, true, false>
-        <<<grid, num_threads<false, true, false>(), kSmemBytes, stream>>>(ma, mb, mc, p);
+    e = launch_pdl(kPdlGemm, grouped_gemm_sm100_kernel<false, true, false>, dim3(grid),
+                   dim3(num_threads<false, true, false>()), kSmemBytes, stream, ma, mb, mc, p);
   } else {
     if ((e = ensure_smem_attr<false, false, false>()) != cudaSuccess) return e;
-    grouped_gemm_sm100_kernel<false, false, false>
-        <<<grid, num_threads<false, false, false>(), kSmemBytes, stream>>>(ma, mb, mc, p);
+    e = launch_pdl(kPdlGemm, grouped_gemm_sm100_kernel<false, false, false>, dim3(grid),
+                   dim3(num_threads<false, false, false>()), kSmemBytes, stream, ma, mb, mc, p);
   }
-  return cudaGetLastError();
+  return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 }  // namespace hmoe

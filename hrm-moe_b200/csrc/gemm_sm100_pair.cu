@@ -156,6 +156,7 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA,
 
   // ---------------------------------------------------------------- setup
   if (warp == 0) {
+    grid_dependency_wait();  // launched early (launch_pdl): the counts are written before this
     const int per = cdiv(G, 32);
     const int g0 = min(G, lane * per), g1 = min(G, g0 + per);
     int rows = 0, tiles = 0;
@@ -208,6 +209,8 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA,
   __syncthreads();
   cluster_sync_all();  // barrier inits visible to the peer CTA before any remote signal
   tc_fence_after();
+  grid_dependency_wait();
+  grid_launch_dependents();
 
   const uint32_t tmem_base = ctl.tmem_base;
   const int num_tiles = ctl.num_m_tiles * p.n_tiles;
@@ -494,18 +497,18 @@ cudaError_t launch_grouped_gemm_pair(const GroupedGemmArgs& a, cudaStream_t stre
   cudaError_t e;
   if (a.swiglu && a.save_gate_up) {
     if ((e = ensure_pair_attr<true, true>()) != cudaSuccess) return e;
-    grouped_gemm_pair_kernel<true, true><<<2 * pairs, pair_threads<true>(), kPSmemBytes, stream>>>(
-        ma, mb, mc, p);
+    e = launch_pdl(kPdlGemm, grouped_gemm_pair_kernel<true, true>, dim3(2 * pairs),
+                   dim3(pair_threads<true>()), kPSmemBytes, stream, ma, mb, mc, p);
   } else if (a.swiglu) {
     if ((e = ensure_pair_attr<true>()) != cudaSuccess) return e;
-    grouped_gemm_pair_kernel<true><<<2 * pairs, pair_threads<true>(), kPSmemBytes, stream>>>(
-        ma, mb, mc, p);
+    e = launch_pdl(kPdlGemm, grouped_gemm_pair_kernel<true>, dim3(2 * pairs),
+                   dim3(pair_threads<true>()), kPSmemBytes, stream, ma, mb, mc, p);
   } else {
     if ((e = ensure_pair_attr<false>()) != cudaSuccess) return e;
-    grouped_gemm_pair_kernel<false><<<2 * pairs, pair_threads<false>(), kPSmemBytes, stream>>>(
-        ma, mb, mc, p);
+    e = launch_pdl(kPdlGemm, grouped_gemm_pair_kernel<false>, dim3(2 * pairs),
+                   dim3(pair_threads<false>()), kPSmemBytes, stream, ma, mb, mc, p);
   }
-  return cudaGetLastError();
+  return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 }  // namespace hmoe

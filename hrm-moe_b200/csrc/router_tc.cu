@@ -1577,6 +1577,8 @@ router_pair_kernel(const __grid_constant__ CUtensorMap tmX2, const __grid_consta
   __syncthreads();
   cluster_sync_all();  // barrier inits visible to the peer CTA before any remote signal
   tc_fence_after();
+  grid_dependency_wait();  // launched early (launch_pdl): no global access before this
+  grid_launch_dependents();
   const uint32_t tmem = ctl.tmem_base;
   volatile int* abort = &ctl.abort;
   int never = 0;
@@ -1847,10 +1849,10 @@ cudaError_t launch_pair_tc(const void* x, const void* w, const RtParams& p, cuda
   const int64_t ntiles = cdiv64(p.T, 2 * kRpTok);
   const int sms = num_sms_for_current_device();
   const int64_t pairs = ntiles < sms / 2 ? ntiles : sms / 2;
-  router_pair_kernel<EMAX, KMAX, KFIX><<<static_cast<unsigned>(2 * (pairs < 1 ? 1 : pairs)), kRpThreads,
-                             C::smem(nkb, stages), st>>>(
-      mx, mw, p, static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(w), stages);
-  return cudaGetLastError();
+  return launch_pdl(kPdlRouter, router_pair_kernel<EMAX, KMAX, KFIX>,
+                    dim3(static_cast<unsigned>(2 * (pairs < 1 ? 1 : pairs))), dim3(kRpThreads),
+                    C::smem(nkb, stages), st, mx, mw, p, static_cast<const uint16_t*>(x),
+                    static_cast<const uint16_t*>(w), stages);
 }
 
 template <int EPAD, int KMAX>

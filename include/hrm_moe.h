@@ -390,6 +390,18 @@ int hmoe_ffn_backward_marked(const hmoe_shape* shape, const void* grad_y, const 
  */
 int hmoe_workspace_status(const void* workspace, void* stream);
 
+/*
+ * Programmatic dependent launch: the classes of the layer's forward kernels
+ * (1 router pass, 2 dispatch, 4 grouped GEMMs, 8 combine) launched so that
+ * their launch and on-chip setup overlap the tail of the kernel before them
+ * (each still waits for that kernel's results before touching memory).
+ * The environment variable HMOE_PDL gives the initial mask (default 7:
+ * every class but the combine).
+ * Affects launches made after the call; a captured CUDA graph keeps the
+ * launches it was captured with.  Returns the previous mask.
+ */
+unsigned hmoe_set_pdl_mask(unsigned mask);
+
 #ifdef __cplusplus
 }
 #endif

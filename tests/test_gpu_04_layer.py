@@ -186,3 +186,41 @@ def test_host_buffer_pipeline_matches_device_path(T, chunk):
     torch.cuda.synchronize()
     y_dev = ops.ffn_forward(x_host.cuda(), *w, 8, True).cpu()
     assert torch.equal(y_host, y_dev)
+
+
+@pytest.mark.parametrize("T,E", [(64, 64), (1000, 64), (16384, 64), (3000, 128)])
+def test_programmatic_launch_same_bits(T, E):
+    """Kernels launched with programmatic dependent launch (every class, the
+    combine included) give the bits of plain launches, eagerly and replayed
+    from a captured CUDA graph; the layer at small T runs the single-CTA
+    GEMM, at large T the CTA-pair GEMM."""
+    import importlib
+
+    ops = get_ops()
+    lib = importlib.import_module("hrm-moe_b200._lib").load()
+    shape = synthetic().MoEShape(T, 1536, E, 512, 8, True, "bf16")
+    inp = synthetic().make_inputs(shape, seed=17)
+    x, wr, wgu, wd = (to_dev(a, "bf16") for a in (inp.x, inp.w_router, inp.w_gate_up, inp.w_down))
+    old = lib.hmoe_set_pdl_mask(0)
+    try:
+        ref, r0 = ops.ffn_forward(x, wr, wgu, wd, 8, True, return_routing=True)
+        lib.hmoe_set_pdl_mask(15)
+        y, r1 = ops.ffn_forward(x, wr, wgu, wd, 8, True, return_routing=True)
+        out = torch.empty_like(ref)
+        cap = torch.cuda.Stream()
+        cap.wait_stream(torch.cuda.current_stream())
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=cap, capture_error_mode="relaxed"):
+            ops.ffn_forward(x, wr, wgu, wd, 8, True, out=out)
+        torch.cuda.current_stream().wait_stream(cap)
+        for _ in range(3):
+            out.zero_()
+            g.replay()
+        torch.cuda.synchronize()
+        del g
+    finally:
+        lib.hmoe_set_pdl_mask(old)
+    assert torch.equal(y, ref)
+    assert torch.equal(out, ref)
+    for key in r0:
+        assert torch.equal(r1[key], r0[key]), key
