@@ -214,8 +214,13 @@ int sm_margin() {
 int run_dispatch(const hmoe_shape& s, const int32_t* idx, const void* w, int w_is_f32,
                  const void* x, const DispatchBufs& b, int32_t* pos, int32_t* sort_idx,
                  int32_t* sorted_token, void* sorted_w, void* x_sorted, cudaStream_t st) {
-  const int64_t nblk = dispatch_num_blocks(s.tokens, s.top_k);
-  (void)nblk;
+  if (dispatch_fits_one_block(s.tokens, s.top_k)) {
+    HMOE_CUDA(launch_dispatch_small(idx, w, w_is_f32, x, s.tokens, s.hidden, s.top_k, s.experts,
+                                    s.dtype, b.counts, pos, sort_idx, sorted_token, sorted_w,
+                                    x_sorted, b.err, st),
+              "dispatch_small");
+    return HMOE_OK;
+  }
   HMOE_CUDA(launch_hist_scan(idx, s.tokens, s.top_k, s.experts, b.local_rank, b.block_counts,
                              b.counts, b.err, st), "hist_rank/scan");
   HMOE_CUDA(launch_permute_gather(idx, b.local_rank, b.block_counts, b.counts, w, w_is_f32, x, s.tokens,

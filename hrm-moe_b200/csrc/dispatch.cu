@@ -172,6 +172,46 @@ __device__ __forceinline__ void expert_bases(const int32_t* __restrict__ counts,
 constexpr int kPermThreads = 256;
 constexpr int kPermSeg = 8;  // 16-byte chunks per lane held in registers at a time
 
+// Routing records of assignment f (token t) at sorted position p.
+__device__ __forceinline__ void write_record(int p, int64_t f, int64_t t, const void* topk_w,
+                                             int topk_w_is_f32, int dtype, int32_t* sort_idx,
+                                             int32_t* sorted_token, void* sorted_w) {
+  if (sort_idx) sort_idx[p] = static_cast<int32_t>(f);
+  if (sorted_token) sorted_token[p] = static_cast<int32_t>(t);
+  if (sorted_w) {
+    const float w = topk_w_is_f32 ? static_cast<const float*>(topk_w)[f]
+                                  : load_elem(topk_w, f, dtype);
+    store_elem(sorted_w, p, w, dtype);
+  }
+}
+
+// Slice cb (of ncb) of token t's row to its k positions; lane j < k holds
+// position j (< 0: not placed).
+__device__ __forceinline__ void copy_row_slice(const uint4* __restrict__ src,
+                                               uint4* __restrict__ x_sorted, int row_chunks,
+                                               int ncb, int cb, int k, int p, int lane) {
+  const int span = ncb == 1 ? row_chunks : cdiv(row_chunks, 32 * ncb) * 32;
+  const int cbeg = cb * span, cend = min(row_chunks, cbeg + span);
+  for (int c0 = cbeg; c0 < cend; c0 += 32 * kPermSeg) {
+    uint4 buf[kPermSeg];
+#pragma unroll
+    for (int s = 0; s < kPermSeg; ++s) {
+      const int c = c0 + s * 32 + lane;
+      if (c < cend) buf[s] = __ldg(src + c);
+    }
+    for (int j = 0; j < k; ++j) {
+      const int pj = __shfl_sync(0xffffffffu, p, j);
+      if (pj < 0) continue;
+      uint4* dst = x_sorted + static_cast<int64_t>(pj) * row_chunks;
+#pragma unroll
+      for (int s = 0; s < kPermSeg; ++s) {
+        const int c = c0 + s * 32 + lane;
+        if (c < cend) dst[c] = buf[s];
+      }
+    }
+  }
+}
+
 __global__ void __launch_bounds__(kPermThreads)
 permute_gather_kernel(const int32_t* __restrict__ topk_idx, const int32_t* __restrict__ local_rank,
                       const int32_t* __restrict__ block_offsets, const int32_t* __restrict__ counts,
@@ -199,40 +239,123 @@ permute_gather_kernel(const int32_t* __restrict__ topk_idx, const int32_t* __res
     const int r = local_rank[f];
     if (e >= 0 && e < E && r >= 0) {
       p = base[e] + block_offsets[blk * E + e] + r;
-      if (cb == 0) {
-        if (sort_idx) sort_idx[p] = static_cast<int32_t>(f);
-        if (sorted_token) sorted_token[p] = static_cast<int32_t>(t);
-        if (sorted_w) {
-          const float w = topk_w_is_f32 ? static_cast<const float*>(topk_w)[f]
-                                        : load_elem(topk_w, f, dtype);
-          store_elem(sorted_w, p, w, dtype);
-        }
-      }
+      if (cb == 0)
+        write_record(p, f, t, topk_w, topk_w_is_f32, dtype, sort_idx, sorted_token, sorted_w);
     }
     if (cb == 0) pos[f] = p;
   }
   if (!x_sorted) return;
-  const int span = ncb == 1 ? row_chunks : cdiv(row_chunks, 32 * ncb) * 32;
-  const int cbeg = cb * span, cend = min(row_chunks, cbeg + span);
-  const uint4* src = static_cast<const uint4*>(x) + t * row_chunks;
-  for (int c0 = cbeg; c0 < cend; c0 += 32 * kPermSeg) {
-    uint4 buf[kPermSeg];
+  copy_row_slice(static_cast<const uint4*>(x) + t * row_chunks, x_sorted, row_chunks, ncb, cb, k,
+                 p, lane);
+}
+
+// All of dispatch in one kernel when the T*k assignments fit one histogram
+// block (T*k <= kHistFlat): every CTA ranks all assignments in shared memory
+// (the hist_rank computation, repeated per CTA), CTA 0 writes the counts,
+// and each warp then places its slice of a token's row as permute_gather
+// does.  Same positions, one launch instead of two.
+__global__ void __launch_bounds__(kPermThreads)
+dispatch_small_kernel(const int32_t* __restrict__ topk_idx, const void* __restrict__ topk_w,
+                      int topk_w_is_f32, const void* __restrict__ x, int64_t T, int row_chunks,
+                      int k, int E, int dtype, int32_t* __restrict__ counts,
+                      int32_t* __restrict__ pos, int32_t* __restrict__ sort_idx,
+                      int32_t* __restrict__ sorted_token, void* __restrict__ sorted_w,
+                      uint4* __restrict__ x_sorted, int ncb, int* __restrict__ err) {
+  static_assert(kPermThreads == kHistThreads, "one histogram pass per CTA");
+  __shared__ int32_t cnt[kHistChunks][kMaxExperts];
+  __shared__ int32_t rank_s[kHistFlat];
+  __shared__ int32_t base[kMaxExperts + 1];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nflat = static_cast<int>(T * k);
+  const int nchunks = cdiv(nflat, 32);
+  for (int i = tid; i < kHistChunks * kMaxExperts; i += kHistThreads)
+    (&cnt[0][0])[i] = 0;
+  __syncthreads();
+  grid_dependency_wait();  // launched early (launch_pdl): the routing is written before this
+  grid_launch_dependents();
+
+  constexpr int kRounds = kHistChunks / (kHistThreads / 32);
+  int my_e[kRounds], my_rank[kRounds];
 #pragma unroll
-    for (int s = 0; s < kPermSeg; ++s) {
-      const int c = c0 + s * 32 + lane;
-      if (c < cend) buf[s] = __ldg(src + c);
-    }
-    for (int j = 0; j < k; ++j) {
-      const int pj = __shfl_sync(0xffffffffu, p, j);
-      if (pj < 0) continue;
-      uint4* dst = x_sorted + static_cast<int64_t>(pj) * row_chunks;
-#pragma unroll
-      for (int s = 0; s < kPermSeg; ++s) {
-        const int c = c0 + s * 32 + lane;
-        if (c < cend) dst[c] = buf[s];
+  for (int r = 0; r < kRounds; ++r) {
+    const int c = r * (kHistThreads / 32) + warp;
+    const int f = c * 32 + lane;
+    int e = -1;
+    if (f < nflat) {
+      e = topk_idx[f];
+      if (e < 0 || e >= E) {
+        if (blockIdx.x == 0) record_error(err, kDevBadExpert);
+        e = -1;
       }
     }
+    const unsigned m = __match_any_sync(0xffffffffu, e);
+    my_e[r] = e;
+    my_rank[r] = __popc(m & ((1u << lane) - 1u));
+    if (e >= 0 && lane == __ffs(m) - 1) cnt[c][e] = __popc(m);
   }
+  __syncthreads();
+  if (tid < E) {  // exclusive scan over chunks, per expert; the total is the count
+    int run = 0;
+    for (int c = 0; c < nchunks; ++c) {
+      const int v = cnt[c][tid];
+      cnt[c][tid] = run;
+      run += v;
+    }
+    base[tid] = run;
+    if (blockIdx.x == 0) counts[tid] = run;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int r = 0; r < kRounds; ++r) {
+    const int c = r * (kHistThreads / 32) + warp;
+    const int f = c * 32 + lane;
+    if (f < nflat) rank_s[f] = my_e[r] >= 0 ? cnt[c][my_e[r]] + my_rank[r] : -1;
+  }
+  // counts -> expert bases, in place (warp 0; E <= 128)
+  if (warp == 0) {
+    int c4[4], sum = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int e = lane * 4 + i;
+      c4[i] = e < E ? base[e] : 0;
+      sum += c4[i];
+    }
+    int incl = sum;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int o = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += o;
+    }
+    int run = incl - sum;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int e = lane * 4 + i;
+      if (e <= E) base[e] = run;
+      run += c4[i];
+    }
+    if (lane == 31 && 128 <= E) base[E] = run;
+  }
+  __syncthreads();
+
+  const int64_t wid = static_cast<int64_t>(blockIdx.x) * (kPermThreads / 32) + warp;
+  const int64_t t = wid / ncb;
+  const int cb = static_cast<int>(wid - t * ncb);
+  if (t >= T) return;
+  int p = -1;
+  if (lane < k) {
+    const int64_t f = t * k + lane;
+    const int e = topk_idx[f];
+    const int r = rank_s[f];
+    if (e >= 0 && e < E && r >= 0) {
+      p = base[e] + r;
+      if (cb == 0)
+        write_record(p, f, t, topk_w, topk_w_is_f32, dtype, sort_idx, sorted_token, sorted_w);
+    }
+    if (cb == 0) pos[f] = p;
+  }
+  if (!x_sorted) return;
+  copy_row_slice(static_cast<const uint4*>(x) + t * row_chunks, x_sorted, row_chunks, ncb, cb, k,
+                 p, lane);
 }
 
 __global__ void invert_perm_kernel(const int32_t* __restrict__ sort_idx, int64_t n,
@@ -300,6 +423,24 @@ cudaError_t launch_permute_gather(const int32_t* topk_idx, const int32_t* local_
                     dim3(kPermThreads), 0, stream, topk_idx, local_rank, block_offsets, counts,
                     topk_w, topk_w_is_f32, x, T, row_chunks, k, E, dispatch_block_tokens(k), dtype,
                     pos, sort_idx, sorted_token, sorted_w, static_cast<uint4*>(x_sorted), ncb);
+}
+
+bool dispatch_fits_one_block(int64_t T, int k) { return T > 0 && dispatch_num_blocks(T, k) == 1; }
+
+cudaError_t launch_dispatch_small(const int32_t* topk_idx, const void* topk_w, int topk_w_is_f32,
+                                  const void* x, int64_t T, int d, int k, int E, int dtype,
+                                  int32_t* counts, int32_t* pos, int32_t* sort_idx,
+                                  int32_t* sorted_token, void* sorted_w, void* x_sorted, int* err,
+                                  cudaStream_t stream) {
+  if (!dispatch_fits_one_block(T, k) || E > kMaxExperts) return cudaErrorInvalidValue;
+  const int es = dtype == kDtypeBF16 ? 2 : 4;
+  const int row_chunks = d * es / 16;
+  const int ncb = x_sorted ? cdiv(row_chunks, 32) : 1;
+  const int64_t blocks = cdiv64(T * ncb, kPermThreads / 32);
+  return launch_pdl(kPdlDispatch, dispatch_small_kernel, dim3(static_cast<unsigned>(blocks)),
+                    dim3(kPermThreads), 0, stream, topk_idx, topk_w, topk_w_is_f32, x, T,
+                    row_chunks, k, E, dtype, counts, pos, sort_idx, sorted_token, sorted_w,
+                    static_cast<uint4*>(x_sorted), ncb, err);
 }
 
 cudaError_t launch_invert_perm(const int32_t* sort_idx, int64_t n, int32_t* pos,

@@ -85,6 +85,15 @@ cudaError_t launch_scan(int32_t* block_counts, int64_t nblk, int E, int32_t* cou
 cudaError_t launch_hist_scan(const int32_t* topk_idx, int64_t T, int k, int E,
                              int32_t* local_rank, int32_t* block_counts, int32_t* counts, int* err,
                              cudaStream_t stream);
+// True when the T*k assignments fit one histogram block: then
+// launch_dispatch_small does all of dispatch in one kernel (counts, pos and
+// the optional outputs; no local_rank / block_counts scratch).
+bool dispatch_fits_one_block(int64_t T, int k);
+cudaError_t launch_dispatch_small(const int32_t* topk_idx, const void* topk_w, int topk_w_is_f32,
+                                  const void* x, int64_t T, int d, int k, int E, int dtype,
+                                  int32_t* counts, int32_t* pos, int32_t* sort_idx,
+                                  int32_t* sorted_token, void* sorted_w, void* x_sorted, int* err,
+                                  cudaStream_t stream);
 // pos[T*k] and (optionally) sort_idx, sorted_token, sorted weights, x_sorted.
 cudaError_t launch_permute_gather(const int32_t* topk_idx, const int32_t* local_rank,
                                   const int32_t* block_offsets, const int32_t* counts,
