@@ -166,12 +166,18 @@ FfnBufs carve_ffn(Carve& c, const hmoe_shape& s) {
 }
 
 // Router stage: tensor cores with exact-order fix-up for bf16, CUDA cores for fp32.
+// reset_err: the error word is cleared first (in the default pass's kernel).
 cudaError_t run_router(const hmoe_shape& s, const void* x, const void* w_router, const void* bias,
                        int32_t* idx, float* w_f32, void* w_dtype, void* logits, void* scratch,
-                       int* err, cudaStream_t st) {
+                       int* err, cudaStream_t st, bool reset_err = false) {
   if (s.dtype == kDtypeBF16)
     return launch_router_topk_tc(x, w_router, bias, s.tokens, s.hidden, s.experts, s.top_k,
-                                 s.norm_topk_prob, idx, w_f32, w_dtype, logits, scratch, err, st);
+                                 s.norm_topk_prob, idx, w_f32, w_dtype, logits, scratch, err, st,
+                                 nullptr, reset_err);
+  if (reset_err) {
+    const cudaError_t e = cudaMemsetAsync(err, 0, sizeof(int), st);
+    if (e != cudaSuccess) return e;
+  }
   return launch_router_topk(x, w_router, bias, s.tokens, s.hidden, s.experts, s.top_k, s.dtype,
                             s.norm_topk_prob, idx, w_f32, w_dtype, logits, st);
 }
@@ -418,10 +424,9 @@ int ffn_forward_impl(const hmoe_shape* shape, const void* x, const void* w_route
   Carve c{static_cast<char*>(workspace)};
   FfnBufs b = carve_ffn(c, s);
   int32_t* idx = topk_idx ? topk_idx : b.topk_idx;
-  HMOE_CUDA(cudaMemsetAsync(b.x.d.err, 0, sizeof(int), st), "reset error word");
   if ((rc = pm.mark(0, st))) return rc;
   HMOE_CUDA(run_router(s, x, w_router, router_bias, idx, b.topk_w, topk_weight, nullptr,
-                       b.router_scratch, b.x.d.err, st),
+                       b.router_scratch, b.x.d.err, st, true),
             "router_topk");
   if ((rc = pm.mark(1, st))) return rc;
   return run_experts(s, x, idx, b.topk_w, 1, w_gate_up, w_down, accumulate ? y : nullptr, y,

@@ -60,12 +60,13 @@ cudaError_t launch_router_topk(const void* x, const void* w_router, const void* 
 constexpr float kRouterCertRel = 1.0f / 65536.0f;
 size_t router_tc_scratch_bytes(int64_t T);
 // sums_out (optional, diagnostic): the fp32 tensor-core sums [T, E] before
-// the bias, as the certification sees them.
+// the bias, as the certification sees them.  reset_err: clear *err first
+// (the pair pass does it in the kernel, saving the memset in front of it).
 cudaError_t launch_router_topk_tc(const void* x, const void* w_router, const void* bias,
                                   int64_t T, int d, int E, int k, int norm, int32_t* topk_idx,
                                   float* topk_w_f32, void* topk_w_dtype, void* logits_out,
                                   void* scratch, int* err, cudaStream_t stream,
-                                  float* sums_out = nullptr);
+                                  float* sums_out = nullptr, bool reset_err = false);
 
 // dispatch.cu -----------------------------------------------------------
 // Tokens per histogram block for a given top_k.

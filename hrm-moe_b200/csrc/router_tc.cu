@@ -91,6 +91,7 @@ struct RtParams {
   unsigned* group_done;   // split fix-up: finished expert groups per token group
   uint16_t* fix_logits;   // split fix-up: rounded logits per fix slot
   int* err;
+  int reset_err;          // pair pass: CTA 0 clears *err once its dependency wait returns
   unsigned long long wait_limit_ns;
   float cert_rel;
 };
@@ -1579,6 +1580,10 @@ router_pair_kernel(const __grid_constant__ CUtensorMap tmX2, const __grid_consta
   tc_fence_after();
   grid_dependency_wait();  // launched early (launch_pdl): no global access before this
   grid_launch_dependents();
+  // The call's error word starts clear.  The pass records an error only
+  // after a wait of kWaitLimitNs, and every later kernel of the call waits
+  // for this grid, so nothing is overwritten.
+  if (p.reset_err && blockIdx.x == 0 && threadIdx.x == 0) *p.err = 0;
   const uint32_t tmem = ctl.tmem_base;
   volatile int* abort = &ctl.abort;
   int never = 0;
@@ -1982,11 +1987,17 @@ size_t router_tc_scratch_bytes(int64_t T) {
 cudaError_t launch_router_topk_tc(const void* x, const void* w_router, const void* bias,
                                   int64_t T, int d, int E, int k, int norm, int32_t* topk_idx,
                                   float* topk_w_f32, void* topk_w_dtype, void* logits_out,
-                                  void* scratch, int* err, cudaStream_t stream, float* sums_out) {
+                                  void* scratch, int* err, cudaStream_t stream, float* sums_out,
+                                  bool reset_err) {
+  // the pair pass fixes its uncertified tokens itself (no fix list) and can
+  // clear the error word itself; the other passes get both cleared here
+  const bool pair = T > 0 && pair_pass_fits(T, d, E);
+  if (reset_err && !pair) {
+    cudaError_t e = cudaMemsetAsync(err, 0, sizeof(int), stream);
+    if (e != cudaSuccess) return e;
+  }
   if (T == 0) return cudaSuccess;
   int* fix_count = static_cast<int*>(scratch);
-  // the pair pass fixes its uncertified tokens itself: no fix list
-  const bool pair = pair_pass_fits(T, d, E);
   if (!pair) {
     cudaError_t e = cudaMemsetAsync(fix_count, 0, sizeof(int), stream);
     if (e != cudaSuccess) return e;
@@ -2008,6 +2019,7 @@ cudaError_t launch_router_topk_tc(const void* x, const void* w_router, const voi
   p.fix_list = fix_count + 64 + fix_groups(T);
   p.fix_logits = reinterpret_cast<uint16_t*>(p.fix_list + align4(T));
   p.err = err;
+  p.reset_err = pair && reset_err ? 1 : 0;
   p.wait_limit_ns = kWaitLimitNs;
   p.cert_rel = router_cert_rel();
   if (pair)
