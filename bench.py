@@ -39,8 +39,6 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "MoE-FFN fwd tokens/s (XL 64x8 bf16)"
 L2_FLUSH_BYTES = 256 << 20
-
-
 L2_NOTE = ("256 MiB buffer rewritten, then another 256 MiB read, before every step "
            "(outside the timed events)")
 
@@ -57,6 +55,8 @@ class L2Flush:
     def __call__(self):
         self.w.zero_()
         self.r.max()
+
+
 # measured peer copy bandwidth per direction per GPU on this pool (NVLink 5)
 NVLINK_GBS = 770.0
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per forward of
@@ -874,6 +874,10 @@ def b200_arm(args, rank, world, local_rank):
             ach = work / sec / 1e12
             phases[n] = {"ms": phase_ms[n], "bound": "tensor", "achieved": ach,
                          "unit": "TFLOP/s", "frac": ach / peaks["bf16_tflops"]}
+            if peaks.get("bf16_tflops_sustained"):
+                # the timed steps run back to back under the power cap: the
+                # measured sustained cuBLAS figure, beside the burst one
+                phases[n]["frac_of_sustained"] = ach / peaks["bf16_tflops_sustained"]
         elif bound == "latency":
             phases[n] = {"ms": phase_ms[n], "bound": "latency", "achieved": None, "unit": None,
                          "frac": None}
@@ -900,6 +904,8 @@ def b200_arm(args, rank, world, local_rank):
                 "peak": peak_of[dp["bound"]],
                 "unit": dp["unit"], "frac": dp["frac"],
                 "peak_source": f"{peaks['source']} (burst)" if dp["bound"] == "tensor" else peaks["source"],
+                "peak_sustained": peaks.get("bf16_tflops_sustained") if dp["bound"] == "tensor" else None,
+                "frac_of_sustained": dp.get("frac_of_sustained"),
                 "traffic": (NCU_TRAFFIC_BYTES.get((args.config, T), {}).get(dom)
                             if world == 1 else None),
                 "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum per launch, "

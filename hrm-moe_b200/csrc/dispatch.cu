@@ -416,7 +416,8 @@ cudaError_t launch_permute_gather(const int32_t* topk_idx, const int32_t* local_
   const int row_chunks = d * es / 16;
   // small T: a row over several warps (512 bytes each); measured on B200
   // (XL layer): 12.6 -> 11.6 us at T=64, slower at T=1024 (more CTAs, each
-  // scanning the counts)
+  // scanning the counts) and at T=16384 (2, 3 or 6 warps per row: 1-6 %
+  // slower for the whole layer)
   const int ncb = T < 512 && x_sorted ? cdiv(row_chunks, 32) : 1;
   const int64_t blocks = cdiv64(T * ncb, kPermThreads / 32);
   return launch_pdl(kPdlDispatch, permute_gather_kernel, dim3(static_cast<unsigned>(blocks)),
