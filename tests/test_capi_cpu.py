@@ -99,3 +99,21 @@ def test_expert_parallel_arguments(lib):
     assert rc == errno.EINVAL and b"2^28" in so.hmoe_last_error()
     assert so.hmoe_ep_symmetric_alloc(0, None, None) == errno.EINVAL
     assert so.hmoe_ep_symmetric_open(None, None) == errno.EINVAL
+
+
+def test_pdl_mask_setter(lib):
+    """hmoe_set_pdl_mask returns the previous mask and keeps only the four
+    kernel-class bits; the default (HMOE_PDL unset) is every class but the
+    combine.  Host state only: no GPU needed."""
+    import os
+
+    so = lib.load()
+    start = so.hmoe_set_pdl_mask(7)
+    try:
+        if "HMOE_PDL" not in os.environ:
+            assert start == 7
+        assert so.hmoe_set_pdl_mask(0xFF) == 7
+        assert so.hmoe_set_pdl_mask(0) == 15
+        assert so.hmoe_set_pdl_mask(2) == 0
+    finally:
+        so.hmoe_set_pdl_mask(start)
